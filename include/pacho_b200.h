@@ -1,0 +1,184 @@
+/*
+ * pacho_b200.h -- C ABI of libpacho_b200.so, the B200 (sm_100a) backend for
+ * OpenPacho's linear-algebra hot path: batched GEMM with broadcast leading
+ * dimensions, GEMV, DOT and the overflow-safe scaled Euclidean/Frobenius norm.
+ *
+ * Conventions
+ *  - Every entry point returns an int status (PB_OK == 0).  On failure the
+ *    message is available from pb_last_error(), which is thread-local.
+ *  - Device pointers are plain `void*` obtained from pb_alloc(); sizes are
+ *    element or byte counts as documented; no C++ or framework types appear.
+ *  - All work of one device is ordered on one non-blocking CUDA stream owned
+ *    by the context.  Calls return after *submission*; pb_sync() and
+ *    pb_d2h() synchronise.  A host mutex per context serialises submission,
+ *    mirroring the reference CUDA backend's RLock (src/openpacho/_cuda.py:148,
+ *    201-220).
+ *  - Matrices are C-contiguous (row-major).  Batched operands are a sequence
+ *    of contiguous matrices; broadcast is expressed by per-dimension batch
+ *    strides counted in whole matrices, 0 for a broadcast dimension.
+ *  - There is no CPU fallback anywhere: an unsupported request is an error.
+ */
+#ifndef PACHO_B200_H
+#define PACHO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Only the entry points below are exported from the shared library. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define PB_ABI_VERSION 1
+
+/* Status codes. */
+enum {
+  PB_OK = 0,
+  PB_ERR_INVALID = 1,     /* bad argument (shape, pointer, dtype value)          */
+  PB_ERR_CUDA = 2,        /* a CUDA runtime/driver call failed                    */
+  PB_ERR_UNSUPPORTED = 3, /* valid request this library does not implement       */
+  PB_ERR_OOM = 4,         /* device allocation failed                            */
+  PB_ERR_NCCL = 5,        /* NCCL missing or a collective failed                  */
+  PB_ERR_DEVICE = 6,      /* a kernel reported an error (e.g. a bounded wait ran out) */
+  PB_ERR_UNAVAILABLE = 7  /* no usable device / driver                           */
+};
+
+/* Element types (the reference supports float32 and float64 on this path:
+ * src/openpacho/_cuda.py:226-230). */
+enum { PB_F32 = 0, PB_F64 = 1 };
+
+typedef struct pb_ctx pb_ctx;
+
+/* ---- errors / discovery ------------------------------------------------ */
+
+/* Thread-local message of the last failing call on this thread. */
+const char* pb_last_error(void);
+/* PB_ABI_VERSION of the loaded library. */
+int pb_abi_version(void);
+/* Replaces cuda_devices() (src/openpacho/_cuda.py, used by backends.devices
+ * at src/openpacho/backends.py:55-60). */
+int pb_device_count(int* count);
+int pb_device_info(int ordinal, char* name, size_t name_len, size_t* total_bytes,
+                   int* sm_count, int* cc_major, int* cc_minor);
+
+/* ---- context / memory (CUDABackend.__init__/empty/upload/download/close,
+ *      src/openpacho/_cuda.py:138-199, 232-311, 644-673) ------------------ */
+
+/* Create a context over `ndev` CUDA ordinals; one stream and one stream-ordered
+ * memory pool per device. */
+int pb_init(int ndev, const int* ordinals, pb_ctx** out);
+/* Synchronise and release every resource of the context. */
+int pb_destroy(pb_ctx* ctx);
+/* Stream-ordered device allocation (never returns NULL for bytes > 0). */
+int pb_alloc(pb_ctx* ctx, int dev, size_t bytes, void** ptr);
+int pb_free(pb_ctx* ctx, int dev, void* ptr);
+/* Host -> device copy on the context stream.  blocking != 0 waits for the copy
+ * (snapshot semantics of CUDABackend.upload, _cuda.py:293-303). */
+int pb_h2d(pb_ctx* ctx, int dev, void* dst, const void* src, size_t bytes, int blocking);
+/* Device -> host copy; synchronises the stream first (download, _cuda.py:305-311). */
+int pb_d2h(pb_ctx* ctx, int dev, void* dst, const void* src, size_t bytes);
+/* Asynchronous device -> host copy into pinned memory (no synchronisation). */
+int pb_d2h_async(pb_ctx* ctx, int dev, void* dst, const void* src, size_t bytes);
+int pb_d2d(pb_ctx* ctx, int dev, void* dst, const void* src, size_t bytes);
+/* Fill `count` elements with `value` (CUDABackend.full, _cuda.py:399-409). */
+int pb_fill(pb_ctx* ctx, int dev, int dtype, void* dst, size_t count, double value);
+/* Wait for all submitted work; reports kernel-side error flags. */
+int pb_sync(pb_ctx* ctx, int dev);
+/* Page-lock host memory for asynchronous copies. */
+int pb_host_register(void* ptr, size_t bytes);
+int pb_host_unregister(void* ptr);
+/* Return pooled device memory and scratch to the driver
+ * (release_cached_memory, _cuda.py:262-274). */
+int pb_trim(pb_ctx* ctx, int dev);
+/* CUDA-event timer on the device stream (for benchmarks). */
+int pb_timer_start(pb_ctx* ctx, int dev);
+int pb_timer_stop(pb_ctx* ctx, int dev, float* ms);
+/* Number of kernels this library launched on `dev` since pb_init. */
+int pb_launch_count(pb_ctx* ctx, int dev, uint64_t* count);
+
+/* ---- hot path ---------------------------------------------------------- */
+
+/* C[b] = A[a_off(b)] @ B[b_off(b)] for every index b of the broadcast batch
+ * shape `batch_shape[0..batch_ndim)`; a_off/b_off = sum(idx_i * stride_i)
+ * with strides in whole matrices (0 = broadcast).  A matrices are M x K,
+ * B matrices K x N, C (batch x M x N) is written densely.  K == 0 writes
+ * zeros.  float32 uses error-compensated 3xTF32 on tcgen05 tensor cores
+ * (never plain TF32), float64 an FP64 tile kernel.
+ * Replaces NumpyBackend.matmul (src/openpacho/backends.py:139-142) and
+ * CUDABackend.matmul (src/openpacho/_cuda.py:493-637) with the register GEMM
+ * (src/openpacho/_gemm.py:102-137) and broadcast offsets (_gemm.py:13-21). */
+int pb_gemm(pb_ctx* ctx, int dev, int dtype, int batch_ndim, const int64_t* batch_shape,
+            const int64_t* a_bstride, const int64_t* b_bstride, int64_t M, int64_t N,
+            int64_t K, const void* A, const void* B, void* C);
+
+/* pb_gemm with an explicit kernel choice: PB_GEMM_AUTO (what pb_gemm does),
+ * PB_GEMM_SIMT (register-tiled CUDA-core kernel; the only float64 kernel) or
+ * PB_GEMM_TF32X3 (float32 only).  The reference exposes the same kind of
+ * provider choice as CUDABackend(blas="custom"|"cublas")
+ * (src/openpacho/_cuda.py:138-141). */
+enum { PB_GEMM_AUTO = 0, PB_GEMM_SIMT = 1, PB_GEMM_TF32X3 = 2 };
+int pb_gemm_ex(pb_ctx* ctx, int dev, int dtype, int batch_ndim, const int64_t* batch_shape,
+               const int64_t* a_bstride, const int64_t* b_bstride, int64_t M, int64_t N,
+               int64_t K, const void* A, const void* B, void* C, int algo);
+
+/* y[r] = sum_k A[r,k] * x[k] for r < rows (leading dims flattened into rows).
+ * Replaces matvec_data (src/openpacho/_cuda_gemv.py:47-95) and the cuBLAS
+ * ?gemv loop (src/openpacho/_cuda_blas.py:32-61). */
+int pb_gemv(pb_ctx* ctx, int dev, int dtype, int64_t rows, int64_t K, const void* A,
+            const void* x, void* y);
+
+/* *out = sum_i x[i] * y[i] written to device memory.  Replaces the long-DOT
+ * chunked path (src/openpacho/_cuda_gemv.py:67-84) and cuBLAS ?dot in
+ * device-pointer mode (src/openpacho/_cuda_blas.py:18-30). */
+int pb_dot(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, const void* y,
+           void* out);
+
+/* out[o*inner + i] = || x[o, :, i] ||_2 over the middle axis of the
+ * contiguous view (outer, reduced, inner).  Overflow/underflow-safe; NaN
+ * dominates Inf; -0.0 yields +0.0; reduced == 0 yields 0.
+ * Replaces norm_data (src/openpacho/_norm.py:39-118) for any contiguous run
+ * of reduced axes. */
+int pb_norm(pb_ctx* ctx, int dev, int dtype, int64_t outer, int64_t reduced, int64_t inner,
+            const void* x, void* out);
+
+/* General axis sets: output element o (row-major over out_shape) reduces the
+ * elements at sum(out_idx*out_strides) + sum(red_idx*red_strides) (element
+ * strides) for every index of red_shape.  ndims <= 8 each.  Same semantics
+ * as pb_norm; replaces the _index() addressing of src/openpacho/_norm.py:12-25. */
+int pb_norm_strided(pb_ctx* ctx, int dev, int dtype, int out_ndim, const int64_t* out_shape,
+                    const int64_t* out_strides, int red_ndim, const int64_t* red_shape,
+                    const int64_t* red_strides, const void* x, void* out);
+
+/* ---- multi-GPU (one process per GPU; NCCL loaded on first use) --------- */
+
+/* Opaque NCCL unique id (128 bytes) made by rank 0 and shared out of band. */
+int pb_comm_unique_id(unsigned char id[128]);
+/* Join the communicator of `nranks` processes as `rank` for device `dev`. */
+int pb_comm_init(pb_ctx* ctx, int dev, int nranks, int rank, const unsigned char id[128]);
+int pb_comm_destroy(pb_ctx* ctx, int dev);
+/* In-place broadcast of `bytes` from `root` (used to give every GPU the
+ * shared B operand of a row-block sharded GEMM). */
+int pb_broadcast(pb_ctx* ctx, int dev, void* buf, size_t bytes, int root);
+/* Full-array norm of a tensor sliced contiguously across ranks: each rank
+ * passes its own slice (n local elements, possibly 0); every rank receives
+ * the global norm in `out` (device, 1 element).  Local (scale, ssq) partials
+ * are merged with NCCL all-reduces (max of the scale exponent and the
+ * NaN/Inf class, then a sum of rescaled ssq).  No counterpart in the
+ * reference, which is single-device (src/openpacho/_cuda.py:138-199). */
+int pb_norm_sharded(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, void* out);
+/* Sum all-reduce of `count` elements in place (used for sharded DOT). */
+int pb_allreduce_sum(pb_ctx* ctx, int dev, int dtype, void* buf, size_t count);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PACHO_B200_H */

@@ -1,0 +1,291 @@
+// GEMV, DOT and fill kernels of libpacho_b200 (HBM-bound).
+//
+// Reference behaviour: matvec_data (src/openpacho/_cuda_gemv.py:47-95) flattens
+// every leading dimension of A into independent rows and computes y = A @ x;
+// DOT is the one-row case.  The reference launches one 128-thread block per row
+// (or per 1024-term DOT chunk) with scalar strided loads and a shared-memory
+// tree, then a second reduction launch (_cuda_gemv.py:67-84).
+//
+// This design: 256-thread blocks, 128-bit non-caching loads of the streamed
+// operand (A, or both DOT vectors), the reused vector x through the read-only
+// L1 path, a warp-shuffle tree, and -- when a row is split across blocks to
+// fill 148 SMs -- per-block partials in scratch merged by the last block to
+// arrive (one launch, fixed merge order, hence deterministic results).
+#include "pb_internal.cuh"
+
+namespace pb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kUnroll = 4;
+
+template <typename T> struct V16;
+template <> struct V16<float> { using type = float4; static constexpr int n = 4; };
+template <> struct V16<double> { using type = double2; static constexpr int n = 2; };
+
+// Streaming 16-byte load that does not allocate in L1 (the matrix is read once).
+__device__ __forceinline__ float4 ld_stream(const float4* p) {
+  float4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ double2 ld_stream(const double2* p) {
+  double2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.f64 {%0,%1}, [%2];"
+               : "=d"(v.x), "=d"(v.y)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float dotv(float4 a, float4 b, float acc) {
+  acc = fmaf(a.x, b.x, acc);
+  acc = fmaf(a.y, b.y, acc);
+  acc = fmaf(a.z, b.z, acc);
+  return fmaf(a.w, b.w, acc);
+}
+__device__ __forceinline__ double dotv(double2 a, double2 b, double acc) {
+  acc = fma(a.x, b.x, acc);
+  return fma(a.y, b.y, acc);
+}
+
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Sum of A[row, k0:k1] * x[k0:k1] by the `nthr` threads of one row group.
+// STREAM_X: x is itself streamed once (DOT) instead of reused (GEMV).
+template <typename T, bool ALIGNED, bool STREAM_X>
+__device__ __forceinline__ T row_partial(const T* __restrict__ a, const T* __restrict__ x,
+                                         int64_t k0, int64_t k1, int tid, int nthr) {
+  using V = typename V16<T>::type;
+  constexpr int VN = V16<T>::n;
+  T acc[kUnroll];
+#pragma unroll
+  for (int u = 0; u < kUnroll; ++u) acc[u] = T(0);
+  int64_t body_end = k0;
+  if (ALIGNED) {
+    // k0 is a multiple of VN and the row start is 16-byte aligned.
+    const int64_t nv = (k1 - k0) / VN;
+    const V* av = reinterpret_cast<const V*>(a + k0);
+    const V* xv = reinterpret_cast<const V*>(x + k0);
+    int64_t v = tid;
+    for (; v + (kUnroll - 1) * (int64_t)nthr < nv; v += kUnroll * (int64_t)nthr) {
+      V ra[kUnroll], rx[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        ra[u] = ld_stream(av + v + u * nthr);
+        rx[u] = STREAM_X ? ld_stream(xv + v + u * nthr) : __ldg(xv + v + u * nthr);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) acc[u] = dotv(ra[u], rx[u], acc[u]);
+    }
+    for (; v < nv; v += nthr) {
+      V ra = ld_stream(av + v);
+      V rx = STREAM_X ? ld_stream(xv + v) : __ldg(xv + v);
+      acc[0] = dotv(ra, rx, acc[0]);
+    }
+    body_end = k0 + nv * VN;
+  }
+  for (int64_t k = body_end + tid; k < k1; k += nthr) acc[1] = fma(__ldg(a + k), __ldg(x + k), acc[1]);
+  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+}
+
+// Block = kWarps warps; G = kWarps / rows_per_block warps per row.  Block b
+// covers row group b / nchunks and K-chunk b % nchunks.
+template <typename T, bool ALIGNED, bool STREAM_X>
+__global__ void __launch_bounds__(kThreads)
+    gemv_kernel(const T* __restrict__ A, const T* __restrict__ x, T* __restrict__ y,
+                int64_t rows, int64_t K, int64_t lda, int rows_per_block, int64_t chunk,
+                int nchunks, T* __restrict__ partial, unsigned int* __restrict__ counters) {
+  __shared__ T red[kWarps];
+  __shared__ bool last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = kWarps / rows_per_block;
+  const int64_t group = blockIdx.x / nchunks;
+  const int c = blockIdx.x % nchunks;
+  const int sub = warp / G;
+  const int64_t row = group * rows_per_block + sub;
+  const int tid = (warp % G) * 32 + lane;
+  T v = T(0);
+  if (row < rows) {
+    const int64_t k0 = (int64_t)c * chunk;
+    const int64_t k1 = min(K, k0 + chunk);
+    v = row_partial<T, ALIGNED, STREAM_X>(A + row * lda, x, k0, k1, tid, G * 32);
+  }
+  v = warp_sum(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (nchunks == 1) {
+    if (threadIdx.x < rows_per_block) {
+      const int64_t r = group * rows_per_block + threadIdx.x;
+      if (r < rows) {
+        T s = T(0);
+        for (int w = 0; w < G; ++w) s += red[threadIdx.x * G + w];
+        y[r] = s;
+      }
+    }
+    return;
+  }
+  // Split row (rows_per_block == 1): publish this chunk's partial, and let the
+  // last block to arrive merge all of them in chunk order.
+  if (threadIdx.x == 0) {
+    T s = T(0);
+    for (int w = 0; w < kWarps; ++w) s += red[w];
+    partial[row * nchunks + c] = s;
+    __threadfence();
+    unsigned int prev = atomicAdd(&counters[row], 1u);
+    last = (prev == (unsigned int)(nchunks - 1));
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  T s = T(0);
+  for (int i = threadIdx.x; i < nchunks; i += kThreads) s += __ldcg(partial + row * nchunks + i);
+  s = warp_sum(s);
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    T t = T(0);
+    for (int w = 0; w < kWarps; ++w) t += red[w];
+    y[row] = t;
+    counters[row] = 0u;  // leave the counter ready for the next launch
+  }
+}
+
+template <typename T>
+__global__ void fill_kernel(T* __restrict__ out, size_t n, T value) {
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) out[i] = value;
+}
+
+struct GemvPlan {
+  int rows_per_block;
+  int nchunks;
+  int64_t chunk;
+  int64_t blocks;
+};
+
+GemvPlan plan_gemv(int64_t rows, int64_t K, int sm_count) {
+  GemvPlan p;
+  const int64_t resident = (int64_t)sm_count * (2048 / kThreads);
+  if (rows >= 2 * resident || K <= 4096) {
+    p.nchunks = 1;
+    p.chunk = K;
+    int G = K >= 4096 ? 8 : K >= 1024 ? 4 : K >= 256 ? 2 : 1;
+    p.rows_per_block = kWarps / G;
+  } else {
+    p.rows_per_block = 1;
+    int64_t want = ceil_div(2 * resident, rows);
+    int64_t most = ceil_div(K, 2048);
+    int64_t n = want < most ? want : most;
+    if (n < 1) n = 1;
+    p.chunk = ceil_div(ceil_div(K, n), 64) * 64;
+    p.nchunks = (int)ceil_div(K, p.chunk);
+  }
+  p.blocks = ceil_div(rows, p.rows_per_block) * p.nchunks;
+  return p;
+}
+
+template <typename T, bool STREAM_X>
+int launch_gemv(Device* d, const T* A, const T* x, T* y, int64_t rows, int64_t K, int64_t lda) {
+  GemvPlan p = plan_gemv(rows, K, d->sm_count);
+  if (p.blocks > INT32_MAX) PB_FAIL(PB_ERR_UNSUPPORTED, "GEMV grid too large");
+  T* partial = nullptr;
+  unsigned int* cnt = nullptr;
+  if (p.nchunks > 1) {
+    void* s;
+    PB_CHECK(scratch(d, (size_t)rows * p.nchunks * sizeof(T), &s));
+    partial = (T*)s;
+    PB_CHECK(counters(d, (size_t)rows, &cnt));
+  }
+  constexpr int VN = V16<T>::n;
+  bool aligned = ((uintptr_t)A % 16 == 0) && ((uintptr_t)x % 16 == 0) &&
+                 (rows == 1 || lda % VN == 0) && (p.chunk % VN == 0);
+  if (aligned)
+    gemv_kernel<T, true, STREAM_X><<<(unsigned)p.blocks, kThreads, 0, d->stream>>>(
+        A, x, y, rows, K, lda, p.rows_per_block, p.chunk, p.nchunks, partial, cnt);
+  else
+    gemv_kernel<T, false, STREAM_X><<<(unsigned)p.blocks, kThreads, 0, d->stream>>>(
+        A, x, y, rows, K, lda, p.rows_per_block, p.chunk, p.nchunks, partial, cnt);
+  PB_LAUNCHED(d);
+  return PB_OK;
+}
+
+template <typename T>
+int launch_fill(Device* d, T* out, size_t n, T value) {
+  if (!n) return PB_OK;
+  size_t blocks = (n + 255) / 256;
+  size_t cap = (size_t)d->sm_count * 32;
+  if (blocks > cap) blocks = cap;
+  fill_kernel<T><<<(unsigned)blocks, 256, 0, d->stream>>>(out, n, value);
+  PB_LAUNCHED(d);
+  return PB_OK;
+}
+
+}  // namespace
+
+int fill_device(Device* d, int dtype, void* dst, size_t count, double value) {
+  if (dtype == PB_F32) return launch_fill<float>(d, (float*)dst, count, (float)value);
+  if (dtype == PB_F64) return launch_fill<double>(d, (double*)dst, count, value);
+  PB_FAIL(PB_ERR_INVALID, "unknown dtype %d", dtype);
+}
+
+}  // namespace pb
+
+using namespace pb;
+
+extern "C" {
+
+int pb_fill(pb_ctx* ctx, int dev, int dtype, void* dst, size_t count, double value) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  if (!count) return PB_OK;
+  if (!dst) PB_FAIL(PB_ERR_INVALID, "null destination");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  return fill_device(d, dtype, dst, count, value);
+}
+
+int pb_gemv(pb_ctx* ctx, int dev, int dtype, int64_t rows, int64_t K, const void* A,
+            const void* x, void* y) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  if (rows < 0 || K < 0) PB_FAIL(PB_ERR_INVALID, "negative GEMV extent");
+  if (!rows) return PB_OK;
+  if (!y) PB_FAIL(PB_ERR_INVALID, "null output");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  if (!K) return fill_device(d, dtype, y, (size_t)rows, 0.0);
+  if (!A || !x) PB_FAIL(PB_ERR_INVALID, "null input");
+  if (dtype == PB_F32)
+    return launch_gemv<float, false>(d, (const float*)A, (const float*)x, (float*)y, rows, K, K);
+  if (dtype == PB_F64)
+    return launch_gemv<double, false>(d, (const double*)A, (const double*)x, (double*)y, rows, K,
+                                      K);
+  PB_FAIL(PB_ERR_INVALID, "unknown dtype %d", dtype);
+}
+
+int pb_dot(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, const void* y, void* out) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  if (n < 0) PB_FAIL(PB_ERR_INVALID, "negative DOT length");
+  if (!out) PB_FAIL(PB_ERR_INVALID, "null output");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  if (!n) return fill_device(d, dtype, out, 1, 0.0);
+  if (!x || !y) PB_FAIL(PB_ERR_INVALID, "null input");
+  if (dtype == PB_F32)
+    return launch_gemv<float, true>(d, (const float*)x, (const float*)y, (float*)out, 1, n, n);
+  if (dtype == PB_F64)
+    return launch_gemv<double, true>(d, (const double*)x, (const double*)y, (double*)out, 1, n,
+                                     n);
+  PB_FAIL(PB_ERR_INVALID, "unknown dtype %d", dtype);
+}
+
+}  // extern "C"

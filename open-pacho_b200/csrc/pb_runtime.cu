@@ -1,0 +1,364 @@
+// Context, memory, copies, errors and timers of libpacho_b200.
+//
+// Behavioural model: CUDABackend in src/openpacho/_cuda.py -- one
+// non-blocking stream per device (:157-160), synchronous snapshot uploads
+// (:293-303), downloads that synchronise first (:305-311), a reusable memory
+// pool (:232-274) and explicit close (:644-673).  The pool here is CUDA's
+// stream-ordered allocator instead of a Python LRU of cuMemAlloc blocks.
+#include <cudaTypedefs.h>
+#include <stdarg.h>
+#include <string.h>
+
+#include <vector>
+
+#include "pb_internal.cuh"
+
+namespace pb {
+
+static thread_local char g_error[1024] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, ap);
+  va_end(ap);
+}
+
+int enter(pb_ctx* ctx, int dev, Device** out) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  if (dev < 0 || dev >= ctx->ndev) PB_FAIL(PB_ERR_INVALID, "device index %d out of range", dev);
+  Device* d = &ctx->devs[dev];
+  PB_CUDA(cudaSetDevice(d->ordinal));
+  *out = d;
+  return PB_OK;
+}
+
+int scratch(Device* d, size_t bytes, void** out) {
+  if (bytes > d->scratch_bytes) {
+    if (d->scratch) PB_CUDA(cudaFreeAsync(d->scratch, d->stream));
+    d->scratch = nullptr;
+    d->scratch_bytes = 0;
+    size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+    PB_CUDA(cudaMallocAsync(&d->scratch, want, d->pool, d->stream));
+    d->scratch_bytes = want;
+  }
+  *out = d->scratch;
+  return PB_OK;
+}
+
+int counters(Device* d, size_t n, unsigned int** out) {
+  if (n > d->counters_n) {
+    if (d->counters) PB_CUDA(cudaFreeAsync(d->counters, d->stream));
+    d->counters = nullptr;
+    d->counters_n = 0;
+    size_t want = n < 4096 ? 4096 : n;
+    PB_CUDA(cudaMallocAsync((void**)&d->counters, want * sizeof(unsigned int), d->pool,
+                            d->stream));
+    PB_CUDA(cudaMemsetAsync(d->counters, 0, want * sizeof(unsigned int), d->stream));
+    d->counters_n = want;
+  }
+  *out = d->counters;
+  return PB_OK;
+}
+
+int tensor_map_encoder(void** fn) {
+  static std::once_flag once;
+  static void* encoder = nullptr;
+  static cudaError_t status = cudaSuccess;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    status = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &encoder, cudaEnableDefault, &q);
+    if (status == cudaSuccess && q != cudaDriverEntryPointSuccess) status = cudaErrorNotSupported;
+  });
+  if (status != cudaSuccess || !encoder)
+    PB_FAIL(PB_ERR_UNAVAILABLE, "cuTensorMapEncodeTiled unavailable: %s",
+            cudaGetErrorString(status));
+  *fn = encoder;
+  return PB_OK;
+}
+
+static void release_device(Device* d) {
+  if (d->ordinal < 0) return;
+  cudaSetDevice(d->ordinal);
+  if (d->stream) cudaStreamSynchronize(d->stream);
+  if (d->scratch) cudaFreeAsync(d->scratch, d->stream);
+  if (d->counters) cudaFreeAsync(d->counters, d->stream);
+  if (d->stream) cudaStreamSynchronize(d->stream);
+  if (d->t0) cudaEventDestroy(d->t0);
+  if (d->t1) cudaEventDestroy(d->t1);
+  if (d->err_host) cudaFreeHost(d->err_host);
+  if (d->stream) cudaStreamDestroy(d->stream);
+  if (d->pool) cudaMemPoolTrimTo(d->pool, 0);
+  d->scratch = nullptr;
+  d->counters = nullptr;
+  d->err_host = d->err_dev = nullptr;
+  d->stream = nullptr;
+}
+
+// Kernel error word check (after a synchronisation).
+static int check_kernel_error(Device* d) {
+  if (d->err_host && *(volatile int*)d->err_host != KERR_NONE) {
+    int code = *(volatile int*)d->err_host;
+    *(volatile int*)d->err_host = KERR_NONE;
+    PB_FAIL(PB_ERR_DEVICE, "kernel reported error %d (%s)", code,
+            code == KERR_WAIT_TIMEOUT ? "bounded wait timed out" : "bad argument");
+  }
+  return PB_OK;
+}
+
+}  // namespace pb
+
+using namespace pb;
+
+extern "C" {
+
+const char* pb_last_error(void) { return g_error; }
+
+int pb_abi_version(void) { return PB_ABI_VERSION; }
+
+int pb_device_count(int* count) {
+  if (!count) PB_FAIL(PB_ERR_INVALID, "null count");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    *count = 0;
+    PB_FAIL(PB_ERR_UNAVAILABLE, "no CUDA device: %s", cudaGetErrorString(e));
+  }
+  *count = n;
+  return PB_OK;
+}
+
+int pb_device_info(int ordinal, char* name, size_t name_len, size_t* total_bytes, int* sm_count,
+                   int* cc_major, int* cc_minor) {
+  cudaDeviceProp p;
+  cudaError_t e = cudaGetDeviceProperties(&p, ordinal);
+  if (e != cudaSuccess) PB_FAIL(PB_ERR_UNAVAILABLE, "device %d: %s", ordinal, cudaGetErrorString(e));
+  if (name && name_len) {
+    strncpy(name, p.name, name_len - 1);
+    name[name_len - 1] = 0;
+  }
+  if (total_bytes) *total_bytes = p.totalGlobalMem;
+  if (sm_count) *sm_count = p.multiProcessorCount;
+  if (cc_major) *cc_major = p.major;
+  if (cc_minor) *cc_minor = p.minor;
+  return PB_OK;
+}
+
+int pb_init(int ndev, const int* ordinals, pb_ctx** out) {
+  if (!out || ndev <= 0 || !ordinals) PB_FAIL(PB_ERR_INVALID, "pb_init needs >=1 device");
+  *out = nullptr;
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0)
+    PB_FAIL(PB_ERR_UNAVAILABLE, "no CUDA device: %s", cudaGetErrorString(e));
+  pb_ctx* ctx = new pb_ctx();
+  ctx->ndev = ndev;
+  ctx->devs = new Device[ndev];
+  int status = PB_OK;
+  for (int i = 0; i < ndev && status == PB_OK; ++i) {
+    Device* d = &ctx->devs[i];
+    int ord = ordinals[i];
+    if (ord < 0 || ord >= count) {
+      set_error("CUDA device %d not found (%d visible)", ord, count);
+      status = PB_ERR_UNAVAILABLE;
+      break;
+    }
+    cudaDeviceProp p;
+    if ((e = cudaGetDeviceProperties(&p, ord)) != cudaSuccess) {
+      set_error("cudaGetDeviceProperties: %s", cudaGetErrorString(e));
+      status = PB_ERR_UNAVAILABLE;
+      break;
+    }
+    if (p.major != 10) {
+      set_error("device %d (%s, sm_%d%d) is not a B200-class sm_100 GPU", ord, p.name, p.major,
+                p.minor);
+      status = PB_ERR_UNAVAILABLE;
+      break;
+    }
+    d->ordinal = ord;
+    d->sm_count = p.multiProcessorCount;
+    auto fail = [&](const char* what, cudaError_t err) {
+      set_error("%s: %s", what, cudaGetErrorString(err));
+      status = err == cudaErrorMemoryAllocation ? PB_ERR_OOM : PB_ERR_CUDA;
+    };
+    if ((e = cudaSetDevice(ord)) != cudaSuccess) { fail("cudaSetDevice", e); break; }
+    if ((e = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking)) != cudaSuccess) {
+      fail("cudaStreamCreate", e);
+      break;
+    }
+    if ((e = cudaDeviceGetDefaultMemPool(&d->pool, ord)) != cudaSuccess) {
+      fail("cudaDeviceGetDefaultMemPool", e);
+      break;
+    }
+    // Keep freed blocks cached in the pool (no release at each sync point).
+    uint64_t keep = UINT64_MAX;
+    cudaMemPoolSetAttribute(d->pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    if ((e = cudaHostAlloc((void**)&d->err_host, sizeof(int), cudaHostAllocMapped)) !=
+        cudaSuccess) {
+      fail("cudaHostAlloc(error word)", e);
+      break;
+    }
+    *d->err_host = KERR_NONE;
+    if ((e = cudaHostGetDevicePointer((void**)&d->err_dev, d->err_host, 0)) != cudaSuccess) {
+      fail("cudaHostGetDevicePointer", e);
+      break;
+    }
+    if ((e = cudaEventCreate(&d->t0)) != cudaSuccess || (e = cudaEventCreate(&d->t1)) != cudaSuccess) {
+      fail("cudaEventCreate", e);
+      break;
+    }
+  }
+  if (status != PB_OK) {
+    for (int i = 0; i < ndev; ++i) release_device(&ctx->devs[i]);
+    delete[] ctx->devs;
+    delete ctx;
+    return status;
+  }
+  *out = ctx;
+  return PB_OK;
+}
+
+int pb_comm_destroy(pb_ctx* ctx, int dev);
+
+int pb_destroy(pb_ctx* ctx) {
+  if (!ctx) return PB_OK;
+  {
+    std::lock_guard<std::recursive_mutex> g(ctx->mu);
+    for (int i = 0; i < ctx->ndev; ++i) {
+      if (ctx->devs[i].comm) pb_comm_destroy(ctx, i);
+      release_device(&ctx->devs[i]);
+    }
+  }
+  delete[] ctx->devs;
+  delete ctx;
+  return PB_OK;
+}
+
+int pb_alloc(pb_ctx* ctx, int dev, size_t bytes, void** ptr) {
+  if (!ptr || !ctx) PB_FAIL(PB_ERR_INVALID, "null argument");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  if (bytes == 0) bytes = 16;
+  PB_CUDA(cudaMallocAsync(ptr, bytes, d->pool, d->stream));
+  return PB_OK;
+}
+
+int pb_free(pb_ctx* ctx, int dev, void* ptr) {
+  if (!ptr) return PB_OK;
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  PB_CUDA(cudaFreeAsync(ptr, d->stream));
+  return PB_OK;
+}
+
+int pb_h2d(pb_ctx* ctx, int dev, void* dst, const void* src, size_t bytes, int blocking) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  if (!bytes) return PB_OK;
+  if (!dst || !src) PB_FAIL(PB_ERR_INVALID, "null pointer in pb_h2d");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  PB_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, d->stream));
+  if (blocking) PB_CUDA(cudaStreamSynchronize(d->stream));
+  return PB_OK;
+}
+
+int pb_d2h(pb_ctx* ctx, int dev, void* dst, const void* src, size_t bytes) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  if (bytes) {
+    if (!dst || !src) PB_FAIL(PB_ERR_INVALID, "null pointer in pb_d2h");
+    PB_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, d->stream));
+  }
+  PB_CUDA(cudaStreamSynchronize(d->stream));
+  return check_kernel_error(d);
+}
+
+int pb_d2h_async(pb_ctx* ctx, int dev, void* dst, const void* src, size_t bytes) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  if (!bytes) return PB_OK;
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  PB_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, d->stream));
+  return PB_OK;
+}
+
+int pb_d2d(pb_ctx* ctx, int dev, void* dst, const void* src, size_t bytes) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  if (!bytes) return PB_OK;
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  PB_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, d->stream));
+  return PB_OK;
+}
+
+int pb_sync(pb_ctx* ctx, int dev) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  if (d->comm) PB_CHECK(comm_stream_wait(d));
+  else PB_CUDA(cudaStreamSynchronize(d->stream));
+  return check_kernel_error(d);
+}
+
+int pb_host_register(void* ptr, size_t bytes) {
+  if (!ptr || !bytes) PB_FAIL(PB_ERR_INVALID, "empty host range");
+  PB_CUDA(cudaHostRegister(ptr, bytes, cudaHostRegisterDefault));
+  return PB_OK;
+}
+
+int pb_host_unregister(void* ptr) {
+  if (!ptr) return PB_OK;
+  PB_CUDA(cudaHostUnregister(ptr));
+  return PB_OK;
+}
+
+int pb_trim(pb_ctx* ctx, int dev) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  if (d->scratch) PB_CUDA(cudaFreeAsync(d->scratch, d->stream));
+  d->scratch = nullptr;
+  d->scratch_bytes = 0;
+  PB_CUDA(cudaStreamSynchronize(d->stream));
+  PB_CUDA(cudaMemPoolTrimTo(d->pool, 0));
+  return PB_OK;
+}
+
+int pb_timer_start(pb_ctx* ctx, int dev) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  PB_CUDA(cudaEventRecord(d->t0, d->stream));
+  return PB_OK;
+}
+
+int pb_timer_stop(pb_ctx* ctx, int dev, float* ms) {
+  if (!ctx || !ms) PB_FAIL(PB_ERR_INVALID, "null argument");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  PB_CUDA(cudaEventRecord(d->t1, d->stream));
+  PB_CUDA(cudaEventSynchronize(d->t1));
+  PB_CUDA(cudaEventElapsedTime(ms, d->t0, d->t1));
+  return check_kernel_error(d);
+}
+
+int pb_launch_count(pb_ctx* ctx, int dev, uint64_t* count) {
+  if (!ctx || !count) PB_FAIL(PB_ERR_INVALID, "null argument");
+  if (dev < 0 || dev >= ctx->ndev) PB_FAIL(PB_ERR_INVALID, "device index %d out of range", dev);
+  *count = ctx->devs[dev].launches.load();
+  return PB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,62 @@
+"""pacho_b200: B200 (sm_100a) backend for OpenPacho's linear-algebra hot path.
+
+* :class:`B200Backend` -- OpenPacho's backend protocol (``matmul``, ``norm``,
+  ``upload``/``download``/``empty``/``full``, ``synchronize``) over the C-ABI
+  library ``libpacho_b200.so`` (hand-written CUDA for sm_100a).
+* :func:`register` -- adds ``"b200"`` to an installed OpenPacho's dispatch.
+* ``asarray``/``asnumpy``/``matmul``/``dot``/``linalg.norm``/``set_backend``/
+  ``use_backend`` -- the same public API for environments without OpenPacho.
+* :mod:`pacho_b200.distributed` -- sharded GEMM and norm across GPUs (NCCL).
+"""
+
+from . import linalg
+from .api import (
+    array,
+    asarray,
+    asnumpy,
+    dot,
+    empty,
+    full,
+    get_backend,
+    matmul,
+    ndarray,
+    ones,
+    reshape,
+    set_backend,
+    synchronize,
+    to_backend,
+    use_backend,
+    zeros,
+)
+from .backend import B200Backend, DeviceBuffer
+from .exceptions import BackendMismatchError, BackendUnavailableError, UnsupportedDtypeError
+from .register import register, unregister
+
+__version__ = "0.1.0"
+
+__all__ = [
+    "B200Backend",
+    "BackendMismatchError",
+    "BackendUnavailableError",
+    "DeviceBuffer",
+    "UnsupportedDtypeError",
+    "array",
+    "asarray",
+    "asnumpy",
+    "dot",
+    "empty",
+    "full",
+    "get_backend",
+    "linalg",
+    "matmul",
+    "ndarray",
+    "ones",
+    "register",
+    "reshape",
+    "set_backend",
+    "synchronize",
+    "to_backend",
+    "unregister",
+    "use_backend",
+    "zeros",
+]

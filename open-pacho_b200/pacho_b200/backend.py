@@ -1,0 +1,310 @@
+"""``B200Backend``: OpenPacho's backend protocol implemented on libpacho_b200.
+
+The object plugs in where OpenPacho's ``NumpyBackend``/``CUDABackend`` do
+(src/openpacho/backends.py:82-150, src/openpacho/_cuda.py:129-679): the
+front end calls ``validate_dtype``, ``upload``, ``download``, ``empty``,
+``full``, ``matmul(a, b, shape, dtype)``, ``norm(a, axes, keepdims, dtype)``
+and ``synchronize`` with operands that expose ``shape``, ``ndim``, ``dtype``
+and ``_data``.  Storage is a :class:`DeviceBuffer` (flat, C-contiguous).
+Operations outside the linear-algebra hot path raise ``NotImplementedError``;
+nothing ever runs on the host CPU instead.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import threading
+import weakref
+from contextlib import contextmanager
+from math import prod
+
+import numpy as np
+
+from . import _lib
+from .exceptions import BackendUnavailableError, UnsupportedDtypeError
+
+SUPPORTED = (np.dtype(np.float32), np.dtype(np.float64))
+
+
+class DeviceBuffer:
+    """Flat device allocation owned by one backend (cf. ``_Allocation``,
+    src/openpacho/_cuda.py:100-126).  Freed stream-ordered when collected."""
+
+    __slots__ = ("backend", "ptr", "nbytes", "__weakref__")
+
+    def __init__(self, backend: "B200Backend", ptr: int, nbytes: int):
+        self.backend = backend
+        self.ptr = ptr
+        self.nbytes = nbytes
+
+    def __int__(self):
+        return self.ptr
+
+    def release(self):
+        ptr, self.ptr = self.ptr, 0
+        backend = self.backend
+        if ptr and backend is not None and not backend._closed:
+            with backend._lock:
+                backend._lib.pb_free(backend._ctx, 0, C.c_void_p(ptr))
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+
+def _matrix_strides(batch, own):
+    """Per broadcast batch dim, the stride in whole matrices of an operand
+    whose own batch shape is ``own`` (0 where the operand broadcasts)."""
+    padded = (1,) * (len(batch) - len(own)) + tuple(own)
+    strides = []
+    for j, dim in enumerate(padded):
+        strides.append(0 if dim == 1 else prod(padded[j + 1 :]))
+    return strides
+
+
+class B200Backend:
+    """OpenPacho backend object for one B200 GPU (the ``"b200"`` name)."""
+
+    name = "b200"
+    fp64 = True
+
+    def __init__(self, device=None):
+        self._lib = _lib.load()
+        identifier = 0 if device is None else int(str(device))
+        count = C.c_int(0)
+        status = self._lib.pb_device_count(C.byref(count))
+        if status != _lib.PB_OK or count.value == 0:
+            raise BackendUnavailableError(f"no CUDA device for b200: {_lib.last_error()}")
+        if not 0 <= identifier < count.value:
+            raise BackendUnavailableError(f"b200 device {device!r} not found ({count.value} visible)")
+        name = C.create_string_buffer(256)
+        total = C.c_size_t(0)
+        sms, major, minor = C.c_int(), C.c_int(), C.c_int()
+        _lib.check(
+            self._lib.pb_device_info(identifier, name, 256, C.byref(total), C.byref(sms),
+                                     C.byref(major), C.byref(minor)),
+            "pb_device_info",
+        )
+        self.ordinal = identifier
+        self.device = name.value.decode()
+        self.memory_bytes = total.value
+        self.sm_count = sms.value
+        self.compute_capability = (major.value, minor.value)
+        self._lock = threading.RLock()
+        self._closed = False
+        self._buffers = weakref.WeakSet()
+        ctx = C.c_void_p()
+        ordinals = (C.c_int * 1)(identifier)
+        status = self._lib.pb_init(1, ordinals, C.byref(ctx))
+        if status != _lib.PB_OK:
+            raise BackendUnavailableError(f"b200 initialization failed: {_lib.last_error()}")
+        self._ctx = ctx
+
+    # ---------------------------------------------------------------- basics
+    def __repr__(self):
+        return f"B200Backend(device={self.ordinal}, name={self.device!r})"
+
+    def _check(self, status, what):
+        _lib.check(status, what)
+
+    def _require_open(self):
+        if self._closed:
+            raise RuntimeError("b200 backend is closed")
+
+    def validate_dtype(self, dtype):
+        """float32 and float64 only (the dtypes of the hot path)."""
+        try:
+            dtype = np.dtype(dtype)
+        except TypeError as exc:
+            raise UnsupportedDtypeError(str(exc)) from exc
+        if dtype not in SUPPORTED or not dtype.isnative:
+            raise UnsupportedDtypeError(f"b200 backend supports float32 and float64, not {dtype}")
+        return dtype
+
+    @contextmanager
+    def execution_scope(self):
+        with self._lock:
+            self._require_open()
+            yield
+
+    def synchronize(self):
+        with self._lock:
+            self._require_open()
+            self._check(self._lib.pb_sync(self._ctx, 0), "pb_sync")
+
+    # ---------------------------------------------------------------- memory
+    def _alloc(self, nbytes):
+        ptr = C.c_void_p()
+        with self._lock:
+            self._require_open()
+            self._check(self._lib.pb_alloc(self._ctx, 0, max(int(nbytes), 1), C.byref(ptr)),
+                        "pb_alloc")
+        buf = DeviceBuffer(self, ptr.value, int(nbytes))
+        self._buffers.add(buf)
+        return buf
+
+    def empty(self, shape, dtype):
+        dtype = self.validate_dtype(dtype)
+        return self._alloc(prod(shape) * dtype.itemsize)
+
+    def full(self, shape, value, dtype):
+        dtype = self.validate_dtype(dtype)
+        out = self.empty(shape, dtype)
+        count = prod(shape)
+        if count:
+            with self._lock:
+                self._check(
+                    self._lib.pb_fill(self._ctx, 0, _lib.dtype_code(dtype), C.c_void_p(out.ptr),
+                                      count, float(np.asarray(value, dtype=dtype))),
+                    "pb_fill",
+                )
+        return out
+
+    def upload(self, a):
+        """Synchronous copy: the device buffer snapshots the host array."""
+        host = np.ascontiguousarray(a)
+        self.validate_dtype(host.dtype)
+        out = self._alloc(host.nbytes)
+        if host.nbytes:
+            with self._lock:
+                self._check(
+                    self._lib.pb_h2d(self._ctx, 0, C.c_void_p(out.ptr),
+                                     C.c_void_p(host.ctypes.data), host.nbytes, 1),
+                    "pb_h2d",
+                )
+        return out
+
+    def download(self, a):
+        out = np.empty(a.shape, a.dtype)
+        with self._lock:
+            self._require_open()
+            self._check(
+                self._lib.pb_d2h(self._ctx, 0, C.c_void_p(out.ctypes.data),
+                                 C.c_void_p(a._data.ptr), out.nbytes),
+                "pb_d2h",
+            )
+        return out
+
+    def release_cached_memory(self):
+        with self._lock:
+            self._require_open()
+            self._check(self._lib.pb_trim(self._ctx, 0), "pb_trim")
+
+    # ------------------------------------------------------------ hot path
+    def matmul(self, a, b, shape, dtype):
+        """``a @ b`` with NumPy broadcasting of leading dimensions.
+
+        Mirrors the shape handling of CUDABackend.matmul
+        (src/openpacho/_cuda.py:493-517): vector-vector is a DOT, a trailing
+        vector is a GEMV over the flattened rows of ``a``, everything else one
+        batched GEMM launch with per-operand batch strides (0 = broadcast)."""
+        dtype = self.validate_dtype(dtype)
+        if a.dtype != dtype or b.dtype != dtype:
+            raise NotImplementedError("b200 matmul needs operands already in the result dtype")
+        code = _lib.dtype_code(dtype)
+        m, k = (1, a.shape[0]) if a.ndim == 1 else a.shape[-2:]
+        n = b.shape[-1] if b.ndim > 1 else 1
+        out = self.empty(shape, dtype)
+        if not prod(shape):
+            return out
+        with self._lock:
+            self._require_open()
+            ctx, lib = self._ctx, self._lib
+            A, B, O = C.c_void_p(a._data.ptr), C.c_void_p(b._data.ptr), C.c_void_p(out.ptr)
+            if a.ndim == 1 and b.ndim == 1:
+                self._check(lib.pb_dot(ctx, 0, code, k, A, B, O), "pb_dot")
+            elif b.ndim == 1:
+                rows = prod(a.shape[:-1])
+                self._check(lib.pb_gemv(ctx, 0, code, rows, k, A, B, O), "pb_gemv")
+            else:
+                a_batch = a.shape[:-2] if a.ndim > 1 else ()
+                b_batch = b.shape[:-2]
+                batch = np.broadcast_shapes(a_batch, b_batch)
+                self._check(
+                    lib.pb_gemm(ctx, 0, code, len(batch), _lib.i64_array(batch),
+                                _lib.i64_array(_matrix_strides(batch, a_batch)),
+                                _lib.i64_array(_matrix_strides(batch, b_batch)),
+                                m, n, k, A, B, O),
+                    "pb_gemm",
+                )
+        return out
+
+    def norm(self, a, axes, keepdims, dtype):
+        """Euclidean/Frobenius norm over ``axes`` (norm_data,
+        src/openpacho/_norm.py:39-118); ``keepdims`` only shapes the wrapper."""
+        dtype = self.validate_dtype(dtype)
+        if a.dtype != dtype:
+            raise NotImplementedError("b200 norm needs its input in the result dtype")
+        code = _lib.dtype_code(dtype)
+        shape = tuple(a.shape)
+        axes = tuple(sorted(axes))
+        count = prod(d for i, d in enumerate(shape) if i not in axes)
+        reduced = prod(shape[i] for i in axes)
+        out = self.empty((count,), dtype)
+        if not count:
+            return out
+        with self._lock:
+            self._require_open()
+            X, O = C.c_void_p(a._data.ptr), C.c_void_p(out.ptr)
+            if not axes or axes == tuple(range(axes[0], axes[-1] + 1)):
+                first = axes[0] if axes else len(shape)
+                last = axes[-1] if axes else len(shape) - 1
+                outer = prod(shape[:first])
+                inner = prod(shape[last + 1 :])
+                self._check(
+                    self._lib.pb_norm(self._ctx, 0, code, outer, reduced, inner, X, O), "pb_norm"
+                )
+            else:
+                elem = [prod(shape[i + 1 :]) for i in range(len(shape))]
+                keep = [i for i in range(len(shape)) if i not in axes]
+                self._check(
+                    self._lib.pb_norm_strided(
+                        self._ctx, 0, code, len(keep), _lib.i64_array(shape[i] for i in keep),
+                        _lib.i64_array(elem[i] for i in keep), len(axes),
+                        _lib.i64_array(shape[i] for i in axes),
+                        _lib.i64_array(elem[i] for i in axes), X, O),
+                    "pb_norm_strided",
+                )
+        return out
+
+    def prepare_padded_matmul(self, ashape, bshape, shape, dtype):
+        """Decline the padding hint (src/openpacho/_padding.py:19-22): TMA
+        zero-fills ragged tiles, so padded copies would only add traffic."""
+        return None
+
+    # ------------------------------------------------ outside the hot path
+    def elementwise(self, name, args, shape, dtype):
+        raise NotImplementedError(f"b200 backend implements the linear-algebra path only ({name})")
+
+    def gather(self, a, shape, offset, strides):
+        raise NotImplementedError("b200 backend implements the linear-algebra path only (gather)")
+
+    def reduce(self, a, axes, keepdims, dtype, *, operation="sum"):
+        raise NotImplementedError(f"b200 backend implements the linear-algebra path only ({operation})")
+
+    # --------------------------------------------------------------- timing
+    def launch_count(self) -> int:
+        value = C.c_uint64(0)
+        self._check(self._lib.pb_launch_count(self._ctx, 0, C.byref(value)), "pb_launch_count")
+        return value.value
+
+    def close(self):
+        """Free every live buffer and the context (CUDABackend.close,
+        src/openpacho/_cuda.py:644-673); arrays become unusable."""
+        with self._lock:
+            if self._closed:
+                return
+            self._lib.pb_sync(self._ctx, 0)
+            for buf in list(self._buffers):
+                buf.release()
+            self._closed = True
+            self._lib.pb_destroy(self._ctx)
+            self._ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass

@@ -1,0 +1,90 @@
+"""Install ``"b200"`` into an installed OpenPacho's backend dispatch.
+
+OpenPacho hard-codes its backend names: ``get_backend`` accepts backend
+objects only if they are a ``NumpyBackend`` or are named opencl/vulkan/cuda,
+and strings only from that set (src/openpacho/backends.py:198-214).
+``_array`` binds ``get_backend`` at import (src/openpacho/_array.py:11), as
+does ``random`` (src/openpacho/random.py:17), while ``set_backend`` and
+``use_backend`` look the module global up at call time (backends.py:219,226).
+So :func:`register` wraps ``get_backend`` and rebinds the wrapper in each of
+those places.  The wrapper resolves ``"b200"`` (optionally ``device=``) and
+``B200Backend`` objects and delegates everything else unchanged.
+"""
+
+from __future__ import annotations
+
+from functools import lru_cache
+
+from .backend import B200Backend
+
+_MARK = "_pacho_b200_wrapped"
+
+
+@lru_cache(maxsize=8)
+def _get_b200(device):
+    return B200Backend(device)
+
+
+def register(openpacho=None):
+    """Make ``openpacho.set_backend("b200", device=...)`` and friends work.
+
+    Idempotent.  Returns the OpenPacho module it patched."""
+    if openpacho is None:
+        import openpacho  # type: ignore[import-not-found]
+    import importlib
+
+    backends = importlib.import_module(openpacho.__name__ + ".backends")
+    original = backends.get_backend
+    if getattr(original, _MARK, False):
+        return openpacho
+
+    def get_backend(backend=None, *, device=None, blas=None, clblast_library=None):
+        if isinstance(backend, B200Backend):
+            if device is not None or blas is not None or clblast_library is not None:
+                raise ValueError("device cannot accompany an existing backend")
+            return backend
+        if isinstance(backend, str) and backend == "b200":
+            if blas is not None:
+                raise ValueError("BLAS configuration requires backend='opencl' or 'cuda'")
+            if clblast_library is not None:
+                raise ValueError("clblast_library requires backend='opencl'")
+            return _get_b200(None if device is None else str(device))
+        return original(backend, device=device, blas=blas, clblast_library=clblast_library)
+
+    setattr(get_backend, _MARK, True)
+    get_backend.__wrapped__ = original
+    get_backend.__doc__ = original.__doc__
+    backends.get_backend = get_backend
+    for name in ("_array", "random"):
+        try:
+            module = importlib.import_module(f"{openpacho.__name__}.{name}")
+        except ImportError:
+            continue
+        if getattr(module, "get_backend", None) is original:
+            module.get_backend = get_backend
+    if getattr(openpacho, "get_backend", None) is original:
+        openpacho.get_backend = get_backend
+    return openpacho
+
+
+def unregister(openpacho=None):
+    """Undo :func:`register` (used by tests)."""
+    if openpacho is None:
+        import openpacho  # type: ignore[import-not-found]
+    import importlib
+
+    backends = importlib.import_module(openpacho.__name__ + ".backends")
+    wrapped = backends.get_backend
+    if not getattr(wrapped, _MARK, False):
+        return
+    original = wrapped.__wrapped__
+    backends.get_backend = original
+    for name in ("_array", "random"):
+        try:
+            module = importlib.import_module(f"{openpacho.__name__}.{name}")
+        except ImportError:
+            continue
+        if getattr(module, "get_backend", None) is wrapped:
+            module.get_backend = original
+    if getattr(openpacho, "get_backend", None) is wrapped:
+        openpacho.get_backend = original

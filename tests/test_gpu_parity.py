@@ -1,0 +1,218 @@
+"""CUDA path vs the reference's outputs on the reference's own test cases (B200).
+
+Inputs are regenerated from tests/golden/cases.py (checked against the
+fixture's SHA-256); outputs are compared with the golden reference outputs
+under the acceptance bounds of oracle/tolerance.py:
+GEMM |C - C_ref| <= 4*K*u*(|A||B|), norm relative <= 8u.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import cases
+import numpy as np
+import pytest
+
+import pacho_b200 as pb
+from oracle import exact, numpy_backend, tolerance
+from pacho_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+def _matmul_cases():
+    for gen in (cases.matmul_cases, cases.batched_cases, cases.gemv_cases, cases.dot_cases):
+        yield from gen()
+    yield cases.cancellation_case()
+
+
+def _gpu_matmul(backend, a, b):
+    return pb.asnumpy(pb.matmul(pb.asarray(a, backend=backend), pb.asarray(b, backend=backend)))
+
+
+@pytest.mark.parametrize("case", list(_matmul_cases()), ids=lambda c: c[0])
+def test_matmul_matches_reference(b200, golden, case):
+    data, meta = golden
+    name, a, b = case
+    assert cases.digest(a, b) == meta[name]["inputs"]
+    got = _gpu_matmul(b200, a, b)
+    want = data[name]
+    assert got.shape == want.shape and got.dtype == want.dtype
+    assert tolerance.gemm_violations(got, want, a, b) == 0
+
+
+@pytest.mark.parametrize("case", list(cases.empty_cases()), ids=lambda c: c[0])
+def test_empty_and_k0_products(b200, golden, case):
+    data, _ = golden
+    name, a, b = case
+    got = _gpu_matmul(b200, a, b)
+    np.testing.assert_array_equal(got, data[name])
+    assert got.dtype == data[name].dtype
+
+
+@pytest.mark.parametrize("case", list(cases.signed_cases()), ids=lambda c: c[0])
+def test_gemv_cancellation_signed_zero_and_nonfinite(b200, golden, case):
+    # tests/test_cuda_gemv.py:195-222 of the reference.
+    data, _ = golden
+    name, a, b = case
+    values = _gpu_matmul(b200, a, b)
+    np.testing.assert_array_equal(values, data[name])
+    assert values[0] == 0 and values[1] == 1
+    assert values[2] == 0 and not np.signbit(values[2])
+    assert np.isnan(values[3]) and np.isneginf(values[4])
+
+
+def _norm_cases():
+    for gen in (cases.norm_extreme_cases, cases.norm_special_cases, cases.norm_chunk_cases,
+                cases.norm_distribution_cases):
+        yield from gen()
+
+
+@pytest.mark.parametrize("case", list(_norm_cases()), ids=lambda c: c[0])
+def test_norm_matches_reference(b200, golden, case):
+    data, meta = golden
+    name, x, axis, keepdims = case
+    assert cases.digest(x) == meta[name]["inputs"]
+    got = pb.asnumpy(pb.linalg.norm(pb.asarray(x, backend=b200), axis=axis, keepdims=keepdims))
+    want = data[name]
+    assert got.shape == want.shape and got.dtype == want.dtype
+    assert tolerance.norm_violations(got, want) == 0
+    # A -0.0 row gives +0.0 (tests/test_cuda.py:462 of the reference).
+    assert not np.any(np.signbit(got[got == 0]))
+
+
+def test_norm_extremes_against_exact_decimal(b200):
+    rng = np.random.default_rng(17)
+    for dtype, lo, hi in ((np.float32, -35, 35), (np.float64, -300, 300)):
+        x = (rng.standard_normal(5000) * 10.0 ** rng.uniform(lo, hi, 5000)).astype(dtype)
+        got = pb.linalg.norm(pb.asarray(x, backend=b200)).item()
+        ref = exact.norm_decimal(x)
+        u = tolerance.unit_roundoff(dtype)
+        assert abs(got - ref) <= 2 * u * ref
+
+
+# ------------------------------------------------- both GEMM kernels --
+
+def _call_gemm_ex(backend, a, b, algo):
+    """pb_gemm_ex through the C ABI on uploaded operands."""
+    dtype = np.result_type(a.dtype, b.dtype)
+    batch = np.broadcast_shapes(a.shape[:-2], b.shape[:-2])
+    m, k = a.shape[-2:]
+    n = b.shape[-1]
+    from pacho_b200.backend import _matrix_strides
+
+    da, db = backend.upload(a), backend.upload(b)
+    out_shape = batch + (m, n)
+    dc = backend.empty(out_shape, dtype)
+    status = backend._lib.pb_gemm_ex(
+        backend._ctx, 0, _lib.dtype_code(dtype), len(batch), _lib.i64_array(batch),
+        _lib.i64_array(_matrix_strides(batch, a.shape[:-2])),
+        _lib.i64_array(_matrix_strides(batch, b.shape[:-2])), m, n, k,
+        C.c_void_p(da.ptr), C.c_void_p(db.ptr), C.c_void_p(dc.ptr), algo)
+    _lib.check(status, "pb_gemm_ex")
+    return backend.download(pb.api.ndarray._wrap(dc, out_shape, dtype, backend))
+
+
+def _gemm_shapes():
+    for name, a, b in cases.matmul_cases():
+        if a.ndim == 2 and b.ndim == 2:
+            yield name, a, b
+    for name, a, b in cases.batched_cases():
+        if a.ndim >= 2 and b.ndim >= 2 and a.size and b.size:
+            yield name, a, b
+    rng = np.random.default_rng(11)
+    for m, n, k in ((128, 128, 32), (129, 255, 33), (300, 520, 97), (1, 300, 64), (257, 1, 40),
+                    (64, 64, 1), (200, 136, 1000)):
+        yield (f"rand{m}x{n}x{k}", rng.standard_normal((m, k)).astype(np.float32),
+               rng.standard_normal((k, n)).astype(np.float32))
+
+
+@pytest.mark.parametrize("algo", [_lib.PB_GEMM_SIMT, _lib.PB_GEMM_TF32X3], ids=["simt", "tf32x3"])
+@pytest.mark.parametrize("case", list(_gemm_shapes()), ids=lambda c: c[0])
+def test_every_gemm_kernel_on_every_shape(b200, algo, case):
+    name, a, b = case
+    if algo == _lib.PB_GEMM_TF32X3 and a.dtype != np.float32:
+        pytest.skip("3xTF32 is the float32 kernel")
+    got = _call_gemm_ex(b200, a, b, algo)
+    want = numpy_backend.matmul(a, b)
+    assert tolerance.gemm_violations(got, want, a, b) == 0
+
+
+def test_tf32x3_keeps_float32_accuracy(b200):
+    """3xTF32 must be as accurate as float32 GEMM, unlike plain TF32."""
+    rng = np.random.default_rng(12)
+    a = rng.standard_normal((256, 2048)).astype(np.float32)
+    b = rng.standard_normal((2048, 192)).astype(np.float32)
+    ref = a.astype(np.float64) @ b.astype(np.float64)
+    got = _call_gemm_ex(b200, a, b, _lib.PB_GEMM_TF32X3).astype(np.float64)
+    err = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+
+    def tf32(x):  # what a single TF32 pass would see (round to 10 mantissa bits)
+        bits = x.view(np.uint32).astype(np.uint64)
+        return ((bits + 0x1000) & 0xFFFFE000).astype(np.uint32).view(np.float32)
+
+    one_pass = tf32(a).astype(np.float64) @ tf32(b).astype(np.float64)
+    err_1x = np.linalg.norm(one_pass - ref) / np.linalg.norm(ref)
+    sgemm = np.linalg.norm(numpy_backend.matmul(a, b) - ref) / np.linalg.norm(ref)
+    assert err_1x > 1e-4  # the check can tell TF32 from float32
+    assert err < 1e-6 and err < 4 * sgemm, (err, sgemm)
+
+
+def test_products_overwrite_nan_and_inf_destinations(b200, monkeypatch):
+    # tests/test_cuda.py:345-389 of the reference: every output is written.
+    for dtype in (np.float32, np.float64):
+        for poison in (np.nan, np.inf):
+            for name, a, b in list(cases.matmul_cases())[:4] + [("big", np.ones((130, 70), dtype),
+                                                                  np.ones((70, 260), dtype))]:
+                a, b = a.astype(dtype), b.astype(dtype)
+                expected = numpy_backend.matmul(a, b)
+                dest = b200.full(expected.shape, poison, dtype)
+                original = b200.empty
+
+                def poisoned(shape, requested, dest=dest, shape0=expected.shape):
+                    if tuple(shape) == shape0 and np.dtype(requested) == np.dtype(dtype):
+                        return dest
+                    return original(shape, requested)
+
+                with monkeypatch.context() as patch:
+                    patch.setattr(b200, "empty", poisoned)
+                    got = _gpu_matmul(b200, a, b)
+                assert np.isfinite(got).all(), name
+                assert tolerance.gemm_violations(got, expected, a, b) == 0
+
+
+def test_norm_strided_general_axes(b200):
+    rng = np.random.default_rng(21)
+    x = rng.standard_normal((3, 5, 7, 2))
+    for axis in ((0, 2), (1, 3), (0, 3), (0, 1, 3)):
+        for keep in (False, True):
+            got = pb.asnumpy(pb.linalg.norm(pb.asarray(x, backend=b200), axis=axis, keepdims=keep))
+            want = numpy_backend.norm(x, axis=axis, keepdims=keep)
+            assert got.shape == want.shape
+            assert tolerance.norm_violations(got, want) == 0
+
+
+def test_norm_columns_split_over_blocks(b200):
+    # Reduced axis first with few outputs: split across blocks + merge.
+    rng = np.random.default_rng(22)
+    for dtype in (np.float32, np.float64):
+        x = (rng.standard_normal((20000, 3)) * 10.0 ** rng.uniform(-20, 20, (20000, 3))).astype(dtype)
+        x[5, 1] = np.inf
+        x[7, 2] = np.nan
+        got = pb.asnumpy(pb.linalg.norm(pb.asarray(x, backend=b200), axis=0))
+        want = numpy_backend.norm(x, axis=0)
+        assert tolerance.norm_violations(got, want) == 0
+        assert np.isinf(got[1]) and np.isnan(got[2])
+
+
+def test_repeated_calls_are_deterministic(b200):
+    rng = np.random.default_rng(23)
+    x = rng.standard_normal(1 << 22).astype(np.float32)
+    y = rng.standard_normal(1 << 22).astype(np.float32)
+    dx, dy = pb.asarray(x, backend=b200), pb.asarray(y, backend=b200)
+    dots = {pb.matmul(dx, dy).item() for _ in range(5)}
+    norms = {pb.linalg.norm(dx).item() for _ in range(5)}
+    assert len(dots) == 1 and len(norms) == 1
+    assert math.isclose(next(iter(norms)), float(np.linalg.norm(x.astype(np.float64))), rel_tol=1e-7)
