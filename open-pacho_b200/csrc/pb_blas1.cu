@@ -171,13 +171,16 @@ struct GemvPlan {
   int64_t blocks;
 };
 
-GemvPlan plan_gemv(int64_t rows, int64_t K, int sm_count) {
+GemvPlan plan_gemv(int64_t rows, int64_t K, int64_t elem, int sm_count) {
   GemvPlan p;
   const int64_t resident = (int64_t)sm_count * (2048 / kThreads);
-  if (rows >= 2 * resident || K <= 4096) {
+  if (rows >= 2 * resident || K * elem <= 16384) {
+    // Whole rows per block: one warp per row up to 32 KiB rows (warp-only
+    // reduction), more warps per row beyond that.
     p.nchunks = 1;
     p.chunk = K;
-    int G = K >= 4096 ? 8 : K >= 1024 ? 4 : K >= 256 ? 2 : 1;
+    const int64_t bytes = K * elem;
+    int G = bytes > (128 << 10) ? 8 : bytes > (64 << 10) ? 4 : bytes > (32 << 10) ? 2 : 1;
     p.rows_per_block = kWarps / G;
   } else {
     p.rows_per_block = 1;
@@ -194,7 +197,7 @@ GemvPlan plan_gemv(int64_t rows, int64_t K, int sm_count) {
 
 template <typename T, bool STREAM_X>
 int launch_gemv(Device* d, const T* A, const T* x, T* y, int64_t rows, int64_t K, int64_t lda) {
-  GemvPlan p = plan_gemv(rows, K, d->sm_count);
+  GemvPlan p = plan_gemv(rows, K, sizeof(T), d->sm_count);
   if (p.blocks > INT32_MAX) PB_FAIL(PB_ERR_UNSUPPORTED, "GEMV grid too large");
   T* partial = nullptr;
   unsigned int* cnt = nullptr;

@@ -34,16 +34,19 @@ __device__ __forceinline__ double pow2(int e) {  // 2^e for e in [-1022, 1023]
   return __hiloint2double((e + 1023) << 20, 0);
 }
 
-// Pair merge: a <- a (+) b.
+// Pair merge: a <- a (+) b.  Equal exponents (always the case for float32
+// input, whose pairs all carry e = 0) need no rescaling.
 __device__ __forceinline__ void merge(NormPair& a, const NormPair& b) {
-  int E = max(a.e, b.e);
-  double s = 0.0;
-  if (a.ssq != 0.0) s += ldexp(a.ssq, 2 * (a.e - E));
-  if (b.ssq != 0.0) s += ldexp(b.ssq, 2 * (b.e - E));
-  // NaN/Inf in ssq (float32 path) propagate through ldexp and the sum.
-  if (!(a.ssq == a.ssq) || !(b.ssq == b.ssq)) s = a.ssq + b.ssq;
-  a.ssq = s;
-  a.e = E;
+  if (a.e == b.e) {
+    a.ssq += b.ssq;
+  } else {
+    const int E = max(a.e, b.e);
+    double s = 0.0;
+    if (a.ssq != 0.0) s += ldexp(a.ssq, 2 * (a.e - E));
+    if (b.ssq != 0.0) s += ldexp(b.ssq, 2 * (b.e - E));
+    a.ssq = s;
+    a.e = E;
+  }
   a.cls = max(a.cls, b.cls);
 }
 
@@ -424,13 +427,16 @@ struct Plan {
   int64_t blocks;
 };
 
-Plan plan_rows(int64_t rows, int64_t K, int sm_count) {
+Plan plan_rows(int64_t rows, int64_t K, int64_t elem, int sm_count) {
   Plan p;
   const int64_t resident = (int64_t)sm_count * (2048 / kThreads);
-  if (rows >= 2 * resident || K <= 4096) {
+  if (rows >= 2 * resident || K * elem <= 16384) {
+    // Whole rows per block: a warp per row up to 32 KiB rows (warp-only
+    // reduction), more warps per row beyond that.
     p.nchunks = 1;
     p.chunk = K;
-    int G = K >= 4096 ? 8 : K >= 1024 ? 4 : K >= 256 ? 2 : 1;
+    const int64_t bytes = K * elem;
+    int G = bytes > (128 << 10) ? 8 : bytes > (64 << 10) ? 4 : bytes > (32 << 10) ? 2 : 1;
     p.rows_per_block = kWarps / G;
   } else {
     p.rows_per_block = 1;
@@ -447,7 +453,7 @@ Plan plan_rows(int64_t rows, int64_t K, int sm_count) {
 
 template <typename T, bool PAIR_OUT>
 int launch_rows(Device* d, const T* x, T* out, NormPair* pair_out, int64_t rows, int64_t K) {
-  Plan p = plan_rows(rows, K, d->sm_count);
+  Plan p = plan_rows(rows, K, sizeof(T), d->sm_count);
   if (p.blocks > INT32_MAX) PB_FAIL(PB_ERR_UNSUPPORTED, "norm grid too large");
   NormPair* partial = nullptr;
   unsigned int* cnt = nullptr;

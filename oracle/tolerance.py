@@ -3,6 +3,13 @@
 * GEMM/GEMV/DOT, elementwise: |C - C_ref| <= 4 * K * u * (|A| |B|)_ij with
   u = 2^-24 (float32) or 2^-53 (float64); |A||B| is formed in float64.
 * Norm, relative: |n - n_ref| <= 8 * u * |n_ref| (NaN matches NaN, Inf Inf).
+  Where the NumPy reference is itself further than that from the exact value
+  (float32 normalisation and squaring, src/openpacho/_norm.py:47-49), an
+  optional exact reference makes the error attributable: a result within 2u
+  of the exact norm also passes.
+* Forced 3xTF32 at tiny K: each product carries up to ~12u of split error
+  (dropped lo*lo, tf32 rounding of the lo parts), so ``extra_u=16`` widens the
+  bound by 16*u*(|A||B|); automatic dispatch sends K < 32 to the SIMT kernel.
 """
 
 from __future__ import annotations
@@ -16,18 +23,19 @@ def unit_roundoff(dtype) -> float:
     return UNIT_ROUNDOFF[np.dtype(dtype)]
 
 
-def gemm_bound(a: np.ndarray, b: np.ndarray, dtype=None) -> np.ndarray:
-    """Elementwise 4*K*u*(|A||B|) for ``a @ b`` (broadcasting like matmul)."""
+def gemm_bound(a: np.ndarray, b: np.ndarray, dtype=None, extra_u: float = 0.0) -> np.ndarray:
+    """Elementwise (4*K + extra_u)*u*(|A||B|) for ``a @ b`` (broadcasting like matmul)."""
     dtype = np.dtype(dtype or np.result_type(a.dtype, b.dtype))
     k = a.shape[-1]
     absprod = np.abs(a.astype(np.float64)) @ np.abs(b.astype(np.float64))
-    return 4.0 * max(k, 1) * unit_roundoff(dtype) * absprod
+    return (4.0 * max(k, 1) + extra_u) * unit_roundoff(dtype) * absprod
 
 
-def gemm_violations(c: np.ndarray, c_ref: np.ndarray, a: np.ndarray, b: np.ndarray) -> int:
+def gemm_violations(c: np.ndarray, c_ref: np.ndarray, a: np.ndarray, b: np.ndarray,
+                    extra_u: float = 0.0) -> int:
     """Number of elements outside the GEMM bound (non-finite must match)."""
     c64, r64 = np.asarray(c, np.float64), np.asarray(c_ref, np.float64)
-    bound = gemm_bound(a, b, c_ref.dtype)
+    bound = gemm_bound(a, b, c_ref.dtype, extra_u)
     finite = np.isfinite(r64)
     bad = np.zeros(r64.shape, dtype=bool)
     bad |= finite & ~(np.abs(c64 - r64) <= bound)
@@ -35,13 +43,20 @@ def gemm_violations(c: np.ndarray, c_ref: np.ndarray, a: np.ndarray, b: np.ndarr
     return int(bad.sum())
 
 
-def norm_violations(n: np.ndarray, n_ref: np.ndarray, dtype=None) -> int:
-    """Number of norms outside 8u relative error (non-finite must match)."""
+def norm_violations(n: np.ndarray, n_ref: np.ndarray, dtype=None, exact=None) -> int:
+    """Number of norms outside 8u relative error (non-finite must match).
+
+    ``exact`` (float64, same shape) lets a result that is within 2u of the
+    exact norm pass even where the reference itself is off by more than 8u."""
     dtype = np.dtype(dtype or np.asarray(n_ref).dtype)
     n64, r64 = np.asarray(n, np.float64), np.asarray(n_ref, np.float64)
     finite = np.isfinite(r64)
-    rel = 8.0 * unit_roundoff(dtype)
+    u = unit_roundoff(dtype)
+    ok = np.abs(n64 - r64) <= 8.0 * u * np.abs(r64)
+    if exact is not None:
+        e64 = np.asarray(exact, np.float64)
+        ok |= np.abs(n64 - e64) <= 2.0 * u * np.abs(e64)
     bad = np.zeros(r64.shape, dtype=bool)
-    bad |= finite & ~(np.abs(n64 - r64) <= rel * np.abs(r64))
+    bad |= finite & ~ok
     bad |= ~finite & ~((np.isnan(r64) & np.isnan(n64)) | (r64 == n64))
     return int(bad.sum())
