@@ -137,6 +137,23 @@ int pb_gemv(pb_ctx* ctx, int dev, int dtype, int64_t rows, int64_t K, const void
 int pb_dot(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, const void* y,
            void* out);
 
+/* pb_dot for callers that cannot call cudaMalloc -- for example an engine
+ * that hands all device memory to its own allocator up front and forbids
+ * other allocations, or a latency-critical loop that must never enter the
+ * driver's allocator (which can block, or fail when memory is fully
+ * reserved).  Same kernel and result as pb_dot; it allocates nothing.  The
+ * caller passes x, y and out as usual.  The DOT's partial sums go to a fixed
+ * 33 KiB device array inside the library (room for 4096 partials; a DOT uses
+ * at most 16 per SM, 2368 on a B200), which every GPU that loads the library
+ * keeps until the process exits; a plan needing more is rejected with
+ * PB_ERR_UNSUPPORTED.  The first call on each device looks the array's
+ * address up with that device current -- make that first call before any
+ * stream capture.  All calls share the one array: calls ordered on one
+ * context's stream are safe, calls that overlap on the GPU (other streams or
+ * contexts on the same device) race.  No counterpart in the reference. */
+int pb_dot_noalloc(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, const void* y,
+                   void* out);
+
 /* out[o*inner + i] = || x[o, :, i] ||_2 over the middle axis of the
  * contiguous view (outer, reduced, inner).  Overflow/underflow-safe; NaN
  * dominates Inf; -0.0 yields +0.0; reduced == 0 yields 0.

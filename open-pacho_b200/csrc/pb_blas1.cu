@@ -220,6 +220,70 @@ int launch_gemv(Device* d, const T* A, const T* x, T* y, int64_t rows, int64_t K
   return PB_OK;
 }
 
+// ---- DOT for callers that cannot allocate ------------------------------
+// pb_dot_noalloc runs the same DOT kernel as pb_dot, but its per-block partial
+// sums and arrival counter live in this fixed file-scope device array instead
+// of the context's scratch, so the call never allocates.  The array is part of
+// the library image: every GPU that loads the library holds it (33 KiB) until
+// the process exits.
+constexpr int kStaticDotPartials = 4096;
+constexpr size_t kStaticDotCounterOffset = kStaticDotPartials * sizeof(double);
+static __device__ __align__(256) unsigned char g_dot_scratch[kStaticDotCounterOffset + 256];
+
+// In host code `g_dot_scratch` is only a host-side stand-in for the device
+// array; its device address is looked up once per device, with that device
+// current, and cached here by CUDA ordinal.
+constexpr int kMaxOrdinals = 64;
+std::mutex g_dot_scratch_mu;
+void* g_dot_scratch_addr[kMaxOrdinals] = {};
+
+int dot_scratch_address(Device* d, void** out) {
+  if (d->ordinal < 0 || d->ordinal >= kMaxOrdinals)
+    PB_FAIL(PB_ERR_UNSUPPORTED, "pb_dot_noalloc supports CUDA ordinals below %d", kMaxOrdinals);
+  std::lock_guard<std::mutex> g(g_dot_scratch_mu);
+  if (!g_dot_scratch_addr[d->ordinal]) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_dot_scratch);
+    if (e != cudaSuccess || !ptr)
+      PB_FAIL(PB_ERR_CUDA, "cudaGetSymbolAddress(static DOT scratch) failed: %s",
+              cudaGetErrorString(e));
+    g_dot_scratch_addr[d->ordinal] = ptr;
+  }
+  *out = g_dot_scratch_addr[d->ordinal];
+  return PB_OK;
+}
+
+template <typename T>
+int launch_dot_static(Device* d, const T* x, const T* y, T* out, int64_t n) {
+  GemvPlan p = plan_gemv(1, n, sizeof(T), d->sm_count);
+  if (p.nchunks > kStaticDotPartials)
+    PB_FAIL(PB_ERR_UNSUPPORTED,
+            "pb_dot_noalloc: this DOT needs %d partial sums but the static scratch holds %d",
+            p.nchunks, kStaticDotPartials);
+  T* partial = nullptr;
+  unsigned int* cnt = nullptr;
+  if (p.nchunks > 1) {
+    void* base;
+    PB_CHECK(dot_scratch_address(d, &base));
+    partial = (T*)base;
+    cnt = (unsigned int*)((char*)base + kStaticDotCounterOffset);
+    // The array keeps whatever the previous call left; the arrival counter must
+    // start at zero.  (A memset of existing memory allocates nothing.)
+    PB_CUDA(cudaMemsetAsync(cnt, 0, sizeof(unsigned int), d->stream));
+  }
+  constexpr int VN = V16<T>::n;
+  const bool aligned =
+      ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && (p.chunk % VN == 0);
+  if (aligned)
+    gemv_kernel<T, true, true><<<(unsigned)p.blocks, kThreads, 0, d->stream>>>(
+        x, y, out, 1, n, n, p.rows_per_block, p.chunk, p.nchunks, partial, cnt);
+  else
+    gemv_kernel<T, false, true><<<(unsigned)p.blocks, kThreads, 0, d->stream>>>(
+        x, y, out, 1, n, n, p.rows_per_block, p.chunk, p.nchunks, partial, cnt);
+  PB_LAUNCHED(d);
+  return PB_OK;
+}
+
 template <typename T>
 int launch_fill(Device* d, T* out, size_t n, T value) {
   if (!n) return PB_OK;
@@ -288,6 +352,23 @@ int pb_dot(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, const void
   if (dtype == PB_F64)
     return launch_gemv<double, true>(d, (const double*)x, (const double*)y, (double*)out, 1, n,
                                      n);
+  PB_FAIL(PB_ERR_INVALID, "unknown dtype %d", dtype);
+}
+
+int pb_dot_noalloc(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, const void* y,
+                   void* out) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  if (n < 0) PB_FAIL(PB_ERR_INVALID, "negative DOT length");
+  if (!out) PB_FAIL(PB_ERR_INVALID, "null output");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  if (!n) return fill_device(d, dtype, out, 1, 0.0);
+  if (!x || !y) PB_FAIL(PB_ERR_INVALID, "null input");
+  if (dtype == PB_F32)
+    return launch_dot_static<float>(d, (const float*)x, (const float*)y, (float*)out, n);
+  if (dtype == PB_F64)
+    return launch_dot_static<double>(d, (const double*)x, (const double*)y, (double*)out, n);
   PB_FAIL(PB_ERR_INVALID, "unknown dtype %d", dtype);
 }
 

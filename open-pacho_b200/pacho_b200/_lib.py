@@ -66,6 +66,7 @@ PROTOTYPES = {
     "pb_gemm_ex": [_ctx, _i, _i, _i, _pi64, _pi64, _pi64, _i64, _i64, _i64, _p, _p, _p, _i],
     "pb_gemv": [_ctx, _i, _i, _i64, _i64, _p, _p, _p],
     "pb_dot": [_ctx, _i, _i, _i64, _p, _p, _p],
+    "pb_dot_noalloc": [_ctx, _i, _i, _i64, _p, _p, _p],
     "pb_norm": [_ctx, _i, _i, _i64, _i64, _i64, _p, _p],
     "pb_norm_strided": [_ctx, _i, _i, _i, _pi64, _pi64, _i, _pi64, _pi64, _p, _p],
     "pb_comm_unique_id": [C.c_char_p],
