@@ -97,3 +97,10 @@ def test_tolerance_flags_planted_errors():
     nan = n.copy()
     nan[0] = np.nan
     assert tolerance.norm_violations(nan, n) == 1
+    # With an exact reference, a result closer to exact than a poor reference passes,
+    # one further away does not.
+    exact_n = n.astype(np.float64)
+    poor_ref = (exact_n * (1 + 20 * 2.0**-24)).astype(np.float32)
+    assert tolerance.norm_violations(n, poor_ref, exact=exact_n) == 0
+    worse = (exact_n * (1 - 40 * 2.0**-24)).astype(np.float32)
+    assert tolerance.norm_violations(worse, poor_ref, exact=exact_n) == n.size
