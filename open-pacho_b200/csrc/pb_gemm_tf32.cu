@@ -34,7 +34,6 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 32;  // fp32 elements per 128-byte swizzled row
 constexpr int STAGES = 4;
-constexpr int THREADS = 128;
 constexpr uint64_t kTimeoutNs = 4ull * 1000 * 1000 * 1000;
 
 // ------------------------------------------------------------ split pass --
@@ -204,13 +203,32 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 
 // ------------------------------------------------------------ GEMM kernel --
+//
+// Persistent kernel, one CTA per SM, 10 warps:
+//   warp 0      TMA producer (one elected lane) for the 4-stage A/B ring;
+//   warp 1      TMEM allocator and MMA issuer (one elected lane);
+//   warps 2..9  accumulator warps.  The MMA thread accumulates P = 4 K-slices
+//               (16 tcgen05.mma steps) into one of two TMEM buffers, then
+//               commits it; the accumulator warps add that chunk into float32
+//               registers with round-to-nearest and release the buffer.  The
+//               tensor core's own accumulation truncates (~0.3 ulp of bias per
+//               step, growing linearly with K), so promoting every 16 steps
+//               keeps 3xTF32 at float32-class accuracy.  With two buffers the
+//               promotion of chunk c overlaps the MMAs of chunk c+1, and the
+//               store of one tile overlaps the next tile's first chunks.
+// Warp w (2..9) reads TMEM lane quadrant w % 4 (rows 32*(w%4) .. +31 of the
+// tile) and column half (w - 2) / 4 of the BN columns.
+
+constexpr int CHUNK = 4;                 // K-slices per promotion
+constexpr int ACC_WARPS = 8;
+constexpr int GEMM_THREADS = 32 * (2 + ACC_WARPS);
 
 struct Tf32Params {
   float* C;
   int64_t M, N;
   int kblocks;  // K' / 32
   int tiles_m, tiles_n;
-  int64_t batch;
+  int64_t tiles;  // tiles_m * tiles_n * batch
   BatchMap map;
   int* err;
 };
@@ -220,11 +238,37 @@ struct Smem {
   static constexpr int A_BYTES = BM * BK * 4;
   static constexpr int B_BYTES = BN * BK * 4;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int TOTAL = STAGES * STAGE + 1024 /*align slack*/ + 256 /*barriers*/;
+  // barriers: full[S], empty[S], accf[2], acce[2]; then tmem slot and abort flag
+  static constexpr int TOTAL = STAGES * STAGE + 1024 /*align slack*/ + 256;
 };
 
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+struct TileCoord {
+  int64_t bz, m_tile, n_tile;
+};
+
+// Tile t -> (batch, m, n): batches in order; inside a batch a grouped raster
+// of 16 M-tiles so CTAs running together share A and B tiles in L2.
+__device__ __forceinline__ TileCoord tile_coord(const Tf32Params& p, int64_t t) {
+  constexpr int GM = 16;
+  const int64_t per_batch = (int64_t)p.tiles_m * p.tiles_n;
+  TileCoord c;
+  c.bz = t / per_batch;
+  const int64_t r = t % per_batch;
+  const int64_t per_group = (int64_t)GM * p.tiles_n;
+  const int64_t first_m = (r / per_group) * GM;
+  const int64_t gm = min((int64_t)GM, (int64_t)p.tiles_m - first_m);
+  const int64_t in_group = r % per_group;
+  c.m_tile = first_m + in_group % gm;
+  c.n_tile = in_group / gm;
+  return c;
+}
+
 template <int BN>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
     tf32x3_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b, Tf32Params p) {
   extern __shared__ unsigned char smem_raw[];
@@ -234,30 +278,23 @@ __global__ void __launch_bounds__(THREADS, 1)
   unsigned char* gbase = smem_raw + (base - raw);
   const uint32_t bars = base + STAGES * Smem<BN>::STAGE;
   uint64_t* bar_ptr = reinterpret_cast<uint64_t*>(gbase + STAGES * Smem<BN>::STAGE);
-  // Layout after the stages: full[STAGES], empty[STAGES], done, tmem slot, abort.
-  const uint32_t full0 = bars, empty0 = bars + 8 * STAGES, done = bars + 16 * STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 2 * STAGES + 1);
+  const uint32_t full0 = bars, empty0 = bars + 8 * STAGES;
+  const uint32_t accf0 = bars + 16 * STAGES, acce0 = accf0 + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 2 * STAGES + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  // Tile coordinates: grouped raster (16 M-tiles per group) for L2 reuse.
-  const int64_t t = blockIdx.x;
-  constexpr int GM = 16;
-  const int64_t per_group = (int64_t)GM * p.tiles_n;
-  const int64_t group = t / per_group;
-  const int64_t first_m = group * GM;
-  const int64_t gm = min((int64_t)GM, (int64_t)p.tiles_m - first_m);
-  const int64_t in_group = t % per_group;
-  const int64_t m_tile = first_m + in_group % gm;
-  const int64_t n_tile = in_group / gm;
+  constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
-    mbar_init(done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf0 + 8 * b, 1);
+      mbar_init(acce0 + 8 * b, ACC_WARPS);
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -265,109 +302,142 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"((uint32_t)BN));
+                 "r"(TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
+  const int nk = p.kblocks;
+  const int nchunks = (nk + CHUNK - 1) / CHUNK;
 
-  for (int64_t bz = blockIdx.y; bz < p.batch; bz += gridDim.y) {
-    int64_t ao, bo;
-    batch_offsets(p.map, bz, &ao, &bo);
-    const int32_t a_row = (int32_t)(ao * p.M + m_tile * BM);
-    const int32_t b_row = (int32_t)(bo * p.N + n_tile * BN);
-    const int64_t iter = (bz - blockIdx.y) / gridDim.y;  // phase offset across batch loops
-    const int nk = p.kblocks;
-    const int64_t kbase = iter * nk;
-
-    if (warp == 0) {
-      if (lane == 0) {
-        int issued = 0;
-        for (int kb = 0; kb < nk; ++kb) {
-          const int64_t g = kbase + kb;
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      int64_t g = 0;  // k-slices issued by this CTA (ring position)
+      for (int64_t t = blockIdx.x; t < p.tiles && !*abort_flag; t += gridDim.x) {
+        const TileCoord tc = tile_coord(p, t);
+        int64_t ao, bo;
+        batch_offsets(p.map, tc.bz, &ao, &bo);
+        const int32_t a_row = (int32_t)(ao * p.M + tc.m_tile * BM);
+        const int32_t b_row = (int32_t)(bo * p.N + tc.n_tile * BN);
+        for (int kb = 0; kb < nk; ++kb, ++g) {
           const int s = (int)(g % STAGES);
-          const uint32_t ph = (uint32_t)((g / STAGES) & 1);
-          if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag, p.err)) break;
+          if (!mbar_wait(empty0 + 8 * s, (uint32_t)(((g / STAGES) & 1) ^ 1), abort_flag, p.err))
+            break;
           const uint32_t sa = base + s * Smem<BN>::STAGE;
-          const uint32_t sb = sa + Smem<BN>::A_BYTES;
           mbar_expect_tx(full0 + 8 * s, Smem<BN>::STAGE);
           tma_load_2d(sa, &map_a, kb * BK, a_row, full0 + 8 * s);
-          tma_load_2d(sb, &map_b, kb * BK, b_row, full0 + 8 * s);
-          ++issued;
+          tma_load_2d(sa + Smem<BN>::A_BYTES, &map_b, kb * BK, b_row, full0 + 8 * s);
         }
-        if (*abort_flag) {
-          // Drain: wait (bounded) for the copies this thread issued.
-          for (int kb = (issued > STAGES ? issued - STAGES : 0); kb < issued; ++kb) {
-            const int64_t g = kbase + kb;
-            const uint64_t t0 = globaltimer();
-            while (!mbar_try_wait(full0 + 8 * (int)(g % STAGES), (uint32_t)((g / STAGES) & 1)) &&
-                   globaltimer() - t0 < kTimeoutNs) {
-            }
+      }
+      if (*abort_flag) {
+        // Drain (bounded): the last STAGES copies this thread may have issued.
+        for (int64_t q = (g > STAGES ? g - STAGES : 0); q < g; ++q) {
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(full0 + 8 * (int)(q % STAGES), (uint32_t)((q / STAGES) & 1)) &&
+                 globaltimer() - t0 < kTimeoutNs) {
           }
         }
       }
-    } else if (warp == 1) {
-      if (lane == 0) {
-        const uint32_t idesc = instr_desc(BN);
-        for (int kb = 0; kb < nk; ++kb) {
-          const int64_t g = kbase + kb;
-          const int s = (int)(g % STAGES);
-          const uint32_t ph = (uint32_t)((g / STAGES) & 1);
-          if (!mbar_wait(full0 + 8 * s, ph, abort_flag, p.err)) break;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      const uint32_t idesc = instr_desc(BN);
+      int64_t g = 0, gc = 0;  // k-slices consumed / chunks produced by this CTA
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+        for (int c = 0; c < nchunks && ok; ++c, ++gc) {
+          const int buf = (int)(gc & 1);
+          ok = mbar_wait(acce0 + 8 * buf, (uint32_t)(((gc >> 1) & 1) ^ 1), abort_flag, p.err);
+          if (!ok) break;
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t sa = base + s * Smem<BN>::STAGE;
-          const uint32_t sb = sa + Smem<BN>::A_BYTES;
-          const uint64_t da = smem_desc(sa), db = smem_desc(sb);
+          const uint32_t d = tmem + (uint32_t)(buf * BN);
+          const int kb_end = min(nk, (c + 1) * CHUNK);
+          for (int kb = c * CHUNK; kb < kb_end; ++kb, ++g) {
+            const int s = (int)(g % STAGES);
+            ok = mbar_wait(full0 + 8 * s, (uint32_t)((g / STAGES) & 1), abort_flag, p.err);
+            if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t sa = base + s * Smem<BN>::STAGE;
+            const uint64_t da = smem_desc(sa), db = smem_desc(sa + Smem<BN>::A_BYTES);
 #pragma unroll
-          for (int k = 0; k < BK / 8; ++k) {
-            // +32 bytes per 8-element K step inside the swizzled row.
-            umma_tf32(tmem, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < BK / 8; ++k)  // +32 bytes per 8-element K step
+              umma_tf32(d, da + 2 * k, db + 2 * k, idesc, (kb > c * CHUNK || k > 0) ? 1u : 0u);
+            umma_commit(empty0 + 8 * s);
           }
-          umma_commit(empty0 + 8 * s);
-        }
-        umma_commit(done);  // arrives once every issued MMA has completed
-      }
-    }
-    __syncwarp();
-
-    // Epilogue: all four warps; warp w owns TMEM lanes (tile rows) 32w..32w+31.
-    const bool ok = mbar_wait(done, (uint32_t)(iter & 1), abort_flag, p.err);
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    // tcgen05.ld is warp-collective: take the decision once per warp.
-    if (__all_sync(0xffffffffu, ok && !*abort_flag)) {
-      const int64_t row = m_tile * BM + warp * 32 + lane;
-      float* crow = p.C + bz * p.M * p.N + row * p.N;
-      const bool vec = (p.N % 4) == 0;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(c * 32), r);
-        const int64_t col0 = n_tile * BN + c * 32;
-        if (row < p.M) {
-          if (vec && col0 + 32 <= p.N) {
-            float4* dst = reinterpret_cast<float4*>(crow + col0);
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < p.N) crow[col0 + j] = __uint_as_float(r[j]);
-          }
+          umma_commit(accf0 + 8 * buf);  // chunk complete -> accumulator warps
         }
       }
     }
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();
-    if (*abort_flag) break;
+  } else {
+    // -------------------------------------------------- accumulator warps
+    constexpr int COLS = BN / 2;
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * COLS);
+    int64_t gc = 0;
+    for (int64_t t = blockIdx.x; t < p.tiles; t += gridDim.x) {
+      const TileCoord tc = tile_coord(p, t);
+      float acc[COLS];
+#pragma unroll
+      for (int i = 0; i < COLS; ++i) acc[i] = 0.0f;
+      bool ok = true;
+      for (int c = 0; c < nchunks; ++c, ++gc) {
+        const int buf = (int)(gc & 1);
+        ok = mbar_wait(accf0 + 8 * buf, (uint32_t)((gc >> 1) & 1), abort_flag, p.err);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int piece = 0; piece < COLS / 32; ++piece) {
+          uint32_t r[32];
+          tmem_ld32(lane_base + (uint32_t)(buf * BN + piece * 32), r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[piece * 32 + i] += __uint_as_float(r[i]);
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acce0 + 8 * buf);
+      }
+      if (!ok || *abort_flag) break;
+      // Store this thread's row segment of the finished tile.
+      const int64_t row = tc.m_tile * BM + quad * 32 + lane;
+      if (row < p.M) {
+        const int64_t col0 = tc.n_tile * BN + half * COLS;
+        float* crow = p.C + tc.bz * p.M * p.N + row * p.N + col0;
+        if ((p.N % 4) == 0 && col0 + COLS <= p.N) {
+          float4* dst = reinterpret_cast<float4*>(crow);
+#pragma unroll
+          for (int j = 0; j < COLS / 4; ++j)
+            dst[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < COLS; ++j)
+            if (col0 + j < p.N) crow[j] = acc[j];
+        }
+      }
+    }
   }
 
+  // Every issued MMA has been consumed by an accumulator warp (or the run was
+  // aborted); make sure the MMAs have landed before TMEM is released.
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
   if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (*abort_flag) {
+      // Bounded wait for the last committed chunk of each buffer.
+      const uint64_t t0 = globaltimer();
+      while (globaltimer() - t0 < 1000000ull) {
+      }
+    }
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"((uint32_t)BN));
+                 "r"(TMEM_COLS));
   }
 }
 
@@ -395,10 +465,9 @@ int launch_tf32(Device* d, const CUtensorMap& ma, const CUtensorMap& mb, const T
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured = true;
   }
-  const int64_t tiles = (int64_t)p.tiles_m * p.tiles_n;
-  if (tiles > INT32_MAX) PB_FAIL(PB_ERR_UNSUPPORTED, "GEMM grid too large");
-  const unsigned gy = (unsigned)(p.batch < 65535 ? p.batch : 65535);
-  tf32x3_gemm_kernel<BN><<<dim3((unsigned)tiles, gy), THREADS, smem, d->stream>>>(ma, mb, p);
+  // Persistent: one CTA per SM (shared memory allows no more), tiles strided.
+  const int64_t grid = p.tiles < d->sm_count ? p.tiles : d->sm_count;
+  tf32x3_gemm_kernel<BN><<<(unsigned)grid, GEMM_THREADS, smem, d->stream>>>(ma, mb, p);
   PB_LAUNCHED(d);
   return PB_OK;
 }
@@ -459,7 +528,7 @@ int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
   p.kblocks = (int)(K3 / BK);
   p.tiles_m = tiles_m;
   p.tiles_n = (int)ceil_div(N, (int64_t)BN);
-  p.batch = batch;
+  p.tiles = (int64_t)p.tiles_m * p.tiles_n * batch;
   p.map = map;
   p.err = d->err_dev;
   if (BN == 256) return launch_tf32<256>(d, ma, mb, p);
