@@ -37,6 +37,15 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "open-pacho_b200"))
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+# Tensor-pipe ceilings for the GEMM workloads, measured on this pool's B200 with
+# cuBLAS (8192^3, best of 10): TF32 737.7 TFLOP/s -> 3xTF32 ceiling 245.9 logical;
+# FP64 DGEMM 35.5 TFLOP/s.  MEASURED_PEAKS.json carries bf16 only.
+TENSOR_CEILINGS = {
+    "gemm1024": (737.7 / 3, "measured cuBLAS TF32 / 3"),
+    "gemm_f32": (737.7 / 3, "measured cuBLAS TF32 / 3"),
+    "batched": (737.7 / 3, "measured cuBLAS TF32 / 3"),
+    "gemm_f64": (35.5, "measured cuBLAS DGEMM"),
+}
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -169,6 +178,15 @@ class Clocks:
                 "samples": len(self.samples)}
 
 
+def traffic_per_launch(kernel: str, workload: str):
+    """DRAM bytes (read + write) per launch from the committed ncu summary."""
+    path = ROOT / "profiles" / "traffic.json"
+    if not path.exists():
+        return None
+    entry = json.loads(path.read_text()).get(f"{workload}:{kernel}")
+    return None if entry is None else entry.get("dram_bytes_per_launch")
+
+
 def peaks():
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
@@ -197,6 +215,15 @@ class Gpu:
 
     def check(self, status, what):
         self.lib.check(status, what)
+
+    def busy(self, fn, seconds=0.5):
+        """Untimed steps for `seconds` of wall time, so the clock sampler sees
+        the GPU under this workload's load before the timed region."""
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            for _ in range(8):
+                fn()
+            self.check(self.raw.pb_sync(self.ctx, 0), "sync")
 
     def timer(self, fn, reps):
         self.check(self.raw.pb_sync(self.ctx, 0), "sync")
@@ -239,8 +266,9 @@ def run_gemv_dot(gpu: Gpu, args, dist: Dist, result: dict):
     for _ in range(args.warmup):
         step()
     dist.barrier()
-    l0 = gpu.launches()
     with Clocks(gpu.backend.ordinal) as clocks:
+        gpu.busy(step)
+        l0 = gpu.launches()
         seconds = gpu.timer(step, args.steps)
     launches = gpu.launches() - l0
     seconds = dist.max(seconds)
@@ -316,13 +344,13 @@ def e2e_gemv_dot(gpu, A, x, u, v, args, dist):
 def run_gemm(gpu: Gpu, args, dist: Dist, result: dict, which: str):
     raw, ctx = gpu.raw, gpu.ctx
     if which == "gemm1024":
-        A, B = gen_gemm(0, 1024, np.float32)
+        A, B = gen_gemm(0, args.n or 1024, np.float32)
         dtype, shard = np.float32, False
     elif which == "gemm_f32":
-        A, B = gen_gemm(4, 16384, np.float32)
+        A, B = gen_gemm(4, args.n or 16384, np.float32)
         dtype, shard = np.float32, True
     else:
-        A, B = gen_gemm(4, 8192, np.float64)
+        A, B = gen_gemm(4, args.n or 8192, np.float64)
         dtype, shard = np.float64, True
     n = A.shape[0]
     rows = n // dist.world if shard else n
@@ -339,8 +367,9 @@ def run_gemm(gpu: Gpu, args, dist: Dist, result: dict, which: str):
     for _ in range(args.warmup):
         step()
     dist.barrier()
-    l0 = gpu.launches()
     with Clocks(gpu.backend.ordinal) as clocks:
+        gpu.busy(step)
+        l0 = gpu.launches()
         seconds = gpu.timer(step, args.steps)
     launches = gpu.launches() - l0
     seconds = dist.max(seconds)
@@ -379,8 +408,9 @@ def run_batched(gpu: Gpu, args, dist: Dist, result: dict):
     for _ in range(args.warmup):
         step()
     dist.barrier()
-    l0 = gpu.launches()
     with Clocks(gpu.backend.ordinal) as clocks:
+        gpu.busy(step)
+        l0 = gpu.launches()
         seconds = gpu.timer(step, args.steps)
     launches = gpu.launches() - l0
     seconds = dist.max(seconds)
@@ -433,8 +463,9 @@ def run_norm(gpu: Gpu, args, dist: Dist, result: dict, rows: bool):
     for _ in range(args.warmup):
         step()
     dist.barrier()
-    l0 = gpu.launches()
     with Clocks(gpu.backend.ordinal) as clocks:
+        gpu.busy(step)
+        l0 = gpu.launches()
         seconds = gpu.timer(step, args.steps)
     launches = gpu.launches() - l0
     seconds = dist.max(seconds)
@@ -560,6 +591,8 @@ def main(argv=None):
                         choices=("gemv_dot", "gemm1024", "batched", "norm", "norm_rows", "gemm_f32",
                                  "gemm_f64"))
     parser.add_argument("--dtype", choices=("f32", "f64"), default="f32", help="norm workloads")
+    parser.add_argument("--n", type=int, default=0,
+                        help="GEMM size override (profiling captures); 0 = the BASELINE size")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args(argv)
     if args.warmup < 3:
@@ -588,11 +621,16 @@ def main(argv=None):
             achieved = work / sec / 1e9
             roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                     "frac": achieved / pk["hbm_gbs"], "kernel": name, "peak_source": pk["source"],
-                    "traffic": None}
+                    "traffic": traffic_per_launch(name, args.workload),
+                    "algorithmic_bytes": work}
         else:
             achieved = work / sec / 1e12
-            roof = {"bound": "tensor", "achieved": achieved, "peak": None, "unit": "TFLOP/s",
-                    "frac": None, "kernel": name, "traffic": None}
+            ceiling = TENSOR_CEILINGS.get(args.workload)
+            roof = {"bound": "tensor", "achieved": achieved,
+                    "peak": ceiling[0] if ceiling else None, "unit": "TFLOP/s",
+                    "frac": achieved / ceiling[0] if ceiling else None, "kernel": name,
+                    "peak_source": ceiling[1] if ceiling else None,
+                    "traffic": traffic_per_launch(name, args.workload)}
         line = {
             "metric": result.pop("metric"), "value": result.pop("value"), "unit": result.pop("unit"),
             "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,

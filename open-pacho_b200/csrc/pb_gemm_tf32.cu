@@ -129,7 +129,7 @@ __device__ __forceinline__ uint64_t globaltimer() {
 }
 
 // Bounded wait: false if the wait expired or another role already gave up.
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                        int* err) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
@@ -188,18 +188,27 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
       : "memory");
 }
 
+// TMEM -> registers, 32 lanes x 32 columns of 32-bit values.  The wait is part
+// of the same asm statement so no use of the outputs can precede it.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]),"=r"(r[1]),"=r"(r[2]),"=r"(r[3]),"=r"(r[4]),"=r"(r[5]),"=r"(r[6]),"=r"(r[7]),"=r"(r[8]),"=r"(r[9]),"=r"(r[10]),"=r"(r[11]),"=r"(r[12]),"=r"(r[13]),"=r"(r[14]),"=r"(r[15]),"=r"(r[16]),"=r"(r[17]),"=r"(r[18]),"=r"(r[19]),"=r"(r[20]),"=r"(r[21]),"=r"(r[22]),"=r"(r[23]),"=r"(r[24]),"=r"(r[25]),"=r"(r[26]),"=r"(r[27]),"=r"(r[28]),"=r"(r[29]),"=r"(r[30]),"=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+// Two 32-column loads in flight before one wait.
+__device__ __forceinline__ void tmem_ld32x2(uint32_t ta, uint32_t tb, uint32_t (&a)[32],
+                                            uint32_t (&b)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(a[0]),"=r"(a[1]),"=r"(a[2]),"=r"(a[3]),"=r"(a[4]),"=r"(a[5]),"=r"(a[6]),"=r"(a[7]),"=r"(a[8]),"=r"(a[9]),"=r"(a[10]),"=r"(a[11]),"=r"(a[12]),"=r"(a[13]),"=r"(a[14]),"=r"(a[15]),"=r"(a[16]),"=r"(a[17]),"=r"(a[18]),"=r"(a[19]),"=r"(a[20]),"=r"(a[21]),"=r"(a[22]),"=r"(a[23]),"=r"(a[24]),"=r"(a[25]),"=r"(a[26]),"=r"(a[27]),"=r"(a[28]),"=r"(a[29]),"=r"(a[30]),"=r"(a[31]),"=r"(b[0]),"=r"(b[1]),"=r"(b[2]),"=r"(b[3]),"=r"(b[4]),"=r"(b[5]),"=r"(b[6]),"=r"(b[7]),"=r"(b[8]),"=r"(b[9]),"=r"(b[10]),"=r"(b[11]),"=r"(b[12]),"=r"(b[13]),"=r"(b[14]),"=r"(b[15]),"=r"(b[16]),"=r"(b[17]),"=r"(b[18]),"=r"(b[19]),"=r"(b[20]),"=r"(b[21]),"=r"(b[22]),"=r"(b[23]),"=r"(b[24]),"=r"(b[25]),"=r"(b[26]),"=r"(b[27]),"=r"(b[28]),"=r"(b[29]),"=r"(b[30]),"=r"(b[31])
+      : "r"(ta), "r"(tb)
+      : "memory");
 }
 
 // ------------------------------------------------------------ GEMM kernel --
@@ -207,19 +216,28 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 // Persistent kernel, one CTA per SM, 10 warps:
 //   warp 0      TMA producer (one elected lane) for the 4-stage A/B ring;
 //   warp 1      TMEM allocator and MMA issuer (one elected lane);
-//   warps 2..9  accumulator warps.  The MMA thread accumulates P = 4 K-slices
-//               (16 tcgen05.mma steps) into one of two TMEM buffers, then
-//               commits it; the accumulator warps add that chunk into float32
-//               registers with round-to-nearest and release the buffer.  The
-//               tensor core's own accumulation truncates (~0.3 ulp of bias per
-//               step, growing linearly with K), so promoting every 16 steps
-//               keeps 3xTF32 at float32-class accuracy.  With two buffers the
+//   warps 2..9  accumulator warps.  The MMA thread accumulates CHUNK = 8
+//               K-slices (32 tcgen05.mma steps) into one of two TMEM buffers,
+//               then commits it; the accumulator warps add that chunk into
+//               float32 registers with round-to-nearest and release the
+//               buffer.  The tensor core's own accumulation truncates (~0.3 ulp
+//               of bias per step, so the error grew linearly with K: 1.9e-5 at
+//               K=8192 without promotion); promoting every 32 steps keeps
+//               3xTF32 at float32-class accuracy (6.5e-7 at K=8192, flat in K).
+//               Measured on B200: CHUNK 4/8 cost 216.5/226.6 TFLOP/s at 8192^3
+//               for 3.7e-7/6.5e-7 relative error.  With two buffers the
 //               promotion of chunk c overlaps the MMAs of chunk c+1, and the
 //               store of one tile overlaps the next tile's first chunks.
 // Warp w (2..9) reads TMEM lane quadrant w % 4 (rows 32*(w%4) .. +31 of the
 // tile) and column half (w - 2) / 4 of the BN columns.
 
-constexpr int CHUNK = 4;                 // K-slices per promotion
+#ifndef PB_TF32_CHUNK
+#define PB_TF32_CHUNK 8
+#endif
+#ifndef PB_TF32_LD_PAIR
+#define PB_TF32_LD_PAIR 1
+#endif
+constexpr int CHUNK = PB_TF32_CHUNK;     // K-slices per promotion
 constexpr int ACC_WARPS = 8;
 constexpr int GEMM_THREADS = 32 * (2 + ACC_WARPS);
 
@@ -393,6 +411,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           ok = false;
           break;
         }
+#if PB_TF32_LD_PAIR
+        // Two 32-column loads in flight per wait.
+#pragma unroll
+        for (int piece = 0; piece < COLS / 32; piece += 2) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32x2(lane_base + (uint32_t)(buf * BN + piece * 32),
+                      lane_base + (uint32_t)(buf * BN + piece * 32 + 32), r0, r1);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            acc[piece * 32 + i] += __uint_as_float(r0[i]);
+            acc[piece * 32 + 32 + i] += __uint_as_float(r1[i]);
+          }
+        }
+#else
 #pragma unroll
         for (int piece = 0; piece < COLS / 32; ++piece) {
           uint32_t r[32];
@@ -400,6 +432,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) acc[piece * 32 + i] += __uint_as_float(r[i]);
         }
+#endif
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(acce0 + 8 * buf);
