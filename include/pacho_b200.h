@@ -107,7 +107,7 @@ int pb_launch_count(pb_ctx* ctx, int dev, uint64_t* count);
  * with strides in whole matrices (0 = broadcast).  A matrices are M x K,
  * B matrices K x N, C (batch x M x N) is written densely.  K == 0 writes
  * zeros.  float32 uses error-compensated 3xTF32 on tcgen05 tensor cores
- * (never plain TF32), float64 an FP64 tile kernel.
+ * (never plain TF32), float64 the FP64 tensor cores (DMMA).
  * Replaces NumpyBackend.matmul (src/openpacho/backends.py:139-142) and
  * CUDABackend.matmul (src/openpacho/_cuda.py:493-637) with the register GEMM
  * (src/openpacho/_gemm.py:102-137) and broadcast offsets (_gemm.py:13-21). */
@@ -116,11 +116,11 @@ int pb_gemm(pb_ctx* ctx, int dev, int dtype, int batch_ndim, const int64_t* batc
             int64_t K, const void* A, const void* B, void* C);
 
 /* pb_gemm with an explicit kernel choice: PB_GEMM_AUTO (what pb_gemm does),
- * PB_GEMM_SIMT (register-tiled CUDA-core kernel; the only float64 kernel) or
- * PB_GEMM_TF32X3 (float32 only).  The reference exposes the same kind of
+ * PB_GEMM_SIMT (register-tiled CUDA-core FFMA/DFMA kernel), PB_GEMM_TF32X3
+ * (float32 only) or PB_GEMM_DMMA (float64 only, FP64 tensor cores).  The reference exposes the same kind of
  * provider choice as CUDABackend(blas="custom"|"cublas")
  * (src/openpacho/_cuda.py:138-141). */
-enum { PB_GEMM_AUTO = 0, PB_GEMM_SIMT = 1, PB_GEMM_TF32X3 = 2 };
+enum { PB_GEMM_AUTO = 0, PB_GEMM_SIMT = 1, PB_GEMM_TF32X3 = 2, PB_GEMM_DMMA = 3 };
 int pb_gemm_ex(pb_ctx* ctx, int dev, int dtype, int batch_ndim, const int64_t* batch_shape,
                const int64_t* a_bstride, const int64_t* b_bstride, int64_t M, int64_t N,
                int64_t K, const void* A, const void* B, void* C, int algo);

@@ -2,7 +2,7 @@
 //
 // Reference routing: CUDABackend.matmul (src/openpacho/_cuda.py:493-637):
 // K == 0 -> zeros; float32 tiles -> register GEMM; everything else a direct
-// kernel or cuBLAS.  Here: K == 0 -> zeros, float64 -> DFMA tile kernel,
+// kernel or cuBLAS.  Here: K == 0 -> zeros; float64 -> DMMA tensor-core tiles;
 // float32 -> 3xTF32 tcgen05 when the output has at least one 64x64 block and
 // K >= 32, else the float32 SIMT tile kernel.
 #include "pb_internal.cuh"
@@ -12,6 +12,8 @@ namespace pb {
 int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int64_t N, int64_t K,
                   const float* A, const float* B, float* C, int algo);
 int gemm_simt_f64(Device* d, const BatchMap& map, int64_t batch, int64_t M, int64_t N, int64_t K,
+                  const double* A, const double* B, double* C);
+int gemm_dmma_f64(Device* d, const BatchMap& map, int64_t batch, int64_t M, int64_t N, int64_t K,
                   const double* A, const double* B, double* C);
 int fill_device(Device* d, int dtype, void* dst, size_t count, double value);
 
@@ -50,9 +52,13 @@ int gemm_dispatch(pb_ctx* ctx, int dev, int dtype, int batch_ndim, const int64_t
   if (!K) return fill_device(d, dtype, C, (size_t)count, 0.0);
   if (!A || !B) PB_FAIL(PB_ERR_INVALID, "null input");
   if (dtype == PB_F64) {
-    if (algo != 0 && algo != 1) PB_FAIL(PB_ERR_UNSUPPORTED, "float64 GEMM has only the FP64 tile kernel");
-    return gemm_simt_f64(d, map, batch, M, N, K, (const double*)A, (const double*)B, (double*)C);
+    if (algo == PB_GEMM_SIMT)
+      return gemm_simt_f64(d, map, batch, M, N, K, (const double*)A, (const double*)B, (double*)C);
+    if (algo == PB_GEMM_AUTO || algo == PB_GEMM_DMMA)
+      return gemm_dmma_f64(d, map, batch, M, N, K, (const double*)A, (const double*)B, (double*)C);
+    PB_FAIL(PB_ERR_UNSUPPORTED, "float64 GEMM runs on the DMMA or the DFMA (SIMT) kernel");
   }
+  if (algo == PB_GEMM_DMMA) PB_FAIL(PB_ERR_UNSUPPORTED, "DMMA is the float64 kernel");
   return gemm_f32_algo(d, map, batch, M, N, K, (const float*)A, (const float*)B, (float*)C, algo);
 }
 

@@ -30,6 +30,7 @@ PB_F64 = 1
 PB_GEMM_AUTO = 0
 PB_GEMM_SIMT = 1
 PB_GEMM_TF32X3 = 2
+PB_GEMM_DMMA = 3
 
 LIBRARY_NAME = "libpacho_b200.so"
 

@@ -129,12 +129,15 @@ def _gemm_shapes():
                rng.standard_normal((k, n)).astype(np.float32))
 
 
-@pytest.mark.parametrize("algo", [_lib.PB_GEMM_SIMT, _lib.PB_GEMM_TF32X3], ids=["simt", "tf32x3"])
+@pytest.mark.parametrize("algo", [_lib.PB_GEMM_SIMT, _lib.PB_GEMM_TF32X3, _lib.PB_GEMM_DMMA],
+                         ids=["simt", "tf32x3", "dmma"])
 @pytest.mark.parametrize("case", list(_gemm_shapes()), ids=lambda c: c[0])
 def test_every_gemm_kernel_on_every_shape(b200, algo, case):
     name, a, b = case
     if algo == _lib.PB_GEMM_TF32X3 and a.dtype != np.float32:
         pytest.skip("3xTF32 is the float32 kernel")
+    if algo == _lib.PB_GEMM_DMMA:
+        a, b = a.astype(np.float64), b.astype(np.float64)
     got = _call_gemm_ex(b200, a, b, algo)
     want = numpy_backend.matmul(a, b)
     # Forced 3xTF32 below K=32 carries the split error model (auto sends it to SIMT).
