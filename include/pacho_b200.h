@@ -177,6 +177,9 @@ int pb_comm_unique_id(unsigned char id[128]);
 /* Join the communicator of `nranks` processes as `rank` for device `dev`. */
 int pb_comm_init(pb_ctx* ctx, int dev, int nranks, int rank, const unsigned char id[128]);
 int pb_comm_destroy(pb_ctx* ctx, int dev);
+/* Abandon the communicator without waiting for peers (after a peer failed);
+ * outstanding collectives are aborted by NCCL. */
+int pb_comm_abort(pb_ctx* ctx, int dev);
 /* In-place broadcast of `bytes` from `root` (used to give every GPU the
  * shared B operand of a row-block sharded GEMM). */
 int pb_broadcast(pb_ctx* ctx, int dev, void* buf, size_t bytes, int root);

@@ -190,6 +190,15 @@ int pb_comm_destroy(pb_ctx* ctx, int dev) {
   return st;
 }
 
+int pb_comm_abort(pb_ctx* ctx, int dev) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  abort_comm(d);
+  return PB_OK;
+}
+
 int pb_broadcast(pb_ctx* ctx, int dev, void* buf, size_t bytes, int root) {
   if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
   std::lock_guard<std::recursive_mutex> g(ctx->mu);

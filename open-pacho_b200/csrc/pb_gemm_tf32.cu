@@ -14,7 +14,7 @@
 //     the three-product sum, small terms first.
 //  2. GEMM C = A' B't^T on tcgen05: 128 x BN output tile per CTA (BN 128 or
 //     256), K' in 32-element (128-byte) slices moved by TMA with 128-byte
-//     swizzle into a 4-stage shared-memory ring (no multicast), one thread
+//     swizzle into a 4-stage shared-memory ring (each CTA loads its own tiles), one thread
 //     issuing tcgen05.mma.kind::tf32 into a TMEM accumulator, and all four
 //     warps draining TMEM with tcgen05.ld into C.
 //  Every mbarrier wait is bounded in wall time (%globaltimer); on expiry the

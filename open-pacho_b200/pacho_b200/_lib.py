@@ -73,6 +73,7 @@ PROTOTYPES = {
     "pb_comm_unique_id": [C.c_char_p],
     "pb_comm_init": [_ctx, _i, _i, _i, C.c_char_p],
     "pb_comm_destroy": [_ctx, _i],
+    "pb_comm_abort": [_ctx, _i],
     "pb_broadcast": [_ctx, _i, _p, _sz, _i],
     "pb_norm_sharded": [_ctx, _i, _i, _i64, _p, _p],
     "pb_allreduce_sum": [_ctx, _i, _i, _p, _sz],

@@ -1,0 +1,108 @@
+"""Worker for tests/test_gpu_multi.py: one process per GPU under torchrun.
+
+Checks each sharded path against the oracle on the full (unsharded) input:
+the sharded norm (float32 and float64, including a rank with an empty slice),
+the sharded DOT, row-block GEMM with B broadcast from rank 0, and the batch
+split of a broadcast-batched GEMM.  With PB_TEST_FAILURE=1 it then has rank 1
+leave between steps (nothing in flight) and checks that rank 0 detects it on
+the host before launching its next collective and aborts its communicator.
+Prints one ``RESULT {json}`` line per rank.
+"""
+
+from __future__ import annotations
+
+import datetime
+import json
+import os
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(ROOT / "open-pacho_b200"))
+sys.path.insert(0, str(ROOT))
+
+
+def main() -> int:
+    import torch.distributed as dist
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    store = dist.TCPStore(os.environ["MASTER_ADDR"], int(os.environ["PB_STORE_PORT"]), world,
+                          rank == 0, timeout=datetime.timedelta(seconds=120))
+
+    import pacho_b200 as pb
+    from oracle import numpy_backend, tolerance
+    from pacho_b200 import distributed as D
+
+    be = pb.B200Backend(local)
+    group = D.Group(be, rank, world, store, timeout=60)
+    res: dict = {"rank": rank}
+
+    for dtype, span in ((np.float32, 35), (np.float64, 300)):
+        for n in ((1 << 22) + 5, 1):
+            rng = np.random.default_rng(3)
+            x = (rng.standard_normal(n) * 10.0 ** rng.uniform(-span, span, n)).astype(dtype)
+            s, e = D.shard_range(n, rank, world)
+            got = D.sharded_norm(group, pb.asarray(x[s:e], backend=be)).item()
+            want = numpy_backend.norm(x)
+            res[f"norm_{np.dtype(dtype).name}_{n}"] = tolerance.norm_violations(
+                np.asarray(got, dtype), np.asarray(want, dtype))
+
+    rng = np.random.default_rng(4)
+    n = (1 << 21) + 3
+    u = rng.uniform(-1, 1, n).astype(np.float32)
+    v = rng.uniform(-1, 1, n).astype(np.float32)
+    s, e = D.shard_range(n, rank, world)
+    d = D.sharded_dot(group, pb.asarray(u[s:e], backend=be), pb.asarray(v[s:e], backend=be)).item()
+    res["dot"] = tolerance.gemm_violations(np.asarray(d, np.float32), numpy_backend.dot(u, v), u, v)
+
+    for dtype in (np.float32, np.float64):
+        A = rng.standard_normal((1000, 300)).astype(dtype)
+        B = rng.standard_normal((300, 200)).astype(dtype)
+        dB = pb.asarray(B if rank == 0 else np.zeros_like(B), backend=be)
+        D.broadcast(group, dB, root=0)
+        a_local = D.local_rows(A, group)
+        c_local = pb.asnumpy(D.rowblock_matmul(group, pb.asarray(a_local, backend=be), dB))
+        res[f"rowblock_{np.dtype(dtype).name}"] = tolerance.gemm_violations(
+            c_local, numpy_backend.matmul(a_local, B), a_local, B)
+
+    A = rng.standard_normal((4, 3, 130, 65)).astype(np.float32)
+    B = rng.standard_normal((1, 3, 65, 97)).astype(np.float32)
+    a_local = D.local_rows(A, group)
+    c_local = pb.asnumpy(D.batch_matmul(group, pb.asarray(a_local, backend=be),
+                                        pb.asarray(B, backend=be)))
+    res["batch_split"] = tolerance.gemm_violations(c_local, numpy_backend.matmul(a_local, B),
+                                                   a_local, B)
+
+    be.synchronize()
+    if os.environ.get("PB_TEST_FAILURE") == "1":
+        dist.barrier()
+        if rank == 1:
+            group.close()
+            res["left"] = True
+            print("RESULT " + json.dumps(res), flush=True)
+            return 0
+        group.timeout = 5.0
+        t0 = time.monotonic()
+        try:
+            D.sharded_norm(group, pb.asarray(np.ones(8, np.float32), backend=be))
+            res["failure"] = "not detected"
+        except D.RankFailure:
+            group.abort()
+            res["failure"] = "detected"
+        res["failure_seconds"] = time.monotonic() - t0
+        print("RESULT " + json.dumps(res), flush=True)
+        return 0
+    group.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    print("RESULT " + json.dumps(res), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,75 @@
+"""Sharded paths on 2 GPUs (child processes under torchrun; skipped on 1 GPU).
+
+NVLS is off (NCCL_NVLS_ENABLE=0) and the library's communicator waits are
+bounded (PB_COMM_TIMEOUT_S); the whole launch runs in its own process group
+with a hard timeout.  The departed-rank case leaves only between steps, with
+nothing in flight, and is detected on the host.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import json
+import os
+import signal
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _gpu_count() -> int:
+    from pacho_b200 import _lib
+
+    n = C.c_int(0)
+    return n.value if _lib.load().pb_device_count(C.byref(n)) == 0 else 0
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _launch(failure: bool):
+    env = {**os.environ, "NCCL_NVLS_ENABLE": "0", "PB_COMM_TIMEOUT_S": "60",
+           "PB_STORE_PORT": str(_free_port()), "PB_TEST_FAILURE": "1" if failure else "0"}
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
+           str(ROOT / "tests" / "multigpu_worker.py")]
+    proc = subprocess.Popen(cmd, env=env, cwd=ROOT, stdout=subprocess.PIPE,
+                            stderr=subprocess.STDOUT, text=True, start_new_session=True)
+    try:
+        out, _ = proc.communicate(timeout=400)
+    except subprocess.TimeoutExpired:
+        os.killpg(proc.pid, signal.SIGKILL)
+        out, _ = proc.communicate()
+        pytest.fail("2-GPU worker timed out:\n" + out[-4000:])
+    assert proc.returncode == 0, out[-4000:]
+    results = [json.loads(line.split("RESULT ", 1)[1]) for line in out.splitlines()
+               if "RESULT " in line]
+    assert len(results) == 2, out[-4000:]
+    return {r["rank"]: r for r in results}
+
+
+def test_sharded_norm_dot_rowblock_and_batch_split_on_two_gpus():
+    if _gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    results = _launch(failure=False)
+    for r in results.values():
+        checks = {k: v for k, v in r.items() if k != "rank"}
+        assert checks and all(v == 0 for v in checks.values()), r
+
+
+def test_departed_rank_is_detected_on_two_gpus():
+    if _gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    results = _launch(failure=True)
+    assert results[1].get("left") is True
+    assert results[0]["failure"] == "detected", results[0]
+    assert 4.5 <= results[0]["failure_seconds"] < 60
