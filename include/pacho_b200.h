@@ -117,8 +117,9 @@ int pb_gemm(pb_ctx* ctx, int dev, int dtype, int batch_ndim, const int64_t* batc
 
 /* pb_gemm with an explicit kernel choice: PB_GEMM_AUTO (what pb_gemm does),
  * PB_GEMM_SIMT (register-tiled CUDA-core FFMA/DFMA kernel), PB_GEMM_TF32X3
- * (float32 only) or PB_GEMM_DMMA (float64 only, FP64 tensor cores).  The reference exposes the same kind of
- * provider choice as CUDABackend(blas="custom"|"cublas")
+ * (float32 only) or PB_GEMM_DMMA (float64 only, FP64 tensor cores).  The
+ * reference exposes the same kind of provider choice as
+ * CUDABackend(blas="custom"|"cublas")
  * (src/openpacho/_cuda.py:138-141). */
 enum { PB_GEMM_AUTO = 0, PB_GEMM_SIMT = 1, PB_GEMM_TF32X3 = 2, PB_GEMM_DMMA = 3 };
 int pb_gemm_ex(pb_ctx* ctx, int dev, int dtype, int batch_ndim, const int64_t* batch_shape,
@@ -185,9 +186,10 @@ int pb_comm_abort(pb_ctx* ctx, int dev);
 int pb_broadcast(pb_ctx* ctx, int dev, void* buf, size_t bytes, int root);
 /* Full-array norm of a tensor sliced contiguously across ranks: each rank
  * passes its own slice (n local elements, possibly 0); every rank receives
- * the global norm in `out` (device, 1 element).  Local (scale, ssq) partials
- * are merged with NCCL all-reduces (max of the scale exponent and the
- * NaN/Inf class, then a sum of rescaled ssq).  No counterpart in the
+ * the global norm in `out` (device, 1 element).  Each rank's local
+ * (scale exponent, ssq, NaN/Inf class) triple is all-gathered (16 bytes per
+ * rank, one NCCL call) and merged on the device in rank order, so every rank
+ * computes the identical result.  No counterpart in the
  * reference, which is single-device (src/openpacho/_cuda.py:138-199). */
 int pb_norm_sharded(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, void* out);
 /* Sum all-reduce of `count` elements in place (used for sharded DOT). */

@@ -20,7 +20,7 @@
 
 namespace pb {
 
-int norm_pair_rescale(Device* d, void* pair, const int* global_e_cls);
+int norm_pairs_finalize(Device* d, int dtype, const void* pairs, int n, void* out);
 int norm_pair_zero(Device* d, int dtype, void* pair);
 
 namespace {
@@ -36,6 +36,7 @@ struct NcclApi {
                             cudaStream_t);
   ncclResult_t (*Broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t,
                             cudaStream_t);
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
   const char* (*GetErrorString)(ncclResult_t);
 };
 
@@ -58,6 +59,7 @@ int load_nccl() {
   PB_SYM(CommGetAsyncError, "ncclCommGetAsyncError");
   PB_SYM(AllReduce, "ncclAllReduce");
   PB_SYM(Broadcast, "ncclBroadcast");
+  PB_SYM(AllGather, "ncclAllGather");
   PB_SYM(GetErrorString, "ncclGetErrorString");
 #undef PB_SYM
   g_nccl.loaded = true;
@@ -83,15 +85,19 @@ void abort_comm(Device* d) {
   d->rank = 0;
 }
 
-// Wait until the non-blocking communicator has no operation in progress.
+// Wait until the non-blocking communicator has no operation in progress:
+// spin for the first millisecond (enqueues normally finish in microseconds),
+// then poll with short sleeps until the deadline.
 int settle(Device* d, ncclResult_t r) {
-  const double deadline = now_s() + comm_timeout_s();
+  const double start = now_s();
+  const double deadline = start + comm_timeout_s();
   while (r == ncclInProgress) {
-    if (now_s() > deadline) {
+    const double t = now_s();
+    if (t > deadline) {
       abort_comm(d);
       PB_FAIL(PB_ERR_NCCL, "NCCL operation timed out; communicator aborted");
     }
-    usleep(50);
+    if (t - start > 1e-3) usleep(20);
     g_nccl.CommGetAsyncError((ncclComm_t)d->comm, &r);
   }
   if (r != ncclSuccess) {
@@ -234,30 +240,23 @@ int pb_norm_sharded(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, v
   Device* d;
   PB_CHECK(enter(ctx, dev, &d));
   PB_CHECK(need_comm(d));
-  // Layout in a small dedicated allocation: pair (16 B) | e,cls (8 B).
+  // pairs[r] = rank r's (scale exponent, ssq, class); one all-gather, then
+  // every rank merges them in rank order (identical result everywhere).
   void* buf;
-  PB_CUDA(cudaMallocAsync(&buf, 64, d->pool, d->stream));
-  NormPair* pair = (NormPair*)buf;
-  int* ec = (int*)((char*)buf + 32);
+  const size_t bytes = (size_t)d->nranks * sizeof(NormPair);
+  PB_CUDA(cudaMallocAsync(&buf, bytes, d->pool, d->stream));
+  NormPair* pairs = (NormPair*)buf;
   int st = PB_OK;
   if (n > 0) {
     if (!x) st = (set_error("null input"), PB_ERR_INVALID);
-    else st = norm_pair_global(d, dtype, n, x, pair);
+    else st = norm_pair_global(d, dtype, n, x, pairs + d->rank);
   } else {
-    st = norm_pair_zero(d, dtype, pair);
-  }
-  if (st == PB_OK) {
-    // {e, cls} of this rank -> global max, then rescale ssq and sum it.
-    cudaError_t e = cudaMemcpyAsync(ec, &pair->e, 2 * sizeof(int), cudaMemcpyDeviceToDevice, d->stream);
-    if (e != cudaSuccess) st = (set_error("copy: %s", cudaGetErrorString(e)), PB_ERR_CUDA);
+    st = norm_pair_zero(d, dtype, pairs + d->rank);
   }
   if (st == PB_OK)
-    st = settle(d, g_nccl.AllReduce(ec, ec, 2, ncclInt32, ncclMax, (ncclComm_t)d->comm, d->stream));
-  if (st == PB_OK) st = norm_pair_rescale(d, pair, ec);
-  if (st == PB_OK)
-    st = settle(d, g_nccl.AllReduce(&pair->ssq, &pair->ssq, 1, ncclFloat64, ncclSum,
+    st = settle(d, g_nccl.AllGather(pairs + d->rank, pairs, sizeof(NormPair), ncclUint8,
                                     (ncclComm_t)d->comm, d->stream));
-  if (st == PB_OK) st = norm_pair_finalize(d, dtype, pair, out);
+  if (st == PB_OK) st = norm_pairs_finalize(d, dtype, pairs, d->nranks, out);
   cudaFreeAsync(buf, d->stream);
   return st;
 }

@@ -104,7 +104,6 @@ int tensor_map_encoder(void** fn);
 
 // Entry points implemented per translation unit, all on an entered device.
 int norm_pair_global(Device* d, int dtype, int64_t n, const void* x, void* pair_out);
-int norm_pair_finalize(Device* d, int dtype, const void* pair, void* out);
 // Stream wait bounded in time that also watches the NCCL communicator.
 int comm_stream_wait(Device* d);
 

@@ -398,12 +398,15 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-__global__ void norm_pair_rescale_kernel(NormPair* __restrict__ p, const int* __restrict__ ec) {
+// Merge `n` pairs in index order (rank order for the multi-GPU combine, so
+// every rank computes the identical result) and write the norm.
+template <typename T>
+__global__ void norm_pairs_finalize_kernel(const NormPair* __restrict__ p, int n,
+                                           T* __restrict__ out) {
   if (threadIdx.x == 0 && blockIdx.x == 0) {
-    const int eg = ec[0];
-    if (p->ssq != 0.0) p->ssq = ldexp(p->ssq, 2 * (p->e - eg));
-    p->e = eg;
-    p->cls = ec[1];
+    NormPair s = p[0];
+    for (int i = 1; i < n; ++i) merge(s, p[i]);
+    *out = finalize<T>(s);
   }
 }
 
@@ -413,11 +416,6 @@ __global__ void norm_pair_zero_kernel(NormPair* __restrict__ p, int e0) {
     p->e = e0;
     p->cls = 0;
   }
-}
-
-template <typename T>
-__global__ void norm_finalize_kernel(const NormPair* __restrict__ p, T* __restrict__ out) {
-  if (threadIdx.x == 0 && blockIdx.x == 0) *out = finalize<T>(*p);
 }
 
 struct Plan {
@@ -514,19 +512,12 @@ int norm_pair_global(Device* d, int dtype, int64_t n, const void* x, void* pair_
   PB_FAIL(PB_ERR_INVALID, "unknown dtype %d", dtype);
 }
 
-int norm_pair_finalize(Device* d, int dtype, const void* pair, void* out) {
+int norm_pairs_finalize(Device* d, int dtype, const void* pairs, int n, void* out) {
   if (dtype == PB_F32)
-    norm_finalize_kernel<float><<<1, 32, 0, d->stream>>>((const NormPair*)pair, (float*)out);
-  else if (dtype == PB_F64)
-    norm_finalize_kernel<double><<<1, 32, 0, d->stream>>>((const NormPair*)pair, (double*)out);
+    norm_pairs_finalize_kernel<float><<<1, 32, 0, d->stream>>>((const NormPair*)pairs, n, (float*)out);
   else
-    PB_FAIL(PB_ERR_INVALID, "unknown dtype %d", dtype);
-  PB_LAUNCHED(d);
-  return PB_OK;
-}
-
-int norm_pair_rescale(Device* d, void* pair, const int* global_e_cls) {
-  norm_pair_rescale_kernel<<<1, 32, 0, d->stream>>>((NormPair*)pair, global_e_cls);
+    norm_pairs_finalize_kernel<double><<<1, 32, 0, d->stream>>>((const NormPair*)pairs, n,
+                                                                (double*)out);
   PB_LAUNCHED(d);
   return PB_OK;
 }

@@ -9,7 +9,7 @@ the sharded forms of its hot path that split naturally:
   ``torch.distributed.TCPStore``); a per-step heartbeat lets ranks detect a
   departed peer on the host *before* launching a collective;
 * :func:`sharded_norm` -- global Euclidean norm of a vector sliced across ranks
-  (local (scale, ssq) pairs merged with NCCL all-reduces);
+  (local (scale, ssq) pairs all-gathered and merged in rank order);
 * :func:`sharded_dot` -- global DOT of sliced vectors (local DOT + sum);
 * :func:`rowblock_matmul` -- row blocks of A per rank, B broadcast from a root;
 * :func:`batch_matmul` -- the leading batch dimension split across ranks.
