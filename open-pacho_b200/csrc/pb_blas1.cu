@@ -16,6 +16,19 @@
 namespace pb {
 namespace {
 
+// Plan parameters (compile-time so variants can be built and measured):
+// PB_GEMV_WAVES  -- block-chunks of a split row = WAVES x resident blocks;
+// PB_GEMV_ROW_KB -- row bytes one warp streams before more warps share a row;
+// PB_GEMV_PERSIST -- whole-row grids capped at PERSIST x resident blocks.
+#ifndef PB_GEMV_WAVES
+#define PB_GEMV_WAVES 1
+#endif
+#ifndef PB_GEMV_ROW_KB
+#define PB_GEMV_ROW_KB 8
+#endif
+#ifndef PB_GEMV_PERSIST
+#define PB_GEMV_PERSIST 1
+#endif
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kUnroll = 4;
@@ -59,40 +72,47 @@ __device__ __forceinline__ T warp_sum(T v) {
 
 // Sum of A[row, k0:k1] * x[k0:k1] by the `nthr` threads of one row group.
 // STREAM_X: x is itself streamed once (DOT) instead of reused (GEMV).
+// Offsets inside the chunk are 32-bit (chunks are < 2^31 elements) and the
+// pointers advance incrementally, which keeps the loop at few registers.
 template <typename T, bool ALIGNED, bool STREAM_X>
 __device__ __forceinline__ T row_partial(const T* __restrict__ a, const T* __restrict__ x,
                                          int64_t k0, int64_t k1, int tid, int nthr) {
   using V = typename V16<T>::type;
   constexpr int VN = V16<T>::n;
-  T acc[kUnroll];
-#pragma unroll
-  for (int u = 0; u < kUnroll; ++u) acc[u] = T(0);
-  int64_t body_end = k0;
+  T acc0 = T(0), acc1 = T(0), acc2 = T(0), acc3 = T(0);
+  a += k0;
+  x += k0;
+  const int len = (int)(k1 - k0);
+  int body = 0;
   if (ALIGNED) {
     // k0 is a multiple of VN and the row start is 16-byte aligned.
-    const int64_t nv = (k1 - k0) / VN;
-    const V* av = reinterpret_cast<const V*>(a + k0);
-    const V* xv = reinterpret_cast<const V*>(x + k0);
-    int64_t v = tid;
-    for (; v + (kUnroll - 1) * (int64_t)nthr < nv; v += kUnroll * (int64_t)nthr) {
-      V ra[kUnroll], rx[kUnroll];
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        ra[u] = ld_stream(av + v + u * nthr);
-        rx[u] = STREAM_X ? ld_stream(xv + v + u * nthr) : __ldg(xv + v + u * nthr);
+    const int nv = len / VN;
+    const V* av = reinterpret_cast<const V*>(a) + tid;
+    const V* xv = reinterpret_cast<const V*>(x) + tid;
+    int v = tid;
+#pragma unroll 1
+    for (; v + 3 * nthr < nv; v += 4 * nthr, av += 4 * nthr, xv += 4 * nthr) {
+      const V r0 = ld_stream(av), r1 = ld_stream(av + nthr), r2 = ld_stream(av + 2 * nthr),
+              r3 = ld_stream(av + 3 * nthr);
+      V x0, x1, x2, x3;
+      if (STREAM_X) {
+        x0 = ld_stream(xv); x1 = ld_stream(xv + nthr); x2 = ld_stream(xv + 2 * nthr);
+        x3 = ld_stream(xv + 3 * nthr);
+      } else {
+        x0 = __ldg(xv); x1 = __ldg(xv + nthr); x2 = __ldg(xv + 2 * nthr); x3 = __ldg(xv + 3 * nthr);
       }
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) acc[u] = dotv(ra[u], rx[u], acc[u]);
+      acc0 = dotv(r0, x0, acc0);
+      acc1 = dotv(r1, x1, acc1);
+      acc2 = dotv(r2, x2, acc2);
+      acc3 = dotv(r3, x3, acc3);
     }
-    for (; v < nv; v += nthr) {
-      V ra = ld_stream(av + v);
-      V rx = STREAM_X ? ld_stream(xv + v) : __ldg(xv + v);
-      acc[0] = dotv(ra, rx, acc[0]);
-    }
-    body_end = k0 + nv * VN;
+#pragma unroll 1
+    for (; v < nv; v += nthr, av += nthr, xv += nthr)
+      acc0 = dotv(ld_stream(av), STREAM_X ? ld_stream(xv) : __ldg(xv), acc0);
+    body = nv * VN;
   }
-  for (int64_t k = body_end + tid; k < k1; k += nthr) acc[1] = fma(__ldg(a + k), __ldg(x + k), acc[1]);
-  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  for (int k = body + tid; k < len; k += nthr) acc1 = fma(__ldg(a + k), __ldg(x + k), acc1);
+  return (acc0 + acc1) + (acc2 + acc3);
 }
 
 // Block = kWarps warps; G = kWarps / rows_per_block warps per row.  Block b
@@ -157,6 +177,67 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// Whole rows (no split): G = kWarps / rows_per_block warps per row; blocks
+// stride over row groups, so with the grid capped at the resident block count
+// the imbalance at the end is one group in many instead of a partial last
+// wave.  In-row offsets are 32-bit (the launcher guarantees K < 2^31).
+template <typename T, bool ALIGNED>
+__global__ void __launch_bounds__(kThreads, 4)
+    gemv_rows_kernel(const T* __restrict__ A, const T* __restrict__ x, T* __restrict__ y,
+                     int64_t rows, int K, int rows_per_block) {
+  using V = typename V16<T>::type;
+  constexpr int VN = V16<T>::n;
+  __shared__ T red[kWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = kWarps / rows_per_block;
+  const int sub = warp / G;
+  const int tid = (warp % G) * 32 + lane;
+  const int nthr = G * 32;
+  const int64_t groups = (rows + rows_per_block - 1) / rows_per_block;
+#pragma unroll 1
+  for (int64_t group = blockIdx.x; group < groups; group += gridDim.x) {
+    const int64_t row = group * rows_per_block + sub;
+    T acc0 = T(0), acc1 = T(0), acc2 = T(0), acc3 = T(0);
+    if (row < rows) {
+      const T* a = A + row * (int64_t)K;
+      int body = 0;
+      if (ALIGNED) {
+        const int nv = K / VN;
+        const V* av = reinterpret_cast<const V*>(a) + tid;
+        const V* xv = reinterpret_cast<const V*>(x) + tid;
+        int v = tid;
+#pragma unroll 1
+        for (; v + 3 * nthr < nv; v += 4 * nthr, av += 4 * nthr, xv += 4 * nthr) {
+          const V r0 = ld_stream(av), r1 = ld_stream(av + nthr), r2 = ld_stream(av + 2 * nthr),
+                  r3 = ld_stream(av + 3 * nthr);
+          const V x0 = __ldg(xv), x1 = __ldg(xv + nthr), x2 = __ldg(xv + 2 * nthr),
+                  x3 = __ldg(xv + 3 * nthr);
+          acc0 = dotv(r0, x0, acc0);
+          acc1 = dotv(r1, x1, acc1);
+          acc2 = dotv(r2, x2, acc2);
+          acc3 = dotv(r3, x3, acc3);
+        }
+#pragma unroll 1
+        for (; v < nv; v += nthr, av += nthr, xv += nthr) acc0 = dotv(ld_stream(av), __ldg(xv), acc0);
+        body = nv * VN;
+      }
+      for (int k = body + tid; k < K; k += nthr) acc1 = fma(__ldg(a + k), __ldg(x + k), acc1);
+    }
+    const T v = warp_sum((acc0 + acc1) + (acc2 + acc3));
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (threadIdx.x < rows_per_block) {
+      const int64_t r = group * rows_per_block + threadIdx.x;
+      if (r < rows) {
+        T s = T(0);
+        for (int w = 0; w < G; ++w) s += red[threadIdx.x * G + w];
+        y[r] = s;
+      }
+    }
+    __syncthreads();
+  }
+}
+
 template <typename T>
 __global__ void fill_kernel(T* __restrict__ out, size_t n, T value) {
   size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -180,11 +261,13 @@ GemvPlan plan_gemv(int64_t rows, int64_t K, int64_t elem, int sm_count) {
     p.nchunks = 1;
     p.chunk = K;
     const int64_t bytes = K * elem;
-    int G = bytes > (128 << 10) ? 8 : bytes > (64 << 10) ? 4 : bytes > (32 << 10) ? 2 : 1;
+    constexpr int64_t R = (int64_t)PB_GEMV_ROW_KB << 10;
+    int G = bytes > 4 * R ? 8 : bytes > 2 * R ? 4 : bytes > R ? 2 : 1;
     p.rows_per_block = kWarps / G;
   } else {
     p.rows_per_block = 1;
-    int64_t want = ceil_div(2 * resident, rows);
+    // Equal block-chunks, PB_GEMV_WAVES waves of resident blocks.
+    int64_t want = ceil_div(PB_GEMV_WAVES * resident, rows);
     int64_t most = ceil_div(K, 2048);
     int64_t n = want < most ? want : most;
     if (n < 1) n = 1;
@@ -193,6 +276,12 @@ GemvPlan plan_gemv(int64_t rows, int64_t K, int64_t elem, int sm_count) {
   }
   p.blocks = ceil_div(rows, p.rows_per_block) * p.nchunks;
   return p;
+}
+
+// Grid of the whole-row kernel: persistent (capped at PB_GEMV_PERSIST waves).
+int64_t rows_grid(const GemvPlan& p, int sm_count) {
+  const int64_t cap = (int64_t)PB_GEMV_PERSIST * sm_count * (2048 / kThreads);
+  return p.blocks < cap ? p.blocks : cap;
 }
 
 template <typename T, bool STREAM_X>
@@ -210,6 +299,17 @@ int launch_gemv(Device* d, const T* A, const T* x, T* y, int64_t rows, int64_t K
   constexpr int VN = V16<T>::n;
   bool aligned = ((uintptr_t)A % 16 == 0) && ((uintptr_t)x % 16 == 0) &&
                  (rows == 1 || lda % VN == 0) && (p.chunk % VN == 0);
+  if (p.nchunks == 1 && !STREAM_X && lda == K && K < INT32_MAX) {
+    const unsigned grid = (unsigned)rows_grid(p, d->sm_count);
+    if (aligned)
+      gemv_rows_kernel<T, true><<<grid, kThreads, 0, d->stream>>>(A, x, y, rows, (int)K,
+                                                                   p.rows_per_block);
+    else
+      gemv_rows_kernel<T, false><<<grid, kThreads, 0, d->stream>>>(A, x, y, rows, (int)K,
+                                                                    p.rows_per_block);
+    PB_LAUNCHED(d);
+    return PB_OK;
+  }
   if (aligned)
     gemv_kernel<T, true, STREAM_X><<<(unsigned)p.blocks, kThreads, 0, d->stream>>>(
         A, x, y, rows, K, lda, p.rows_per_block, p.chunk, p.nchunks, partial, cnt);

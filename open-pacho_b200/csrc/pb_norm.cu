@@ -163,28 +163,35 @@ __device__ __forceinline__ double2 ld_stream(const double2* p) {
   return v;
 }
 
-// Partial pair of x[k0:k1] for one row group of `nthr` threads.
+// Partial pair of x[k0:k1] for one row group of `nthr` threads.  Offsets
+// inside the chunk are 32-bit (chunks are < 2^31 elements) and pointers
+// advance incrementally, keeping the streaming loop at few registers.
 template <bool ALIGNED>
 __device__ NormPair row_pair(const float* __restrict__ x, int64_t k0, int64_t k1, int tid,
                              int nthr) {
   AccF32 acc;
   acc.init();
-  int64_t body_end = k0;
+  x += k0;
+  const int len = (int)(k1 - k0);
+  int body = 0;
   if (ALIGNED) {
-    const int64_t nv = (k1 - k0) / 4;
-    const float4* xv = reinterpret_cast<const float4*>(x + k0);
-    int64_t v = tid;
-    for (; v + 3 * (int64_t)nthr < nv; v += 4 * (int64_t)nthr) {
-      float4 r[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) r[u] = ld_stream(xv + v + u * nthr);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) acc.add4(r[u], u);
+    const int nv = len / 4;
+    const float4* xv = reinterpret_cast<const float4*>(x) + tid;
+    int v = tid;
+#pragma unroll 1
+    for (; v + 3 * nthr < nv; v += 4 * nthr, xv += 4 * nthr) {
+      const float4 r0 = ld_stream(xv), r1 = ld_stream(xv + nthr), r2 = ld_stream(xv + 2 * nthr),
+                   r3 = ld_stream(xv + 3 * nthr);
+      acc.add4(r0, 0);
+      acc.add4(r1, 1);
+      acc.add4(r2, 2);
+      acc.add4(r3, 3);
     }
-    for (; v < nv; v += nthr) acc.add4(ld_stream(xv + v), 0);
-    body_end = k0 + nv * 4;
+#pragma unroll 1
+    for (; v < nv; v += nthr, xv += nthr) acc.add4(ld_stream(xv), 0);
+    body = nv * 4;
   }
-  for (int64_t k = body_end + tid; k < k1; k += nthr) acc.add1(__ldg(x + k));
+  for (int k = body + tid; k < len; k += nthr) acc.add1(__ldg(x + k));
   return acc.pair();
 }
 
@@ -193,29 +200,29 @@ __device__ NormPair row_pair(const double* __restrict__ x, int64_t k0, int64_t k
                              int nthr) {
   AccF64 acc;
   acc.init();
-  int64_t body_end = k0;
+  x += k0;
+  const int len = (int)(k1 - k0);
+  int body = 0;
   if (ALIGNED) {
-    const int64_t nv = (k1 - k0) / 2;
-    const double2* xv = reinterpret_cast<const double2*>(x + k0);
-    int64_t v = tid;
-    for (; v + 3 * (int64_t)nthr < nv; v += 4 * (int64_t)nthr) {
-      double r[8];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        double2 t = ld_stream(xv + v + u * nthr);
-        r[2 * u] = t.x;
-        r[2 * u + 1] = t.y;
-      }
+    const int nv = len / 2;
+    const double2* xv = reinterpret_cast<const double2*>(x) + tid;
+    int v = tid;
+#pragma unroll 1
+    for (; v + 3 * nthr < nv; v += 4 * nthr, xv += 4 * nthr) {
+      const double2 t0 = ld_stream(xv), t1 = ld_stream(xv + nthr), t2 = ld_stream(xv + 2 * nthr),
+                    t3 = ld_stream(xv + 3 * nthr);
+      double r[8] = {t0.x, t0.y, t1.x, t1.y, t2.x, t2.y, t3.x, t3.y};
       acc.batch<8>(r);
     }
-    for (; v < nv; v += nthr) {
-      double2 t = ld_stream(xv + v);
+#pragma unroll 1
+    for (; v < nv; v += nthr, xv += nthr) {
+      const double2 t = ld_stream(xv);
       double r[2] = {t.x, t.y};
       acc.batch<2>(r);
     }
-    body_end = k0 + nv * 2;
+    body = nv * 2;
   }
-  for (int64_t k = body_end + tid; k < k1; k += nthr) acc.add1(__ldg(x + k));
+  for (int k = body + tid; k < len; k += nthr) acc.add1(__ldg(x + k));
   return acc.pair();
 }
 
@@ -438,7 +445,7 @@ Plan plan_rows(int64_t rows, int64_t K, int64_t elem, int sm_count) {
     p.rows_per_block = kWarps / G;
   } else {
     p.rows_per_block = 1;
-    int64_t want = ceil_div(2 * resident, rows);
+    int64_t want = ceil_div(resident, rows);  // one wave of equal block-chunks
     int64_t most = ceil_div(K, 2048);
     int64_t n = want < most ? want : most;
     if (n < 1) n = 1;
