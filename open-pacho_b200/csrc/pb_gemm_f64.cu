@@ -70,33 +70,33 @@ __global__ void __launch_bounds__(NT, 1) dmma_gemm_kernel(DmmaParams p) {
     const double* B = p.B + bo * K * N;
     double* C = p.C + bz * M * N;
 
-    // Stage loader: A 128 rows x 16 k (thread: row tid/2, k (tid&1)*8 .. +8),
-    // B 16 k x 128 n stored [n][k] (thread: k tid/16, n (tid&15)*8 .. +8).
+    // Stage loader.  Each warp instruction copies two smem rows of 16 doubles
+    // (lanes 0-15 one row, 16-31 the next), so its 32 eight-byte writes land in
+    // two wavefronts (160-byte pitch: the second row is shifted by 8 banks).
+    // A: rows are K-contiguous in global memory too (two 128-byte reads).
+    // B: stored transposed [n][k]; half-warp lanes read one column down 16
+    //    rows of B (sectors shared by neighbouring columns stay in L1).
     auto load = [&](int64_t kt, int stage) {
       double* sa = smem + stage * STAGE_DOUBLES;
       double* sb = sa + TM * PITCH;
       const int64_t k0 = kt * TK;
-      {
-        const int r = tid >> 1, kc = (tid & 1) * 8;
+      const int kk = lane & 15;
+      const int64_t gk = k0 + kk;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int r = warp * 16 + 2 * i + (lane >> 4);
         const int64_t gr = m0 + r;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int64_t gk = k0 + kc + j;
-          const bool ok = gr < M && gk < K;
-          cp_async8(smem_u32(sa + r * PITCH + kc + j), ok ? (const void*)(A + gr * K + gk) : (const void*)A,
-                    ok ? 8 : 0);
-        }
+        const bool ok = gr < M && gk < K;
+        cp_async8(smem_u32(sa + r * PITCH + kk), ok ? (const void*)(A + gr * K + gk) : (const void*)A,
+                  ok ? 8 : 0);
       }
-      {
-        const int kk = tid >> 4, nc = (tid & 15) * 8;
-        const int64_t gk = k0 + kk;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int64_t gn = n0 + nc + j;
-          const bool ok = gk < K && gn < N;
-          cp_async8(smem_u32(sb + (nc + j) * PITCH + kk), ok ? (const void*)(B + gk * N + gn) : (const void*)B,
-                    ok ? 8 : 0);
-        }
+      for (int i = 0; i < 8; ++i) {
+        const int n = warp * 16 + 2 * i + (lane >> 4);
+        const int64_t gn = n0 + n;
+        const bool ok = gk < K && gn < N;
+        cp_async8(smem_u32(sb + n * PITCH + kk), ok ? (const void*)(B + gk * N + gn) : (const void*)B,
+                  ok ? 8 : 0);
       }
     };
 

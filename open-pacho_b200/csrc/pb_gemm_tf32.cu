@@ -243,13 +243,21 @@ constexpr int GEMM_THREADS = 32 * (2 + ACC_WARPS);
 
 struct Tf32Params {
   float* C;
+  float* partial;  // ksplit > 1: per-split fp32 tiles, [ksplit][batch][M][N]
   int64_t M, N;
   int kblocks;  // K' / 32
   int tiles_m, tiles_n;
   int64_t tiles;  // tiles_m * tiles_n * batch
+  int ksplit;     // K-slice ranges per tile (work items = tiles * ksplit)
   BatchMap map;
   int* err;
 };
+
+// K-slice range [kb0, kb1) of split `s`.
+__device__ __forceinline__ void split_range(const Tf32Params& p, int s, int& kb0, int& kb1) {
+  kb0 = (int)((int64_t)s * p.kblocks / p.ksplit);
+  kb1 = (int)((int64_t)(s + 1) * p.kblocks / p.ksplit);
+}
 
 template <int BN>
 struct Smem {
@@ -327,20 +335,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
-  const int nk = p.kblocks;
-  const int nchunks = (nk + CHUNK - 1) / CHUNK;
+  const int64_t items = p.tiles * p.ksplit;
 
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------ TMA producer
       int64_t g = 0;  // k-slices issued by this CTA (ring position)
-      for (int64_t t = blockIdx.x; t < p.tiles && !*abort_flag; t += gridDim.x) {
-        const TileCoord tc = tile_coord(p, t);
+      for (int64_t w = blockIdx.x; w < items && !*abort_flag; w += gridDim.x) {
+        const TileCoord tc = tile_coord(p, w / p.ksplit);
+        int kb0, kb1;
+        split_range(p, (int)(w % p.ksplit), kb0, kb1);
         int64_t ao, bo;
         batch_offsets(p.map, tc.bz, &ao, &bo);
         const int32_t a_row = (int32_t)(ao * p.M + tc.m_tile * BM);
         const int32_t b_row = (int32_t)(bo * p.N + tc.n_tile * BN);
-        for (int kb = 0; kb < nk; ++kb, ++g) {
+        for (int kb = kb0; kb < kb1; ++kb, ++g) {
           const int s = (int)(g % STAGES);
           if (!mbar_wait(empty0 + 8 * s, (uint32_t)(((g / STAGES) & 1) ^ 1), abort_flag, p.err))
             break;
@@ -366,15 +375,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const uint32_t idesc = instr_desc(BN);
       int64_t g = 0, gc = 0;  // k-slices consumed / chunks produced by this CTA
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+      for (int64_t w = blockIdx.x; w < items && ok; w += gridDim.x) {
+        int kb0, kb1;
+        split_range(p, (int)(w % p.ksplit), kb0, kb1);
+        const int nchunks = (kb1 - kb0 + CHUNK - 1) / CHUNK;
         for (int c = 0; c < nchunks && ok; ++c, ++gc) {
           const int buf = (int)(gc & 1);
           ok = mbar_wait(acce0 + 8 * buf, (uint32_t)(((gc >> 1) & 1) ^ 1), abort_flag, p.err);
           if (!ok) break;
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t d = tmem + (uint32_t)(buf * BN);
-          const int kb_end = min(nk, (c + 1) * CHUNK);
-          for (int kb = c * CHUNK; kb < kb_end; ++kb, ++g) {
+          const int kb_start = kb0 + c * CHUNK;
+          const int kb_end = min(kb1, kb_start + CHUNK);
+          for (int kb = kb_start; kb < kb_end; ++kb, ++g) {
             const int s = (int)(g % STAGES);
             ok = mbar_wait(full0 + 8 * s, (uint32_t)((g / STAGES) & 1), abort_flag, p.err);
             if (!ok) break;
@@ -383,7 +396,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const uint64_t da = smem_desc(sa), db = smem_desc(sa + Smem<BN>::A_BYTES);
 #pragma unroll
             for (int k = 0; k < BK / 8; ++k)  // +32 bytes per 8-element K step
-              umma_tf32(d, da + 2 * k, db + 2 * k, idesc, (kb > c * CHUNK || k > 0) ? 1u : 0u);
+              umma_tf32(d, da + 2 * k, db + 2 * k, idesc, (kb > kb_start || k > 0) ? 1u : 0u);
             umma_commit(empty0 + 8 * s);
           }
           umma_commit(accf0 + 8 * buf);  // chunk complete -> accumulator warps
@@ -397,8 +410,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int half = (warp - 2) >> 2;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * COLS);
     int64_t gc = 0;
-    for (int64_t t = blockIdx.x; t < p.tiles; t += gridDim.x) {
-      const TileCoord tc = tile_coord(p, t);
+    for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
+      const TileCoord tc = tile_coord(p, w / p.ksplit);
+      const int split = (int)(w % p.ksplit);
+      int kb0, kb1;
+      split_range(p, split, kb0, kb1);
+      const int nchunks = (kb1 - kb0 + CHUNK - 1) / CHUNK;
       float acc[COLS];
 #pragma unroll
       for (int i = 0; i < COLS; ++i) acc[i] = 0.0f;
@@ -438,11 +455,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (lane == 0) mbar_arrive(acce0 + 8 * buf);
       }
       if (!ok || *abort_flag) break;
-      // Store this thread's row segment of the finished tile.
+      // Store this thread's row segment of the finished tile (or of this
+      // split's partial tile, summed later by splitk_reduce_kernel).
       const int64_t row = tc.m_tile * BM + quad * 32 + lane;
       if (row < p.M) {
         const int64_t col0 = tc.n_tile * BN + half * COLS;
-        float* crow = p.C + tc.bz * p.M * p.N + row * p.N + col0;
+        const int64_t batch = p.tiles / ((int64_t)p.tiles_m * p.tiles_n);
+        float* dst_base = p.ksplit == 1 ? p.C : p.partial + split * batch * p.M * p.N;
+        float* crow = dst_base + tc.bz * p.M * p.N + row * p.N + col0;
         if ((p.N % 4) == 0 && col0 + COLS <= p.N) {
           float4* dst = reinterpret_cast<float4*>(crow);
 #pragma unroll
@@ -474,6 +494,34 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
 }
 
+// C = sum over splits of the partial tiles, in split order (deterministic).
+__global__ void splitk_reduce_kernel(const float* __restrict__ partial, float* __restrict__ C,
+                                     int64_t count, int ksplit) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if ((count & 3) == 0) {
+    const int64_t n4 = count / 4;
+    const float4* p4 = reinterpret_cast<const float4*>(partial);
+    float4* c4 = reinterpret_cast<float4*>(C);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+      float4 s = p4[i];
+      for (int k = 1; k < ksplit; ++k) {
+        const float4 v = p4[k * n4 + i];
+        s.x += v.x;
+        s.y += v.y;
+        s.z += v.z;
+        s.w += v.w;
+      }
+      c4[i] = s;
+    }
+  } else {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += stride) {
+      float s = partial[i];
+      for (int k = 1; k < ksplit; ++k) s += partial[k * count + i];
+      C[i] = s;
+    }
+  }
+}
+
 int encode_kmajor(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols, int box_rows) {
   void* fn;
   PB_CHECK(tensor_map_encoder(&fn));
@@ -498,8 +546,9 @@ int launch_tf32(Device* d, const CUtensorMap& ma, const CUtensorMap& mb, const T
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured = true;
   }
-  // Persistent: one CTA per SM (shared memory allows no more), tiles strided.
-  const int64_t grid = p.tiles < d->sm_count ? p.tiles : d->sm_count;
+  // Persistent: one CTA per SM (shared memory allows no more), work items strided.
+  const int64_t items = p.tiles * p.ksplit;
+  const int64_t grid = items < d->sm_count ? items : d->sm_count;
   tf32x3_gemm_kernel<BN><<<(unsigned)grid, GEMM_THREADS, smem, d->stream>>>(ma, mb, p);
   PB_LAUNCHED(d);
   return PB_OK;
@@ -528,8 +577,25 @@ int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
     PB_FAIL(PB_ERR_UNSUPPORTED, "GEMM operand too large for 32-bit TMA coordinates");
   const size_t bytes_a = (size_t)rows_a * K3 * sizeof(float);
   const size_t bytes_b = (size_t)rows_b * K3 * sizeof(float);
+  // Tile width: 256 unless 128-wide tiles pad N less (config 3: N = 384).
+  const int64_t waste256 = ceil_div(N, (int64_t)256) * 256 - N;
+  const int64_t waste128 = ceil_div(N, (int64_t)128) * 128 - N;
+  const int BN = (N > 128 && waste256 <= waste128) ? 256 : 128;
+  const int tiles_m = (int)ceil_div(M, (int64_t)BM);
+  const int64_t tiles = (int64_t)tiles_m * ceil_div(N, (int64_t)BN) * batch;
+  const int kblocks = (int)(K3 / BK);
+  // Too few tiles to occupy every SM: split K' into ranges of at least two
+  // promotion chunks each, fp32 partial tiles summed by a second kernel.
+  int ksplit = 1;
+  if (tiles < d->sm_count) {
+    ksplit = (int)(d->sm_count / tiles);
+    const int most = kblocks / (2 * CHUNK);
+    if (ksplit > most) ksplit = most;
+    if (ksplit < 1) ksplit = 1;
+  }
+  const size_t bytes_p = ksplit > 1 ? (size_t)ksplit * batch * M * N * sizeof(float) : 0;
   void* ws;
-  PB_CHECK(scratch(d, bytes_a + bytes_b, &ws));
+  PB_CHECK(scratch(d, bytes_a + bytes_b + bytes_p, &ws));
   float* Ap = (float*)ws;
   float* Bt = (float*)((char*)ws + bytes_a);
 
@@ -548,24 +614,31 @@ int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
     PB_LAUNCHED(d);
   }
 
-  const int tiles_m = (int)ceil_div(M, (int64_t)BM);
-  const bool wide = ceil_div(N, (int64_t)256) * tiles_m * batch >= d->sm_count && N > 128;
-  const int BN = wide ? 256 : 128;
   CUtensorMap ma, mb;
   PB_CHECK(encode_kmajor(&ma, Ap, rows_a, K3, BM));
   PB_CHECK(encode_kmajor(&mb, Bt, rows_b, K3, BN));
   Tf32Params p;
   p.C = C;
+  p.partial = ksplit > 1 ? (float*)((char*)ws + bytes_a + bytes_b) : nullptr;
   p.M = M;
   p.N = N;
-  p.kblocks = (int)(K3 / BK);
+  p.kblocks = kblocks;
   p.tiles_m = tiles_m;
   p.tiles_n = (int)ceil_div(N, (int64_t)BN);
-  p.tiles = (int64_t)p.tiles_m * p.tiles_n * batch;
+  p.tiles = tiles;
+  p.ksplit = ksplit;
   p.map = map;
   p.err = d->err_dev;
-  if (BN == 256) return launch_tf32<256>(d, ma, mb, p);
-  return launch_tf32<128>(d, ma, mb, p);
+  PB_CHECK(BN == 256 ? launch_tf32<256>(d, ma, mb, p) : launch_tf32<128>(d, ma, mb, p));
+  if (ksplit > 1) {
+    const int64_t count = batch * M * N;
+    int64_t blocks = ceil_div(count / 4 + 1, (int64_t)256);
+    const int64_t cap = (int64_t)d->sm_count * 8;
+    if (blocks > cap) blocks = cap;
+    splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, d->stream>>>(p.partial, C, count, ksplit);
+    PB_LAUNCHED(d);
+  }
+  return PB_OK;
 }
 
 }  // namespace pb
