@@ -216,11 +216,18 @@ class Gpu:
     def check(self, status, what):
         self.lib.check(status, what)
 
-    def busy(self, fn, seconds=0.5):
-        """Untimed steps for `seconds` of wall time, so the clock sampler sees
-        the GPU under this workload's load before the timed region."""
+    def busy(self, fn, dist, seconds=0.5):
+        """Untimed steps for about `seconds`, so the clock sampler sees the GPU
+        under this workload's load before the timed region.  The step count is
+        calibrated per rank and agreed (max) across ranks: steps may contain
+        collectives, so every rank must run exactly the same number."""
         t0 = time.perf_counter()
-        while time.perf_counter() - t0 < seconds:
+        for _ in range(8):
+            fn()
+        self.check(self.raw.pb_sync(self.ctx, 0), "sync")
+        per8 = max(time.perf_counter() - t0, 1e-6)
+        rounds = int(dist.max(float(min(max(1, int(seconds / per8)), 4096))))
+        for _ in range(rounds):
             for _ in range(8):
                 fn()
             self.check(self.raw.pb_sync(self.ctx, 0), "sync")
@@ -267,7 +274,7 @@ def run_gemv_dot(gpu: Gpu, args, dist: Dist, result: dict):
         step()
     dist.barrier()
     with Clocks(gpu.backend.ordinal) as clocks:
-        gpu.busy(step)
+        gpu.busy(step, dist)
         l0 = gpu.launches()
         seconds = gpu.timer(step, args.steps)
     launches = gpu.launches() - l0
@@ -368,7 +375,7 @@ def run_gemm(gpu: Gpu, args, dist: Dist, result: dict, which: str):
         step()
     dist.barrier()
     with Clocks(gpu.backend.ordinal) as clocks:
-        gpu.busy(step)
+        gpu.busy(step, dist)
         l0 = gpu.launches()
         seconds = gpu.timer(step, args.steps)
     launches = gpu.launches() - l0
@@ -409,7 +416,7 @@ def run_batched(gpu: Gpu, args, dist: Dist, result: dict):
         step()
     dist.barrier()
     with Clocks(gpu.backend.ordinal) as clocks:
-        gpu.busy(step)
+        gpu.busy(step, dist)
         l0 = gpu.launches()
         seconds = gpu.timer(step, args.steps)
     launches = gpu.launches() - l0
@@ -464,7 +471,7 @@ def run_norm(gpu: Gpu, args, dist: Dist, result: dict, rows: bool):
         step()
     dist.barrier()
     with Clocks(gpu.backend.ordinal) as clocks:
-        gpu.busy(step)
+        gpu.busy(step, dist)
         l0 = gpu.launches()
         seconds = gpu.timer(step, args.steps)
     launches = gpu.launches() - l0

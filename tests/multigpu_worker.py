@@ -6,7 +6,7 @@ the sharded DOT, row-block GEMM with B broadcast from rank 0, and the batch
 split of a broadcast-batched GEMM.  With PB_TEST_FAILURE=1 it then has rank 1
 leave between steps (nothing in flight) and checks that rank 0 detects it on
 the host before launching its next collective and aborts its communicator.
-Prints one ``RESULT {json}`` line per rank.
+Each rank writes its results as JSON to ``$PB_RESULT_DIR/rank<r>.json``.
 """
 
 from __future__ import annotations
@@ -29,6 +29,7 @@ def main() -> int:
     import torch.distributed as dist
 
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    out_path = Path(os.environ["PB_RESULT_DIR"]) / f"rank{rank}.json"
     local = int(os.environ.get("LOCAL_RANK", rank))
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
     store = dist.TCPStore(os.environ["MASTER_ADDR"], int(os.environ["PB_STORE_PORT"]), world,
@@ -84,7 +85,7 @@ def main() -> int:
         if rank == 1:
             group.close()
             res["left"] = True
-            print("RESULT " + json.dumps(res), flush=True)
+            out_path.write_text(json.dumps(res))
             return 0
         group.timeout = 5.0
         t0 = time.monotonic()
@@ -95,12 +96,12 @@ def main() -> int:
             group.abort()
             res["failure"] = "detected"
         res["failure_seconds"] = time.monotonic() - t0
-        print("RESULT " + json.dumps(res), flush=True)
+        out_path.write_text(json.dumps(res))
         return 0
     group.close()
     dist.barrier()
     dist.destroy_process_group()
-    print("RESULT " + json.dumps(res), flush=True)
+    out_path.write_text(json.dumps(res))
     return 0
 
 

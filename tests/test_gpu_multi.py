@@ -36,9 +36,10 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _launch(failure: bool):
+def _launch(failure: bool, tmp_path):
     env = {**os.environ, "NCCL_NVLS_ENABLE": "0", "PB_COMM_TIMEOUT_S": "60",
-           "PB_STORE_PORT": str(_free_port()), "PB_TEST_FAILURE": "1" if failure else "0"}
+           "PB_STORE_PORT": str(_free_port()), "PB_TEST_FAILURE": "1" if failure else "0",
+           "PB_RESULT_DIR": str(tmp_path)}
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
            "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            str(ROOT / "tests" / "multigpu_worker.py")]
@@ -51,25 +52,25 @@ def _launch(failure: bool):
         out, _ = proc.communicate()
         pytest.fail("2-GPU worker timed out:\n" + out[-4000:])
     assert proc.returncode == 0, out[-4000:]
-    results = [json.loads(line.split("RESULT ", 1)[1]) for line in out.splitlines()
-               if "RESULT " in line]
-    assert len(results) == 2, out[-4000:]
+    files = sorted(tmp_path.glob("rank*.json"))
+    assert len(files) == 2, out[-4000:]
+    results = [json.loads(f.read_text()) for f in files]
     return {r["rank"]: r for r in results}
 
 
-def test_sharded_norm_dot_rowblock_and_batch_split_on_two_gpus():
+def test_sharded_norm_dot_rowblock_and_batch_split_on_two_gpus(tmp_path):
     if _gpu_count() < 2:
         pytest.skip("needs 2 GPUs")
-    results = _launch(failure=False)
+    results = _launch(failure=False, tmp_path=tmp_path)
     for r in results.values():
         checks = {k: v for k, v in r.items() if k != "rank"}
         assert checks and all(v == 0 for v in checks.values()), r
 
 
-def test_departed_rank_is_detected_on_two_gpus():
+def test_departed_rank_is_detected_on_two_gpus(tmp_path):
     if _gpu_count() < 2:
         pytest.skip("needs 2 GPUs")
-    results = _launch(failure=True)
+    results = _launch(failure=True, tmp_path=tmp_path)
     assert results[1].get("left") is True
     assert results[0]["failure"] == "detected", results[0]
     assert 4.5 <= results[0]["failure_seconds"] < 60
