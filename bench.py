@@ -98,7 +98,9 @@ class Dist:
 
             import torch.distributed as dist
 
-            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=180))
+            # Bound the library's own collective waits too (default 300 s).
+            os.environ.setdefault("PB_COMM_TIMEOUT_S", "60")
             self.dist = dist
             self.pg = True
 
