@@ -13,7 +13,7 @@ import os
 import threading
 from pathlib import Path
 
-from .exceptions import BackendUnavailableError, UnsupportedDtypeError
+from . import exceptions as _exc
 
 PB_OK = 0
 PB_ERR_INVALID = 1
@@ -105,14 +105,14 @@ def load():
             return _lib
         path = library_path()
         if not path.exists():
-            raise BackendUnavailableError(
+            raise _exc.BackendUnavailableError(
                 f"{LIBRARY_NAME} not found at {path}; build it with "
                 "`python -m pacho_b200._build` (nvcc, sm_100a)"
             )
         try:
             lib = C.CDLL(str(path))
         except OSError as exc:
-            raise BackendUnavailableError(f"cannot load {path}: {exc}") from exc
+            raise _exc.BackendUnavailableError(f"cannot load {path}: {exc}") from exc
         lib.pb_last_error.restype = C.c_char_p
         lib.pb_last_error.argtypes = []
         for name, args in PROTOTYPES.items():
@@ -134,7 +134,7 @@ def check(status: int, what: str = "b200 call") -> None:
         return
     message = f"{what} failed: {last_error()}"
     if status == PB_ERR_UNAVAILABLE:
-        raise BackendUnavailableError(message)
+        raise _exc.BackendUnavailableError(message)
     if status == PB_ERR_INVALID:
         raise ValueError(message)
     if status == PB_ERR_UNSUPPORTED:
@@ -152,7 +152,7 @@ def dtype_code(dtype) -> int:
         return PB_F32
     if dtype == np.float64:
         return PB_F64
-    raise UnsupportedDtypeError(f"b200 backend supports float32 and float64, not {dtype}")
+    raise _exc.UnsupportedDtypeError(f"b200 backend supports float32 and float64, not {dtype}")
 
 
 def i64_array(values):

@@ -29,7 +29,7 @@ import numpy as np
 from numpy.lib.mixins import NDArrayOperatorsMixin
 
 from .backend import B200Backend
-from .exceptions import BackendMismatchError
+from . import exceptions as _exc
 
 _FUNCTIONS = {}
 
@@ -174,7 +174,7 @@ def array(obj, dtype=None, *, copy=True, order="C", backend=None):
     if isinstance(obj, ndarray):
         target = obj._backend if backend is None else get_backend(backend)
         if target is not obj._backend:
-            raise BackendMismatchError("Use to_backend(a, backend) to transfer explicitly")
+            raise _exc.BackendMismatchError("Use to_backend(a, backend) to transfer explicitly")
         return obj.astype(dtype or obj.dtype, copy=copy)
     target = get_backend(backend)
     host = np.asarray(obj, dtype=dtype, order="C")
@@ -246,7 +246,7 @@ def reshape(a, shape, order="C"):
 def _common_backend(args):
     found = [a._backend for a in args if isinstance(a, ndarray)]
     if found and any(b is not found[0] for b in found):
-        raise BackendMismatchError("Arrays belong to different backends/devices; use to_backend()")
+        raise _exc.BackendMismatchError("Arrays belong to different backends/devices; use to_backend()")
     return found[0] if found else get_backend()
 
 

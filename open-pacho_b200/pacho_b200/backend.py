@@ -21,7 +21,7 @@ from math import prod
 import numpy as np
 
 from . import _lib
-from .exceptions import BackendUnavailableError, UnsupportedDtypeError
+from . import exceptions as _exc
 
 SUPPORTED = (np.dtype(np.float32), np.dtype(np.float64))
 
@@ -76,9 +76,9 @@ class B200Backend:
         count = C.c_int(0)
         status = self._lib.pb_device_count(C.byref(count))
         if status != _lib.PB_OK or count.value == 0:
-            raise BackendUnavailableError(f"no CUDA device for b200: {_lib.last_error()}")
+            raise _exc.BackendUnavailableError(f"no CUDA device for b200: {_lib.last_error()}")
         if not 0 <= identifier < count.value:
-            raise BackendUnavailableError(f"b200 device {device!r} not found ({count.value} visible)")
+            raise _exc.BackendUnavailableError(f"b200 device {device!r} not found ({count.value} visible)")
         name = C.create_string_buffer(256)
         total = C.c_size_t(0)
         sms, major, minor = C.c_int(), C.c_int(), C.c_int()
@@ -99,7 +99,7 @@ class B200Backend:
         ordinals = (C.c_int * 1)(identifier)
         status = self._lib.pb_init(1, ordinals, C.byref(ctx))
         if status != _lib.PB_OK:
-            raise BackendUnavailableError(f"b200 initialization failed: {_lib.last_error()}")
+            raise _exc.BackendUnavailableError(f"b200 initialization failed: {_lib.last_error()}")
         self._ctx = ctx
 
     # ---------------------------------------------------------------- basics
@@ -118,9 +118,9 @@ class B200Backend:
         try:
             dtype = np.dtype(dtype)
         except TypeError as exc:
-            raise UnsupportedDtypeError(str(exc)) from exc
+            raise _exc.UnsupportedDtypeError(str(exc)) from exc
         if dtype not in SUPPORTED or not dtype.isnative:
-            raise UnsupportedDtypeError(f"b200 backend supports float32 and float64, not {dtype}")
+            raise _exc.UnsupportedDtypeError(f"b200 backend supports float32 and float64, not {dtype}")
         return dtype
 
     @contextmanager

@@ -25,6 +25,25 @@ def _get_b200(device):
     return B200Backend(device)
 
 
+def _adopt_exceptions(theirs):
+    """Make the errors this backend raises catchable as OpenPacho's own classes
+    (``except openpacho.BackendUnavailableError`` and the dtype/mismatch
+    errors), whatever the import order was: each class is replaced by one that
+    derives from both this package's and OpenPacho's, and the raise sites look
+    the class up at raise time."""
+    import pacho_b200
+
+    from . import exceptions as ours
+
+    for name in ("BackendUnavailableError", "UnsupportedDtypeError", "BackendMismatchError"):
+        mine, other = getattr(ours, name), getattr(theirs, name)
+        if issubclass(mine, other):
+            continue
+        merged = type(name, (mine, other), {"__module__": ours.__name__, "__doc__": mine.__doc__})
+        setattr(ours, name, merged)
+        setattr(pacho_b200, name, merged)
+
+
 def register(openpacho=None):
     """Make ``openpacho.set_backend("b200", device=...)`` and friends work.
 
@@ -34,6 +53,7 @@ def register(openpacho=None):
     import importlib
 
     backends = importlib.import_module(openpacho.__name__ + ".backends")
+    _adopt_exceptions(importlib.import_module(openpacho.__name__ + ".exceptions"))
     original = backends.get_backend
     if getattr(original, _MARK, False):
         return openpacho
