@@ -68,8 +68,11 @@ __global__ void split_a_kernel(const float* __restrict__ A, float* __restrict__ 
   }
 }
 
-// B (nmat x K x N) -> B't (nmat*N x 3Kp): [hi | lo | hi], transposed via a
-// 32x32 shared tile so both the read (along N) and write (along K) coalesce.
+// B (nmat x K x N) -> B't, transposed to K-major via a 32x32 shared tile so
+// both the read (along N) and the write (along K) coalesce.  SEGS = 3 writes
+// [hi | lo | hi] (nmat*N x 3Kp, for the pre-split GEMM), SEGS = 2 writes
+// [hi | lo] (nmat*N x 2Kp, for the GEMM that splits A in shared memory).
+template <int SEGS>
 __global__ void split_bt_kernel(const float* __restrict__ B, float* __restrict__ Bt, int64_t K,
                                 int64_t N, int64_t Kp) {
   __shared__ float tile[32][33];
@@ -81,16 +84,16 @@ __global__ void split_bt_kernel(const float* __restrict__ B, float* __restrict__
     tile[j][threadIdx.x] = (k < K && n < N) ? __ldg(src + k * N + n) : 0.0f;
   }
   __syncthreads();
-  const int64_t K3 = 3 * Kp;
+  const int64_t KS = SEGS * Kp;
   for (int j = threadIdx.y; j < 32; j += blockDim.y) {
     const int64_t n = n0 + j, k = k0 + threadIdx.x;
     if (n < N && k < Kp) {
       float hi, lo;
       split(tile[threadIdx.x][j], hi, lo);
-      float* o = Bt + (mat * N + n) * K3 + k;
+      float* o = Bt + (mat * N + n) * KS + k;
       o[0] = hi;
       o[Kp] = lo;
-      o[2 * Kp] = hi;
+      if (SEGS == 3) o[2 * Kp] = hi;
     }
   }
 }
@@ -494,6 +497,276 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
 }
 
+// --------------------------------------------- GEMM with A split in smem --
+//
+// Variant used when A's rows are 16-byte aligned (K % 4 == 0): A is loaded
+// raw by TMA and split into hi/lo inside shared memory, so A's bytes cross
+// HBM and L2 once (the pre-split path writes and re-reads A three times).
+// B keeps a pre-split K-major copy [hi | lo].  Per raw 32-element K-slice the
+// MMA thread issues lo*hi, hi*lo, hi*hi (small terms first) into the TMEM
+// accumulator, promoted to fp32 registers every FCHUNK slices (36 MMA steps).
+// Warps: 0 TMA producer, 1 MMA issuer, 2..9 accumulators (as in the
+// pre-split kernel), 10..11 transform (raw A -> hi in place + lo copy; the
+// map is elementwise, so the 128-byte swizzle needs no special handling).
+
+constexpr int FBN = 128;
+constexpr int FSTAGES = 3;
+#ifndef PB_TF32_FCHUNK
+#define PB_TF32_FCHUNK 3
+#endif
+constexpr int FCHUNK = PB_TF32_FCHUNK;
+constexpr int F_ACC_WARPS = 8;
+constexpr int F_XFORM_WARPS = 2;
+constexpr int FUSED_THREADS = 32 * (2 + F_ACC_WARPS + F_XFORM_WARPS);
+
+struct FSmem {
+  static constexpr int TILE = BM * BK * 4;  // 16 KiB: a 128 x 32 fp32 tile
+  static constexpr int A = 0, ALO = TILE, BHI = 2 * TILE, BLO = 3 * TILE;
+  static constexpr int STAGE = 4 * TILE;    // 64 KiB
+  static constexpr int TX_BYTES = 3 * TILE; // what TMA delivers per stage
+  static constexpr int TOTAL = FSTAGES * STAGE + 1024 + 256;
+};
+
+// hi = round-to-nearest tf32 of x (ties away), lo = tf32(x - hi); integer
+// rounding keeps the conversion off the slower conversion pipe.  Non-finite x
+// keeps hi = x and lo = 0, as in the pre-split pass.
+__device__ __forceinline__ void split_bits(float x, float& hi, float& lo) {
+  const uint32_t b = __float_as_uint(x);
+  if ((b & 0x7f800000u) == 0x7f800000u) {
+    hi = x;
+    lo = 0.0f;
+    return;
+  }
+  hi = __uint_as_float((b + 0x1000u) & 0xffffe000u);
+  lo = __uint_as_float((__float_as_uint(x - hi) + 0x1000u) & 0xffffe000u);
+}
+
+__global__ void __launch_bounds__(FUSED_THREADS, 1)
+    tf32x3_fused_kernel(const __grid_constant__ CUtensorMap map_a,
+                        const __grid_constant__ CUtensorMap map_b, Tf32Params p, int Kp) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023) & ~1023u;
+  unsigned char* gbase = smem_raw + (base - raw);
+  const uint32_t bars = base + FSTAGES * FSmem::STAGE;
+  uint64_t* bar_ptr = reinterpret_cast<uint64_t*>(gbase + FSTAGES * FSmem::STAGE);
+  // full[S] (TMA landed), ready[S] (A split), empty[S] (MMAs done), accf[2], acce[2]
+  const uint32_t full0 = bars, ready0 = bars + 8 * FSTAGES, empty0 = bars + 16 * FSTAGES;
+  const uint32_t accf0 = bars + 24 * FSTAGES, acce0 = accf0 + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 3 * FSTAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr uint32_t TMEM_COLS = 2 * FBN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < FSTAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(ready0 + 8 * s, F_XFORM_WARPS);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf0 + 8 * b, 1);
+      mbar_init(acce0 + 8 * b, F_ACC_WARPS);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  const int64_t items = p.tiles * p.ksplit;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      int64_t g = 0;
+      for (int64_t w = blockIdx.x; w < items && !*abort_flag; w += gridDim.x) {
+        const TileCoord tc = tile_coord(p, w / p.ksplit);
+        int kb0, kb1;
+        split_range(p, (int)(w % p.ksplit), kb0, kb1);
+        int64_t ao, bo;
+        batch_offsets(p.map, tc.bz, &ao, &bo);
+        const int32_t a_row = (int32_t)(ao * p.M + tc.m_tile * BM);
+        const int32_t b_row = (int32_t)(bo * p.N + tc.n_tile * FBN);
+        for (int kb = kb0; kb < kb1; ++kb, ++g) {
+          const int s = (int)(g % FSTAGES);
+          if (!mbar_wait(empty0 + 8 * s, (uint32_t)(((g / FSTAGES) & 1) ^ 1), abort_flag, p.err))
+            break;
+          const uint32_t st = base + s * FSmem::STAGE;
+          mbar_expect_tx(full0 + 8 * s, FSmem::TX_BYTES);
+          tma_load_2d(st + FSmem::A, &map_a, kb * BK, a_row, full0 + 8 * s);
+          tma_load_2d(st + FSmem::BHI, &map_b, kb * BK, b_row, full0 + 8 * s);
+          tma_load_2d(st + FSmem::BLO, &map_b, Kp + kb * BK, b_row, full0 + 8 * s);
+        }
+      }
+      if (*abort_flag) {
+        for (int64_t q = (g > FSTAGES ? g - FSTAGES : 0); q < g; ++q) {
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(full0 + 8 * (int)(q % FSTAGES), (uint32_t)((q / FSTAGES) & 1)) &&
+                 globaltimer() - t0 < kTimeoutNs) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      const uint32_t idesc = instr_desc(FBN);
+      int64_t g = 0, gc = 0;
+      bool ok = true;
+      for (int64_t w = blockIdx.x; w < items && ok; w += gridDim.x) {
+        int kb0, kb1;
+        split_range(p, (int)(w % p.ksplit), kb0, kb1);
+        const int nchunks = (kb1 - kb0 + FCHUNK - 1) / FCHUNK;
+        for (int c = 0; c < nchunks && ok; ++c, ++gc) {
+          const int buf = (int)(gc & 1);
+          ok = mbar_wait(acce0 + 8 * buf, (uint32_t)(((gc >> 1) & 1) ^ 1), abort_flag, p.err);
+          if (!ok) break;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t d = tmem + (uint32_t)(buf * FBN);
+          const int kb_start = kb0 + c * FCHUNK;
+          const int kb_end = min(kb1, kb_start + FCHUNK);
+          for (int kb = kb_start; kb < kb_end; ++kb, ++g) {
+            const int s = (int)(g % FSTAGES);
+            ok = mbar_wait(ready0 + 8 * s, (uint32_t)((g / FSTAGES) & 1), abort_flag, p.err);
+            if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t st = base + s * FSmem::STAGE;
+            const uint64_t ahi = smem_desc(st + FSmem::A), alo = smem_desc(st + FSmem::ALO);
+            const uint64_t bhi = smem_desc(st + FSmem::BHI), blo = smem_desc(st + FSmem::BLO);
+            const bool first = kb == kb_start;
+#pragma unroll
+            for (int k = 0; k < BK / 8; ++k)
+              umma_tf32(d, alo + 2 * k, bhi + 2 * k, idesc, (!first || k > 0) ? 1u : 0u);
+#pragma unroll
+            for (int k = 0; k < BK / 8; ++k) umma_tf32(d, ahi + 2 * k, blo + 2 * k, idesc, 1u);
+#pragma unroll
+            for (int k = 0; k < BK / 8; ++k) umma_tf32(d, ahi + 2 * k, bhi + 2 * k, idesc, 1u);
+            umma_commit(empty0 + 8 * s);
+          }
+          umma_commit(accf0 + 8 * buf);
+        }
+      }
+    }
+  } else if (warp >= 2 + F_ACC_WARPS) {
+    // -------------------------------------------------- transform warps
+    const int t = (warp - 2 - F_ACC_WARPS) * 32 + lane;
+    int64_t g = 0;
+    for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
+      int kb0, kb1;
+      split_range(p, (int)(w % p.ksplit), kb0, kb1);
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb, ++g) {
+        const int s = (int)(g % FSTAGES);
+        ok = mbar_wait(full0 + 8 * s, (uint32_t)((g / FSTAGES) & 1), abort_flag, p.err);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        float4* a = reinterpret_cast<float4*>(gbase + s * FSmem::STAGE + FSmem::A);
+        float4* alo = reinterpret_cast<float4*>(gbase + s * FSmem::STAGE + FSmem::ALO);
+#pragma unroll 4
+        for (int i = t; i < FSmem::TILE / 16; i += 32 * F_XFORM_WARPS) {
+          const float4 v = a[i];
+          float4 h, l;
+          split_bits(v.x, h.x, l.x);
+          split_bits(v.y, h.y, l.y);
+          split_bits(v.z, h.z, l.z);
+          split_bits(v.w, h.w, l.w);
+          a[i] = h;
+          alo[i] = l;
+        }
+        // Generic-proxy stores must be visible to the tensor core (async proxy).
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ready0 + 8 * s);
+      }
+      if (!ok) break;
+    }
+  } else {
+    // -------------------------------------------------- accumulator warps
+    constexpr int COLS = FBN / 2;
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * COLS);
+    int64_t gc = 0;
+    for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
+      const TileCoord tc = tile_coord(p, w / p.ksplit);
+      const int split = (int)(w % p.ksplit);
+      int kb0, kb1;
+      split_range(p, split, kb0, kb1);
+      const int nchunks = (kb1 - kb0 + FCHUNK - 1) / FCHUNK;
+      float acc[COLS];
+#pragma unroll
+      for (int i = 0; i < COLS; ++i) acc[i] = 0.0f;
+      bool ok = true;
+      for (int c = 0; c < nchunks; ++c, ++gc) {
+        const int buf = (int)(gc & 1);
+        ok = mbar_wait(accf0 + 8 * buf, (uint32_t)((gc >> 1) & 1), abort_flag, p.err);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int piece = 0; piece < COLS / 32; piece += 2) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32x2(lane_base + (uint32_t)(buf * FBN + piece * 32),
+                      lane_base + (uint32_t)(buf * FBN + piece * 32 + 32), r0, r1);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            acc[piece * 32 + i] += __uint_as_float(r0[i]);
+            acc[piece * 32 + 32 + i] += __uint_as_float(r1[i]);
+          }
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acce0 + 8 * buf);
+      }
+      if (!ok || *abort_flag) break;
+      const int64_t row = tc.m_tile * BM + quad * 32 + lane;
+      if (row < p.M) {
+        const int64_t col0 = tc.n_tile * FBN + half * COLS;
+        const int64_t batch = p.tiles / ((int64_t)p.tiles_m * p.tiles_n);
+        float* dst_base = p.ksplit == 1 ? p.C : p.partial + split * batch * p.M * p.N;
+        float* crow = dst_base + tc.bz * p.M * p.N + row * p.N + col0;
+        if ((p.N % 4) == 0 && col0 + COLS <= p.N) {
+          float4* dst = reinterpret_cast<float4*>(crow);
+#pragma unroll
+          for (int j = 0; j < COLS / 4; ++j)
+            dst[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < COLS; ++j)
+            if (col0 + j < p.N) crow[j] = acc[j];
+        }
+      }
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (*abort_flag) {
+      const uint64_t t0 = globaltimer();
+      while (globaltimer() - t0 < 1000000ull) {
+      }
+    }
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(TMEM_COLS));
+  }
+}
+
 // C = sum over splits of the partial tiles, in split order (deterministic).
 __global__ void splitk_reduce_kernel(const float* __restrict__ partial, float* __restrict__ C,
                                      int64_t count, int ksplit) {
@@ -562,6 +835,71 @@ int64_t matrices_used(const BatchMap& m, bool a) {
 
 }  // namespace
 
+// 3xTF32 with A split in shared memory (K % 4 == 0): B -> [hi | lo] K-major
+// once, then the fused kernel (and the split reduction when K is split).
+int gemm_f32_fused(Device* d, const BatchMap& map, int64_t batch, int64_t M, int64_t N, int64_t K,
+                   int64_t Kp, int64_t nA, int64_t nB, const float* A, const float* B, float* C) {
+  const int64_t rows_a = nA * M, rows_b = nB * N;
+  const size_t bytes_b = (size_t)rows_b * 2 * Kp * sizeof(float);
+  const int tiles_m = (int)ceil_div(M, (int64_t)BM);
+  const int tiles_n = (int)ceil_div(N, (int64_t)FBN);
+  const int64_t tiles = (int64_t)tiles_m * tiles_n * batch;
+  const int kblocks = (int)(Kp / BK);
+  int ksplit = 1;
+  if (tiles < d->sm_count) {
+    ksplit = (int)(d->sm_count / tiles);
+    const int most = kblocks / (2 * FCHUNK);
+    if (ksplit > most) ksplit = most;
+    if (ksplit < 1) ksplit = 1;
+  }
+  const size_t bytes_p = ksplit > 1 ? (size_t)ksplit * batch * M * N * sizeof(float) : 0;
+  void* ws;
+  PB_CHECK(scratch(d, bytes_b + bytes_p, &ws));
+  float* Bt = (float*)ws;
+  const int64_t gx = ceil_div(N, (int64_t)32), gy = ceil_div(Kp, (int64_t)32);
+  if (gx > INT32_MAX || gy > 65535 || nB > 65535)
+    PB_FAIL(PB_ERR_UNSUPPORTED, "B operand too large for the split grid");
+  split_bt_kernel<2><<<dim3((unsigned)gx, (unsigned)gy, (unsigned)nB), dim3(32, 8), 0, d->stream>>>(
+      B, Bt, K, N, Kp);
+  PB_LAUNCHED(d);
+
+  CUtensorMap ma, mb;
+  PB_CHECK(encode_kmajor(&ma, A, rows_a, K, BM));
+  PB_CHECK(encode_kmajor(&mb, Bt, rows_b, 2 * Kp, FBN));
+  Tf32Params p;
+  p.C = C;
+  p.partial = ksplit > 1 ? (float*)((char*)ws + bytes_b) : nullptr;
+  p.M = M;
+  p.N = N;
+  p.kblocks = kblocks;
+  p.tiles_m = tiles_m;
+  p.tiles_n = tiles_n;
+  p.tiles = tiles;
+  p.ksplit = ksplit;
+  p.map = map;
+  p.err = d->err_dev;
+  const int smem = FSmem::TOTAL;
+  static bool configured = false;
+  if (!configured) {
+    PB_CUDA(cudaFuncSetAttribute(tf32x3_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 smem));
+    configured = true;
+  }
+  const int64_t items = tiles * ksplit;
+  const int64_t grid = items < d->sm_count ? items : d->sm_count;
+  tf32x3_fused_kernel<<<(unsigned)grid, FUSED_THREADS, smem, d->stream>>>(ma, mb, p, (int)Kp);
+  PB_LAUNCHED(d);
+  if (ksplit > 1) {
+    const int64_t count = batch * M * N;
+    int64_t blocks = ceil_div(count / 4 + 1, (int64_t)256);
+    const int64_t cap = (int64_t)d->sm_count * 8;
+    if (blocks > cap) blocks = cap;
+    splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, d->stream>>>(p.partial, C, count, ksplit);
+    PB_LAUNCHED(d);
+  }
+  return PB_OK;
+}
+
 // algo: 0 auto, 1 SIMT, 2 3xTF32 tcgen05.
 int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int64_t N, int64_t K,
                   const float* A, const float* B, float* C, int algo) {
@@ -572,6 +910,9 @@ int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
   const int64_t Kp = ceil_div(K, (int64_t)BK) * BK;
   const int64_t K3 = 3 * Kp;
   const int64_t nA = matrices_used(map, true), nB = matrices_used(map, false);
+  if (K % 4 == 0 && (uintptr_t)A % 16 == 0 && nA * M <= INT32_MAX && nB * N <= INT32_MAX &&
+      Kp / BK <= INT32_MAX)
+    return gemm_f32_fused(d, map, batch, M, N, K, Kp, nA, nB, A, B, C);
   const int64_t rows_a = nA * M, rows_b = nB * N;
   if (rows_a > INT32_MAX || rows_b > INT32_MAX || K3 / BK > INT32_MAX)
     PB_FAIL(PB_ERR_UNSUPPORTED, "GEMM operand too large for 32-bit TMA coordinates");
@@ -609,7 +950,7 @@ int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
     const int64_t gx = ceil_div(N, (int64_t)32), gy = ceil_div(Kp, (int64_t)32);
     if (gx > INT32_MAX || gy > 65535 || nB > 65535)
       PB_FAIL(PB_ERR_UNSUPPORTED, "B operand too large for the split grid");
-    split_bt_kernel<<<dim3((unsigned)gx, (unsigned)gy, (unsigned)nB), dim3(32, 8), 0, d->stream>>>(
+    split_bt_kernel<3><<<dim3((unsigned)gx, (unsigned)gy, (unsigned)nB), dim3(32, 8), 0, d->stream>>>(
         B, Bt, K, N, Kp);
     PB_LAUNCHED(d);
   }
