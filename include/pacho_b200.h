@@ -117,11 +117,21 @@ int pb_gemm(pb_ctx* ctx, int dev, int dtype, int batch_ndim, const int64_t* batc
 
 /* pb_gemm with an explicit kernel choice: PB_GEMM_AUTO (what pb_gemm does),
  * PB_GEMM_SIMT (register-tiled CUDA-core FFMA/DFMA kernel), PB_GEMM_TF32X3
- * (float32 only) or PB_GEMM_DMMA (float64 only, FP64 tensor cores).  The
+ * (float32; picks one of the two 3xTF32 kernels by size),
+ * PB_GEMM_TF32X3_PRESPLIT (operands split into hi/lo copies in HBM first),
+ * PB_GEMM_TF32X3_FUSED (A split in shared memory; needs K % 4 == 0) or
+ * PB_GEMM_DMMA (float64 only, FP64 tensor cores).  The
  * reference exposes the same kind of provider choice as
  * CUDABackend(blas="custom"|"cublas")
  * (src/openpacho/_cuda.py:138-141). */
-enum { PB_GEMM_AUTO = 0, PB_GEMM_SIMT = 1, PB_GEMM_TF32X3 = 2, PB_GEMM_DMMA = 3 };
+enum {
+  PB_GEMM_AUTO = 0,
+  PB_GEMM_SIMT = 1,
+  PB_GEMM_TF32X3 = 2,
+  PB_GEMM_DMMA = 3,
+  PB_GEMM_TF32X3_PRESPLIT = 4,
+  PB_GEMM_TF32X3_FUSED = 5
+};
 int pb_gemm_ex(pb_ctx* ctx, int dev, int dtype, int batch_ndim, const int64_t* batch_shape,
                const int64_t* a_bstride, const int64_t* b_bstride, int64_t M, int64_t N,
                int64_t K, const void* A, const void* B, void* C, int algo);

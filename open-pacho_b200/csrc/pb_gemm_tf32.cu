@@ -505,9 +505,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 // B keeps a pre-split K-major copy [hi | lo].  Per raw 32-element K-slice the
 // MMA thread issues lo*hi, hi*lo, hi*hi (small terms first) into the TMEM
 // accumulator, promoted to fp32 registers every FCHUNK slices (36 MMA steps).
-// Warps: 0 TMA producer, 1 MMA issuer, 2..9 accumulators (as in the
-// pre-split kernel), 10..11 transform (raw A -> hi in place + lo copy; the
-// map is elementwise, so the 128-byte swizzle needs no special handling).
+// Warps: 0 TMA producer, 1 MMA issuer, 2..11 split each landed A tile (raw A
+// -> hi in place + lo copy; the map is elementwise, so the 128-byte swizzle
+// needs no special handling), and 2..9 also promote and store (as the
+// accumulator warps of the pre-split kernel).
 
 constexpr int FBN = 128;
 constexpr int FSTAGES = 3;
@@ -562,7 +563,7 @@ __global__ void __launch_bounds__(FUSED_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < FSTAGES; ++s) {
       mbar_init(full0 + 8 * s, 1);
-      mbar_init(ready0 + 8 * s, F_XFORM_WARPS);
+      mbar_init(ready0 + 8 * s, F_ACC_WARPS + F_XFORM_WARPS);
       mbar_init(empty0 + 8 * s, 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -657,25 +658,65 @@ __global__ void __launch_bounds__(FUSED_THREADS, 1)
         }
       }
     }
-  } else if (warp >= 2 + F_ACC_WARPS) {
-    // -------------------------------------------------- transform warps
-    const int t = (warp - 2 - F_ACC_WARPS) * 32 + lane;
-    int64_t g = 0;
-    for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
+  } else {
+    // ------------------------------ transform (warps 2..11) + accumulators (2..9)
+    // Every one of these 10 warps splits its share of each landed A tile; the
+    // 8 accumulator warps also promote chunk c-1 right after splitting the last
+    // slice of chunk c (the tensor pipe is then busy with chunk c), promote the
+    // final chunk at the end of the tile and store it.
+    constexpr int COLS = FBN / 2;
+    constexpr int XT = 32 * (F_ACC_WARPS + F_XFORM_WARPS);
+    const bool is_acc = warp < 2 + F_ACC_WARPS;
+    const int xt = (warp - 2) * 32 + lane;
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * COLS);
+    int64_t g = 0, gc = 0;
+    bool ok = true;
+    float acc[COLS];
+
+    auto promote = [&]() {
+      const int buf = (int)(gc & 1);
+      const bool got = mbar_wait(accf0 + 8 * buf, (uint32_t)((gc >> 1) & 1), abort_flag, p.err);
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      if (!__all_sync(0xffffffffu, got)) {
+        ok = false;
+        return;
+      }
+#pragma unroll
+      for (int piece = 0; piece < COLS / 32; piece += 2) {
+        uint32_t r0[32], r1[32];
+        tmem_ld32x2(lane_base + (uint32_t)(buf * FBN + piece * 32),
+                    lane_base + (uint32_t)(buf * FBN + piece * 32 + 32), r0, r1);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          acc[piece * 32 + i] += __uint_as_float(r0[i]);
+          acc[piece * 32 + 32 + i] += __uint_as_float(r1[i]);
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce0 + 8 * buf);
+      ++gc;
+    };
+
+    for (int64_t w = blockIdx.x; w < items && ok; w += gridDim.x) {
+      const TileCoord tc = tile_coord(p, w / p.ksplit);
+      const int split = (int)(w % p.ksplit);
       int kb0, kb1;
-      split_range(p, (int)(w % p.ksplit), kb0, kb1);
-      bool ok = true;
-      for (int kb = kb0; kb < kb1; ++kb, ++g) {
+      split_range(p, split, kb0, kb1);
+#pragma unroll
+      for (int i = 0; i < COLS; ++i) acc[i] = 0.0f;
+      for (int kb = kb0; kb < kb1 && ok; ++kb, ++g) {
         const int s = (int)(g % FSTAGES);
-        ok = mbar_wait(full0 + 8 * s, (uint32_t)((g / FSTAGES) & 1), abort_flag, p.err);
-        if (!__all_sync(0xffffffffu, ok)) {
+        const bool got = mbar_wait(full0 + 8 * s, (uint32_t)((g / FSTAGES) & 1), abort_flag, p.err);
+        if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
         float4* a = reinterpret_cast<float4*>(gbase + s * FSmem::STAGE + FSmem::A);
         float4* alo = reinterpret_cast<float4*>(gbase + s * FSmem::STAGE + FSmem::ALO);
-#pragma unroll 4
-        for (int i = t; i < FSmem::TILE / 16; i += 32 * F_XFORM_WARPS) {
+        for (int i = xt; i < FSmem::TILE / 16; i += XT) {
           const float4 v = a[i];
           float4 h, l;
           split_bits(v.x, h.x, l.x);
@@ -689,49 +730,12 @@ __global__ void __launch_bounds__(FUSED_THREADS, 1)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(ready0 + 8 * s);
+        const int c = (kb - kb0) / FCHUNK;
+        const bool chunk_end = (kb - kb0) % FCHUNK == FCHUNK - 1 || kb == kb1 - 1;
+        if (is_acc && chunk_end && c >= 1) promote();  // chunk c-1
       }
-      if (!ok) break;
-    }
-  } else {
-    // -------------------------------------------------- accumulator warps
-    constexpr int COLS = FBN / 2;
-    const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * COLS);
-    int64_t gc = 0;
-    for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
-      const TileCoord tc = tile_coord(p, w / p.ksplit);
-      const int split = (int)(w % p.ksplit);
-      int kb0, kb1;
-      split_range(p, split, kb0, kb1);
-      const int nchunks = (kb1 - kb0 + FCHUNK - 1) / FCHUNK;
-      float acc[COLS];
-#pragma unroll
-      for (int i = 0; i < COLS; ++i) acc[i] = 0.0f;
-      bool ok = true;
-      for (int c = 0; c < nchunks; ++c, ++gc) {
-        const int buf = (int)(gc & 1);
-        ok = mbar_wait(accf0 + 8 * buf, (uint32_t)((gc >> 1) & 1), abort_flag, p.err);
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        if (!__all_sync(0xffffffffu, ok)) {
-          ok = false;
-          break;
-        }
-#pragma unroll
-        for (int piece = 0; piece < COLS / 32; piece += 2) {
-          uint32_t r0[32], r1[32];
-          tmem_ld32x2(lane_base + (uint32_t)(buf * FBN + piece * 32),
-                      lane_base + (uint32_t)(buf * FBN + piece * 32 + 32), r0, r1);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            acc[piece * 32 + i] += __uint_as_float(r0[i]);
-            acc[piece * 32 + 32 + i] += __uint_as_float(r1[i]);
-          }
-        }
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbar_arrive(acce0 + 8 * buf);
-      }
+      if (!is_acc) continue;
+      if (ok) promote();  // the tile's last chunk
       if (!ok || *abort_flag) break;
       const int64_t row = tc.m_tile * BM + quad * 32 + lane;
       if (row < p.M) {
@@ -900,18 +904,34 @@ int gemm_f32_fused(Device* d, const BatchMap& map, int64_t batch, int64_t M, int
   return PB_OK;
 }
 
-// algo: 0 auto, 1 SIMT, 2 3xTF32 tcgen05.
+// Products with at most this many columns take the shared-memory split
+// kernel.  The pre-split kernel's extra pass over A costs about 12*M*K bytes,
+// i.e. a share of the GEMM that shrinks as 1/N, and its 256-wide tiles waste
+// more of a narrow C.  Measured on B200 (effective TFLOP/s, pre-split vs fused):
+// 1024^3 51 vs 64, (8,16)x512x384x256 53 vs 72, 16384x1024x4096 149 vs 178,
+// 2048^3 138 vs 123, 4096^3 179 vs 170, 8192^3 212 vs 170.
+#ifndef PB_TF32_FUSED_MAX_N
+#define PB_TF32_FUSED_MAX_N 1024
+#endif
+
+// algo: 0 auto, 1 SIMT, 2 3xTF32 (kernel by size), 4 pre-split, 5 A split in smem.
 int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int64_t N, int64_t K,
                   const float* A, const float* B, float* C, int algo) {
   if (algo == 0) algo = (M >= 64 && N >= 64 && K >= 32) ? 2 : 1;
   if (algo == 1) return gemm_simt_f32(d, map, batch, M, N, K, A, B, C);
-  if (algo != 2) PB_FAIL(PB_ERR_INVALID, "unknown GEMM algorithm %d", algo);
+  if (algo != PB_GEMM_TF32X3 && algo != PB_GEMM_TF32X3_FUSED && algo != PB_GEMM_TF32X3_PRESPLIT)
+    PB_FAIL(PB_ERR_INVALID, "unknown GEMM algorithm %d", algo);
 
   const int64_t Kp = ceil_div(K, (int64_t)BK) * BK;
   const int64_t K3 = 3 * Kp;
   const int64_t nA = matrices_used(map, true), nB = matrices_used(map, false);
-  if (K % 4 == 0 && (uintptr_t)A % 16 == 0 && nA * M <= INT32_MAX && nB * N <= INT32_MAX &&
-      Kp / BK <= INT32_MAX)
+  // Two 3xTF32 kernels: A split in shared memory (TMA needs 16-byte aligned
+  // rows of A: K % 4 == 0) or both operands split in HBM first.
+  const bool can_fuse = K % 4 == 0 && (uintptr_t)A % 16 == 0 && nA * M <= INT32_MAX &&
+                        nB * N <= INT32_MAX && Kp / BK <= INT32_MAX;
+  if (algo == PB_GEMM_TF32X3_FUSED && !can_fuse)
+    PB_FAIL(PB_ERR_UNSUPPORTED, "the shared-memory split needs K %% 4 == 0 and aligned A");
+  if (algo == PB_GEMM_TF32X3_FUSED || (algo == PB_GEMM_TF32X3 && can_fuse && N <= PB_TF32_FUSED_MAX_N))
     return gemm_f32_fused(d, map, batch, M, N, K, Kp, nA, nB, A, B, C);
   const int64_t rows_a = nA * M, rows_b = nB * N;
   if (rows_a > INT32_MAX || rows_b > INT32_MAX || K3 / BK > INT32_MAX)

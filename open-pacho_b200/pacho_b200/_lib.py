@@ -31,6 +31,8 @@ PB_GEMM_AUTO = 0
 PB_GEMM_SIMT = 1
 PB_GEMM_TF32X3 = 2
 PB_GEMM_DMMA = 3
+PB_GEMM_TF32X3_PRESPLIT = 4
+PB_GEMM_TF32X3_FUSED = 5
 
 LIBRARY_NAME = "libpacho_b200.so"
 

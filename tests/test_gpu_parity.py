@@ -129,29 +129,35 @@ def _gemm_shapes():
                rng.standard_normal((k, n)).astype(np.float32))
 
 
-@pytest.mark.parametrize("algo", [_lib.PB_GEMM_SIMT, _lib.PB_GEMM_TF32X3, _lib.PB_GEMM_DMMA],
-                         ids=["simt", "tf32x3", "dmma"])
+@pytest.mark.parametrize("algo", [_lib.PB_GEMM_SIMT, _lib.PB_GEMM_TF32X3, _lib.PB_GEMM_TF32X3_PRESPLIT,
+                                  _lib.PB_GEMM_TF32X3_FUSED, _lib.PB_GEMM_DMMA],
+                         ids=["simt", "tf32x3", "tf32x3_presplit", "tf32x3_fused", "dmma"])
 @pytest.mark.parametrize("case", list(_gemm_shapes()), ids=lambda c: c[0])
 def test_every_gemm_kernel_on_every_shape(b200, algo, case):
     name, a, b = case
-    if algo == _lib.PB_GEMM_TF32X3 and a.dtype != np.float32:
+    tf32 = (_lib.PB_GEMM_TF32X3, _lib.PB_GEMM_TF32X3_PRESPLIT, _lib.PB_GEMM_TF32X3_FUSED)
+    if algo in tf32 and a.dtype != np.float32:
         pytest.skip("3xTF32 is the float32 kernel")
+    if algo == _lib.PB_GEMM_TF32X3_FUSED and a.shape[-1] % 4:
+        pytest.skip("the shared-memory split needs K % 4 == 0")
     if algo == _lib.PB_GEMM_DMMA:
         a, b = a.astype(np.float64), b.astype(np.float64)
     got = _call_gemm_ex(b200, a, b, algo)
     want = numpy_backend.matmul(a, b)
     # Forced 3xTF32 below K=32 carries the split error model (auto sends it to SIMT).
-    extra = 16.0 if algo == _lib.PB_GEMM_TF32X3 and a.shape[-1] < 32 else 0.0
+    extra = 16.0 if algo in tf32 and a.shape[-1] < 32 else 0.0
     assert tolerance.gemm_violations(got, want, a, b, extra_u=extra) == 0
 
 
-def test_tf32x3_keeps_float32_accuracy(b200):
+@pytest.mark.parametrize("algo", [_lib.PB_GEMM_TF32X3_PRESPLIT, _lib.PB_GEMM_TF32X3_FUSED],
+                         ids=["presplit", "fused"])
+def test_tf32x3_keeps_float32_accuracy(b200, algo):
     """3xTF32 must be as accurate as float32 GEMM, unlike plain TF32."""
     rng = np.random.default_rng(12)
     a = rng.standard_normal((256, 2048)).astype(np.float32)
     b = rng.standard_normal((2048, 192)).astype(np.float32)
     ref = a.astype(np.float64) @ b.astype(np.float64)
-    got = _call_gemm_ex(b200, a, b, _lib.PB_GEMM_TF32X3).astype(np.float64)
+    got = _call_gemm_ex(b200, a, b, algo).astype(np.float64)
     err = np.linalg.norm(got - ref) / np.linalg.norm(ref)
 
     def tf32(x):  # what a single TF32 pass would see (round to 10 mantissa bits)
@@ -165,7 +171,9 @@ def test_tf32x3_keeps_float32_accuracy(b200):
     assert err < 1e-6 and err < 4 * sgemm, (err, sgemm, err_1x)
 
 
-def test_tf32x3_error_does_not_grow_with_k(b200):
+@pytest.mark.parametrize("algo", [_lib.PB_GEMM_TF32X3_PRESPLIT, _lib.PB_GEMM_TF32X3_FUSED],
+                         ids=["presplit", "fused"])
+def test_tf32x3_error_does_not_grow_with_k(b200, algo):
     """Promotion out of the tensor core's truncating accumulator keeps the
     relative error flat in K (it grew linearly, ~1.9e-5 at K=8192, without)."""
     rng = np.random.default_rng(13)
@@ -174,7 +182,7 @@ def test_tf32x3_error_does_not_grow_with_k(b200):
         a = rng.standard_normal((128, k)).astype(np.float32)
         b = rng.standard_normal((k, 128)).astype(np.float32)
         ref = a.astype(np.float64) @ b.astype(np.float64)
-        got = _call_gemm_ex(b200, a, b, _lib.PB_GEMM_TF32X3).astype(np.float64)
+        got = _call_gemm_ex(b200, a, b, algo).astype(np.float64)
         errs.append(np.linalg.norm(got - ref) / np.linalg.norm(ref))
     assert errs[1] < 1e-6 and errs[1] < 3 * errs[0], errs
 
