@@ -20,6 +20,7 @@
 //  Every mbarrier wait is bounded in wall time (%globaltimer); on expiry the
 //  kernel raises the device error word, stops issuing, waits (bounded) for
 //  its own copies, frees TMEM and returns.
+#include <cfloat>
 #include <cudaTypedefs.h>
 
 #include "pb_internal.cuh"
@@ -44,15 +45,30 @@ __device__ __forceinline__ float tf32_rn(float x) {
   return __uint_as_float(r);
 }
 
-// hi and lo parts; non-finite values keep hi = x and lo = 0.
-__device__ __forceinline__ void split(float x, float& hi, float& lo) {
+// Operand magnitudes the split cannot carry at float32 accuracy: nonzero
+// |x| < 2^-57.  A product with such a factor can fall below 2^-115, where the
+// lo*hi cross terms (or the whole product) become subnormal and the tensor
+// core flushes them.  Rows of A and kTagCols-column groups of B holding one
+// are tagged by the split passes, and the epilogue recomputes the outputs
+// they touch with float32 FMA.
+constexpr uint32_t kTinyExp = 127 - 57;  // biased exponent of 2^-57
+constexpr int kTagCols = 64;
+
+__device__ __forceinline__ bool tiny(float x) {
+  return (__float_as_uint(x) & 0x7fffffffu) - 1u < (kTinyExp << 23) - 1u;
+}
+
+// hi and lo parts; non-finite values keep hi = x and lo = 0.  Returns tiny(x).
+__device__ __forceinline__ bool split(float x, float& hi, float& lo) {
   hi = tf32_rn(x);
   lo = isfinite(x) ? tf32_rn(x - hi) : 0.0f;
+  return tiny(x);
 }
 
 // A (rows x K) -> A' (rows x 3Kp): [lo | hi | hi].
 __global__ void split_a_kernel(const float* __restrict__ A, float* __restrict__ Ap, int64_t rows,
-                               int64_t K, int64_t Kp) {
+                               int64_t K, int64_t Kp, unsigned int* rowtag, unsigned int* tagany,
+                               unsigned int gen) {
   const int64_t total = rows * Kp;
   const int64_t K3 = 3 * Kp;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -60,7 +76,10 @@ __global__ void split_a_kernel(const float* __restrict__ A, float* __restrict__ 
     const int64_t r = i / Kp, k = i % Kp;
     const float x = k < K ? __ldg(A + r * K + k) : 0.0f;
     float hi, lo;
-    split(x, hi, lo);
+    if (split(x, hi, lo)) {
+      rowtag[r] = gen;
+      tagany[0] = gen;
+    }
     float* o = Ap + r * K3 + k;
     o[0] = lo;
     o[Kp] = hi;
@@ -74,14 +93,20 @@ __global__ void split_a_kernel(const float* __restrict__ A, float* __restrict__ 
 // [hi | lo] (nmat*N x 2Kp, for the GEMM that splits A in shared memory).
 template <int SEGS>
 __global__ void split_bt_kernel(const float* __restrict__ B, float* __restrict__ Bt, int64_t K,
-                                int64_t N, int64_t Kp) {
+                                int64_t N, int64_t Kp, unsigned int* coltag, int64_t groups,
+                                unsigned int* tagany, unsigned int gen) {
   __shared__ float tile[32][33];
   const int64_t mat = blockIdx.z;
   const int64_t k0 = (int64_t)blockIdx.y * 32, n0 = (int64_t)blockIdx.x * 32;
   const float* src = B + mat * K * N;
   for (int j = threadIdx.y; j < 32; j += blockDim.y) {
     const int64_t k = k0 + j, n = n0 + threadIdx.x;
-    tile[j][threadIdx.x] = (k < K && n < N) ? __ldg(src + k * N + n) : 0.0f;
+    const float x = (k < K && n < N) ? __ldg(src + k * N + n) : 0.0f;
+    if (tiny(x)) {
+      coltag[mat * groups + n / kTagCols] = gen;
+      tagany[0] = gen;
+    }
+    tile[j][threadIdx.x] = x;
   }
   __syncthreads();
   const int64_t KS = SEGS * Kp;
@@ -89,7 +114,7 @@ __global__ void split_bt_kernel(const float* __restrict__ B, float* __restrict__
     const int64_t n = n0 + j, k = k0 + threadIdx.x;
     if (n < N && k < Kp) {
       float hi, lo;
-      split(tile[threadIdx.x][j], hi, lo);
+      split(tile[threadIdx.x][j], hi, lo);  // tiny values were tagged on load
       float* o = Bt + (mat * N + n) * KS + k;
       o[0] = hi;
       o[Kp] = lo;
@@ -247,13 +272,23 @@ constexpr int GEMM_THREADS = 32 * (2 + ACC_WARPS);
 struct Tf32Params {
   float* C;
   float* partial;  // ksplit > 1: per-split fp32 tiles, [ksplit][batch][M][N]
-  int64_t M, N;
+  const float* A;  // the caller's operands (non-finite repair)
+  const float* B;
+  int64_t M, N, K;
   int kblocks;  // K' / 32
   int tiles_m, tiles_n;
   int64_t tiles;  // tiles_m * tiles_n * batch
   int ksplit;     // K-slice ranges per tile (work items = tiles * ksplit)
   BatchMap map;
   int* err;
+  unsigned int* nf;          // non-finite tile marks (pb_internal.cuh)
+  int64_t nf_tm, nf_tn;      // kNonFiniteTile tiles along M and N
+  int repair_inline;         // recompute flagged outputs where they are written
+  unsigned int* tagany;      // generation if any operand of this launch is tagged
+  unsigned int* rowtag;      // per row of A (all matrices): generation if tiny
+  unsigned int* coltag;      // per kTagCols columns of each B matrix
+  int64_t cgroups;           // ceil(N / kTagCols)
+  unsigned int gen;          // this launch's generation
 };
 
 // K-slice range [kb0, kb1) of split `s`.
@@ -294,6 +329,91 @@ __device__ __forceinline__ TileCoord tile_coord(const Tf32Params& p, int64_t t) 
   c.m_tile = first_m + in_group % gm;
   c.n_tile = in_group / gm;
   return c;
+}
+
+// Above these K a flagged output is not recomputed where it is written but
+// its tile is marked for the tiled repair launch: in the epilogue the
+// pipeline waits for the recomputation (bounded by kTimeoutNs); in the
+// split reduction each flagged element is a strided dot product of its own.
+constexpr int64_t kInlineRepairMaxK = 1 << 18;
+constexpr int64_t kReduceRepairMaxK = 1 << 13;
+
+// Row segment of COLS values from col0: plain stores, float4 when aligned.
+template <int COLS>
+__device__ __forceinline__ void store_row(float* dst, const float (&v)[COLS], int64_t col0,
+                                          int64_t N) {
+  if ((N % 4) == 0 && col0 + COLS <= N) {
+    float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int j = 0; j < COLS / 4; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < COLS; ++j)
+      if (col0 + j < N) dst[j] = v[j];
+  }
+}
+
+__device__ __forceinline__ bool nonfinite(float x) { return !(fabsf(x) <= FLT_MAX); }
+
+// Recomputes C[row, col0 .. col0+ncols) with sequential float32 FMA over the
+// caller's operands: the IEEE classes of +-Inf and NaN results.  Kept out of
+// line so the accumulator registers of the hot loop are not affected.
+__device__ __noinline__ void repair_row(const float* arow, const float* bcol, float* crow,
+                                        int64_t N, int64_t K, int ncols) {
+  for (int j = 0; j < ncols; ++j) {
+    float s = 0.0f;
+    for (int64_t k = 0; k < K; ++k) s = fmaf(arow[k], bcol[k * N + j], s);
+    crow[j] = s;
+  }
+}
+
+// The row segment (row, col0 ..) of batch entry bz was written with a
+// non-finite value or from a tiny operand: recompute it now, or mark its tile
+// for the repair launch.
+__device__ __forceinline__ void handle_nonfinite(const Tf32Params& p, int64_t bz, int64_t row,
+                                                 int64_t col0, int cols) {
+  if (!p.repair_inline) {
+    mark_nonfinite(p.nf, bz, row, col0, p.nf_tm, p.nf_tn);
+    return;
+  }
+  int64_t ao, bo;
+  batch_offsets(p.map, bz, &ao, &bo);
+  repair_row(p.A + (ao * p.M + row) * p.K, p.B + bo * p.K * p.N + col0,
+             p.C + (bz * p.M + row) * p.N + col0, p.N, p.K, (int)min((int64_t)cols, p.N - col0));
+}
+
+// True if row `row` of batch entry bz or one of the columns col0 .. +COLS
+// touches an operand tagged as tiny in this launch.
+template <int COLS>
+__device__ __forceinline__ bool tagged(const Tf32Params& p, int64_t bz, int64_t row, int64_t col0) {
+  int64_t ao, bo;
+  batch_offsets(p.map, bz, &ao, &bo);
+  bool t = __ldcg(p.rowtag + ao * p.M + row) == p.gen;
+  const unsigned int* ct = p.coltag + bo * p.cgroups + col0 / kTagCols;
+  const int64_t last = min(col0 + COLS, p.N) - 1;
+  for (int64_t g = 0; g <= last / kTagCols - col0 / kTagCols; ++g) t |= __ldcg(ct + g) == p.gen;
+  return t;
+}
+
+// Epilogue of one work item: this thread's row segment (row, col0 ..
+// col0+COLS) of the tile.  With K split, the split's partial tile is stored
+// for splitk_reduce_kernel; otherwise the values are final.
+template <int COLS>
+__device__ __forceinline__ void finish_item(const Tf32Params& p, const TileCoord& tc, int split,
+                                            int64_t row, int64_t col0, const float (&acc)[COLS]) {
+  if (row >= p.M) return;
+  if (p.ksplit > 1) {
+    const int64_t batch = p.tiles / ((int64_t)p.tiles_m * p.tiles_n);
+    store_row<COLS>(p.partial + split * batch * p.M * p.N + (tc.bz * p.M + row) * p.N + col0, acc,
+                    col0, p.N);
+    return;
+  }
+  bool bad = false;
+#pragma unroll
+  for (int j = 0; j < COLS; ++j) bad |= nonfinite(acc[j]);
+  store_row<COLS>(p.C + (tc.bz * p.M + row) * p.N + col0, acc, col0, p.N);
+  if (__ldcg(p.tagany) == p.gen) bad |= tagged<COLS>(p, tc.bz, row, col0);
+  if (bad) handle_nonfinite(p, tc.bz, row, col0, COLS);
 }
 
 template <int BN>
@@ -339,6 +459,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   const int64_t items = p.tiles * p.ksplit;
+  // The non-finite repair launch may be scheduled now; it waits for this grid.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     if (lane == 0) {
@@ -458,25 +580,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (lane == 0) mbar_arrive(acce0 + 8 * buf);
       }
       if (!ok || *abort_flag) break;
-      // Store this thread's row segment of the finished tile (or of this
-      // split's partial tile, summed later by splitk_reduce_kernel).
-      const int64_t row = tc.m_tile * BM + quad * 32 + lane;
-      if (row < p.M) {
-        const int64_t col0 = tc.n_tile * BN + half * COLS;
-        const int64_t batch = p.tiles / ((int64_t)p.tiles_m * p.tiles_n);
-        float* dst_base = p.ksplit == 1 ? p.C : p.partial + split * batch * p.M * p.N;
-        float* crow = dst_base + tc.bz * p.M * p.N + row * p.N + col0;
-        if ((p.N % 4) == 0 && col0 + COLS <= p.N) {
-          float4* dst = reinterpret_cast<float4*>(crow);
-#pragma unroll
-          for (int j = 0; j < COLS / 4; ++j)
-            dst[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < COLS; ++j)
-            if (col0 + j < p.N) crow[j] = acc[j];
-        }
-      }
+      finish_item<COLS>(p, tc, split, tc.m_tile * BM + quad * 32 + lane,
+                        tc.n_tile * BN + half * COLS, acc);
     }
   }
 
@@ -528,16 +633,13 @@ struct FSmem {
   static constexpr int TOTAL = FSTAGES * STAGE + 1024 + 256;
 };
 
-// hi = round-to-nearest tf32 of x (ties away), lo = tf32(x - hi); integer
-// rounding keeps the conversion off the slower conversion pipe.  Non-finite x
-// keeps hi = x and lo = 0, as in the pre-split pass.
+// hi = round-to-nearest tf32 of x (ties away), lo = tf32(x - hi), in
+// integer arithmetic (off the slower conversion pipe) and without branches.
+// A non-finite x gives hi = x and lo = NaN, and a magnitude within 2^-12 of
+// FLT_MAX rounds hi up to Inf: both make every output they touch non-finite,
+// and the epilogue recomputes those.
 __device__ __forceinline__ void split_bits(float x, float& hi, float& lo) {
   const uint32_t b = __float_as_uint(x);
-  if ((b & 0x7f800000u) == 0x7f800000u) {
-    hi = x;
-    lo = 0.0f;
-    return;
-  }
   hi = __uint_as_float((b + 0x1000u) & 0xffffe000u);
   lo = __uint_as_float((__float_as_uint(x - hi) + 0x1000u) & 0xffffe000u);
 }
@@ -585,6 +687,8 @@ __global__ void __launch_bounds__(FUSED_THREADS, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   const int64_t items = p.tiles * p.ksplit;
+  // The non-finite repair launch may be scheduled now; it waits for this grid.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     if (lane == 0) {
@@ -705,6 +809,10 @@ __global__ void __launch_bounds__(FUSED_THREADS, 1)
       const int split = (int)(w % p.ksplit);
       int kb0, kb1;
       split_range(p, split, kb0, kb1);
+      int64_t ao, bo;
+      batch_offsets(p.map, tc.bz, &ao, &bo);
+      // Row of A (over all matrices) of the first row of this tile.
+      const int64_t arow0 = ao * p.M + tc.m_tile * BM;
 #pragma unroll
       for (int i = 0; i < COLS; ++i) acc[i] = 0.0f;
       for (int kb = kb0; kb < kb1 && ok; ++kb, ++g) {
@@ -725,6 +833,16 @@ __global__ void __launch_bounds__(FUSED_THREADS, 1)
           split_bits(v.w, h.w, l.w);
           a[i] = h;
           alo[i] = l;
+          // Zero or tiny among the four (smallest exponent field below 2^-57):
+          // tag the row if one is a nonzero tiny value.  128-byte tile rows;
+          // the swizzle only moves 16-byte chunks within a row.
+          const uint32_t e = min(min(__float_as_uint(v.x) & 0x7f800000u, __float_as_uint(v.y) & 0x7f800000u),
+                                 min(__float_as_uint(v.z) & 0x7f800000u, __float_as_uint(v.w) & 0x7f800000u));
+          if (e < (kTinyExp << 23) && (tiny(v.x) || tiny(v.y) || tiny(v.z) || tiny(v.w))) {
+            p.rowtag[arow0 + i / (BK / 4)] = p.gen;
+            p.tagany[0] = p.gen;
+            __threadfence();  // visible before this slice is marked ready
+          }
         }
         // Generic-proxy stores must be visible to the tensor core (async proxy).
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -737,23 +855,8 @@ __global__ void __launch_bounds__(FUSED_THREADS, 1)
       if (!is_acc) continue;
       if (ok) promote();  // the tile's last chunk
       if (!ok || *abort_flag) break;
-      const int64_t row = tc.m_tile * BM + quad * 32 + lane;
-      if (row < p.M) {
-        const int64_t col0 = tc.n_tile * FBN + half * COLS;
-        const int64_t batch = p.tiles / ((int64_t)p.tiles_m * p.tiles_n);
-        float* dst_base = p.ksplit == 1 ? p.C : p.partial + split * batch * p.M * p.N;
-        float* crow = dst_base + tc.bz * p.M * p.N + row * p.N + col0;
-        if ((p.N % 4) == 0 && col0 + COLS <= p.N) {
-          float4* dst = reinterpret_cast<float4*>(crow);
-#pragma unroll
-          for (int j = 0; j < COLS / 4; ++j)
-            dst[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < COLS; ++j)
-            if (col0 + j < p.N) crow[j] = acc[j];
-        }
-      }
+      finish_item<COLS>(p, tc, split, tc.m_tile * BM + quad * 32 + lane,
+                        tc.n_tile * FBN + half * COLS, acc);
     }
   }
 
@@ -771,17 +874,24 @@ __global__ void __launch_bounds__(FUSED_THREADS, 1)
   }
 }
 
-// C = sum over splits of the partial tiles, in split order (deterministic).
-__global__ void splitk_reduce_kernel(const float* __restrict__ partial, float* __restrict__ C,
-                                     int64_t count, int ksplit) {
+// C = sum over splits of the partial tiles, in split order (deterministic);
+// flagged outputs (non-finite, or touching a tagged operand) are recomputed.
+__global__ void splitk_reduce_kernel(const Tf32Params p, int64_t count) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const bool tags = __ldcg(p.tagany) == p.gen;
+  auto check = [&](int64_t i, float v) {
+    const int64_t bz = i / (p.M * p.N), r = i % (p.M * p.N);
+    if (nonfinite(v) || (tags && tagged<1>(p, bz, r / p.N, r % p.N)))
+      handle_nonfinite(p, bz, r / p.N, r % p.N, 1);
+  };
   if ((count & 3) == 0) {
     const int64_t n4 = count / 4;
-    const float4* p4 = reinterpret_cast<const float4*>(partial);
-    float4* c4 = reinterpret_cast<float4*>(C);
+    const float4* p4 = reinterpret_cast<const float4*>(p.partial);
+    float4* c4 = reinterpret_cast<float4*>(p.C);
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
       float4 s = p4[i];
-      for (int k = 1; k < ksplit; ++k) {
+      for (int k = 1; k < p.ksplit; ++k) {
         const float4 v = p4[k * n4 + i];
         s.x += v.x;
         s.y += v.y;
@@ -789,14 +899,30 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, float* _
         s.w += v.w;
       }
       c4[i] = s;
+      if (tags || nonfinite(s.x) || nonfinite(s.y) || nonfinite(s.z) || nonfinite(s.w)) {
+        check(4 * i, s.x);
+        check(4 * i + 1, s.y);
+        check(4 * i + 2, s.z);
+        check(4 * i + 3, s.w);
+      }
     }
   } else {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += stride) {
-      float s = partial[i];
-      for (int k = 1; k < ksplit; ++k) s += partial[k * count + i];
-      C[i] = s;
+      float s = p.partial[i];
+      for (int k = 1; k < p.ksplit; ++k) s += p.partial[k * count + i];
+      p.C[i] = s;
+      check(i, s);
     }
   }
+}
+
+int launch_reduce(Device* d, const Tf32Params& p, int64_t count) {
+  int64_t blocks = ceil_div(count / 4 + 1, (int64_t)256);
+  const int64_t cap = (int64_t)d->sm_count * 8;
+  if (blocks > cap) blocks = cap;
+  splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, d->stream>>>(p, count);
+  PB_LAUNCHED(d);
+  return PB_OK;
 }
 
 int encode_kmajor(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols, int box_rows) {
@@ -831,6 +957,32 @@ int launch_tf32(Device* d, const CUtensorMap& ma, const CUtensorMap& mb, const T
   return PB_OK;
 }
 
+// Operands and non-finite handling of a launch (after p.ksplit is set); the
+// tile marks of the repair launch live in the zeroed counter words.
+int finish_setup(Device* d, Tf32Params& p, int64_t batch, int64_t M, int64_t N, int64_t K,
+                 const float* A, const float* B) {
+  p.A = A;
+  p.B = B;
+  p.K = K;
+  p.repair_inline = K <= (p.ksplit > 1 ? kReduceRepairMaxK : kInlineRepairMaxK);
+  p.nf_tm = ceil_div(M, (int64_t)kNonFiniteTile);
+  p.nf_tn = ceil_div(N, (int64_t)kNonFiniteTile);
+  PB_CHECK(counters(d, 2 + (size_t)(batch * p.nf_tm * p.nf_tn), &p.nf));
+  return PB_OK;
+}
+
+// Operand tag words of a launch: the any word, rows of A, then column groups
+// of each B.
+int tag_setup(Device* d, Tf32Params& p, int64_t rows_a, int64_t nB, int64_t N) {
+  p.cgroups = ceil_div(N, (int64_t)kTagCols);
+  unsigned int* tags;
+  PB_CHECK(operand_tags(d, (size_t)(1 + rows_a + nB * p.cgroups), &tags, &p.gen));
+  p.tagany = tags;
+  p.rowtag = tags + 1;
+  p.coltag = tags + 1 + rows_a;
+  return PB_OK;
+}
+
 int64_t matrices_used(const BatchMap& m, bool a) {
   int64_t last = 0;
   for (int i = 0; i < m.ndim; ++i) last += (m.shape[i] - 1) * (a ? m.a_stride[i] : m.b_stride[i]);
@@ -860,17 +1012,18 @@ int gemm_f32_fused(Device* d, const BatchMap& map, int64_t batch, int64_t M, int
   void* ws;
   PB_CHECK(scratch(d, bytes_b + bytes_p, &ws));
   float* Bt = (float*)ws;
+  Tf32Params p;
+  PB_CHECK(tag_setup(d, p, rows_a, nB, N));
   const int64_t gx = ceil_div(N, (int64_t)32), gy = ceil_div(Kp, (int64_t)32);
   if (gx > INT32_MAX || gy > 65535 || nB > 65535)
     PB_FAIL(PB_ERR_UNSUPPORTED, "B operand too large for the split grid");
   split_bt_kernel<2><<<dim3((unsigned)gx, (unsigned)gy, (unsigned)nB), dim3(32, 8), 0, d->stream>>>(
-      B, Bt, K, N, Kp);
+      B, Bt, K, N, Kp, p.coltag, p.cgroups, p.tagany, p.gen);
   PB_LAUNCHED(d);
 
   CUtensorMap ma, mb;
   PB_CHECK(encode_kmajor(&ma, A, rows_a, K, BM));
   PB_CHECK(encode_kmajor(&mb, Bt, rows_b, 2 * Kp, FBN));
-  Tf32Params p;
   p.C = C;
   p.partial = ksplit > 1 ? (float*)((char*)ws + bytes_b) : nullptr;
   p.M = M;
@@ -882,6 +1035,7 @@ int gemm_f32_fused(Device* d, const BatchMap& map, int64_t batch, int64_t M, int
   p.ksplit = ksplit;
   p.map = map;
   p.err = d->err_dev;
+  PB_CHECK(finish_setup(d, p, batch, M, N, K, A, B));
   const int smem = FSmem::TOTAL;
   static bool configured = false;
   if (!configured) {
@@ -893,15 +1047,9 @@ int gemm_f32_fused(Device* d, const BatchMap& map, int64_t batch, int64_t M, int
   const int64_t grid = items < d->sm_count ? items : d->sm_count;
   tf32x3_fused_kernel<<<(unsigned)grid, FUSED_THREADS, smem, d->stream>>>(ma, mb, p, (int)Kp);
   PB_LAUNCHED(d);
-  if (ksplit > 1) {
-    const int64_t count = batch * M * N;
-    int64_t blocks = ceil_div(count / 4 + 1, (int64_t)256);
-    const int64_t cap = (int64_t)d->sm_count * 8;
-    if (blocks > cap) blocks = cap;
-    splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, d->stream>>>(p.partial, C, count, ksplit);
-    PB_LAUNCHED(d);
-  }
-  return PB_OK;
+  if (ksplit > 1) PB_CHECK(launch_reduce(d, p, batch * M * N));
+  if (p.repair_inline) return PB_OK;
+  return gemm_nonfinite_repair_f32(d, map, batch, M, N, K, A, B, C, p.nf);
 }
 
 // Products with at most this many columns take the shared-memory split
@@ -946,7 +1094,7 @@ int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
   const int64_t tiles = (int64_t)tiles_m * ceil_div(N, (int64_t)BN) * batch;
   const int kblocks = (int)(K3 / BK);
   // Too few tiles to occupy every SM: split K' into ranges of at least two
-  // promotion chunks each, fp32 partial tiles summed by a second kernel.
+  // promotion chunks each; fp32 partial tiles summed by a second kernel.
   int ksplit = 1;
   if (tiles < d->sm_count) {
     ksplit = (int)(d->sm_count / tiles);
@@ -959,26 +1107,28 @@ int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
   PB_CHECK(scratch(d, bytes_a + bytes_b + bytes_p, &ws));
   float* Ap = (float*)ws;
   float* Bt = (float*)((char*)ws + bytes_a);
+  Tf32Params p;
+  PB_CHECK(tag_setup(d, p, rows_a, nB, N));
 
   {
     const int64_t total = rows_a * Kp;
     int64_t blocks = ceil_div(total, (int64_t)256);
     const int64_t cap = (int64_t)d->sm_count * 16;
     if (blocks > cap) blocks = cap;
-    split_a_kernel<<<(unsigned)blocks, 256, 0, d->stream>>>(A, Ap, rows_a, K, Kp);
+    split_a_kernel<<<(unsigned)blocks, 256, 0, d->stream>>>(A, Ap, rows_a, K, Kp, p.rowtag,
+                                                            p.tagany, p.gen);
     PB_LAUNCHED(d);
     const int64_t gx = ceil_div(N, (int64_t)32), gy = ceil_div(Kp, (int64_t)32);
     if (gx > INT32_MAX || gy > 65535 || nB > 65535)
       PB_FAIL(PB_ERR_UNSUPPORTED, "B operand too large for the split grid");
     split_bt_kernel<3><<<dim3((unsigned)gx, (unsigned)gy, (unsigned)nB), dim3(32, 8), 0, d->stream>>>(
-        B, Bt, K, N, Kp);
+        B, Bt, K, N, Kp, p.coltag, p.cgroups, p.tagany, p.gen);
     PB_LAUNCHED(d);
   }
 
   CUtensorMap ma, mb;
   PB_CHECK(encode_kmajor(&ma, Ap, rows_a, K3, BM));
   PB_CHECK(encode_kmajor(&mb, Bt, rows_b, K3, BN));
-  Tf32Params p;
   p.C = C;
   p.partial = ksplit > 1 ? (float*)((char*)ws + bytes_a + bytes_b) : nullptr;
   p.M = M;
@@ -990,16 +1140,11 @@ int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
   p.ksplit = ksplit;
   p.map = map;
   p.err = d->err_dev;
+  PB_CHECK(finish_setup(d, p, batch, M, N, K, A, B));
   PB_CHECK(BN == 256 ? launch_tf32<256>(d, ma, mb, p) : launch_tf32<128>(d, ma, mb, p));
-  if (ksplit > 1) {
-    const int64_t count = batch * M * N;
-    int64_t blocks = ceil_div(count / 4 + 1, (int64_t)256);
-    const int64_t cap = (int64_t)d->sm_count * 8;
-    if (blocks > cap) blocks = cap;
-    splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, d->stream>>>(p.partial, C, count, ksplit);
-    PB_LAUNCHED(d);
-  }
-  return PB_OK;
+  if (ksplit > 1) PB_CHECK(launch_reduce(d, p, batch * M * N));
+  if (p.repair_inline) return PB_OK;
+  return gemm_nonfinite_repair_f32(d, map, batch, M, N, K, A, B, C, p.nf);
 }
 
 }  // namespace pb

@@ -73,6 +73,12 @@ struct Device {
   // Every kernel that uses them leaves them at zero again.
   unsigned int* counters = nullptr;
   size_t counters_n = 0;
+  // Operand tags of the 3xTF32 GEMM: a word per row of A / column group of B
+  // holding the generation of the last launch that found a tiny value there.
+  // Generations only grow, so the tags never need clearing.
+  unsigned int* tags = nullptr;
+  size_t tags_n = 0;
+  unsigned int tag_gen = 0;
   // Kernel error word in mapped, pinned host memory (no copy needed to read it).
   int* err_host = nullptr;
   int* err_dev = nullptr;
@@ -99,6 +105,8 @@ int enter(pb_ctx* ctx, int dev, Device** out);
 int scratch(Device* d, size_t bytes, void** out);
 // Ensure at least `n` zeroed counters; returns the pointer.
 int counters(Device* d, size_t n, unsigned int** out);
+// Ensure at least `n` operand tag words; returns them and a fresh generation.
+int operand_tags(Device* d, size_t n, unsigned int** out, unsigned int* gen);
 // Driver entry point for cuTensorMapEncodeTiled (resolved once).
 int tensor_map_encoder(void** fn);
 
@@ -129,6 +137,33 @@ __host__ __device__ inline void batch_offsets(const BatchMap& m, int64_t b, int6
 }
 
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// ------------------------------------------- non-finite GEMM outputs --
+//
+// The 3xTF32 split gives a non-finite value x the parts hi = x, lo = 0, so a
+// cross term lo * (+-Inf) is 0 * Inf = NaN where IEEE arithmetic (and the
+// reference's float32 GEMM) yields +-Inf; a magnitude within 2^-12 of
+// FLT_MAX can also round its hi part up to Inf.  Every such output is
+// non-finite, so the tcgen05 epilogues mark the kNonFiniteTile-square tile
+// of each non-finite output in a zeroed counter array laid out as
+//   nf[0]      any tile marked
+//   nf[1]      arrival counter of the repair kernel
+//   nf[2 + t]  tile t = (batch * tiles_m + m / kNonFiniteTile) * tiles_n + n / kNonFiniteTile
+// and a repair launch recomputes the marked tiles with float32 FMA from the
+// original operands, then returns every word to zero.
+constexpr int kNonFiniteTile = 128;
+
+__device__ __forceinline__ void mark_nonfinite(unsigned int* nf, int64_t bz, int64_t row,
+                                               int64_t col, int64_t tiles_m, int64_t tiles_n) {
+  nf[2 + (bz * tiles_m + row / kNonFiniteTile) * tiles_n + col / kNonFiniteTile] = 1u;
+  nf[0] = 1u;
+}
+
+// Launched right after the kernels that mark (programmatic dependent launch:
+// it waits for them on the device); returns at once when nothing is marked.
+int gemm_nonfinite_repair_f32(Device* d, const BatchMap& map, int64_t batch, int64_t M, int64_t N,
+                              int64_t K, const float* A, const float* B, float* C,
+                              unsigned int* nf);
 
 // ------------------------------------------------------- device helpers --
 

@@ -61,6 +61,24 @@ int counters(Device* d, size_t n, unsigned int** out) {
   return PB_OK;
 }
 
+int operand_tags(Device* d, size_t n, unsigned int** out, unsigned int* gen) {
+  if (n > d->tags_n || d->tag_gen == UINT32_MAX) {
+    const size_t want = n > d->tags_n ? (n < 65536 ? 65536 : n) : d->tags_n;
+    if (want > d->tags_n) {
+      if (d->tags) PB_CUDA(cudaFreeAsync(d->tags, d->stream));
+      d->tags = nullptr;
+      d->tags_n = 0;
+      PB_CUDA(cudaMallocAsync((void**)&d->tags, want * sizeof(unsigned int), d->pool, d->stream));
+      d->tags_n = want;
+    }
+    PB_CUDA(cudaMemsetAsync(d->tags, 0, d->tags_n * sizeof(unsigned int), d->stream));
+    d->tag_gen = 0;
+  }
+  *out = d->tags;
+  *gen = ++d->tag_gen;
+  return PB_OK;
+}
+
 int tensor_map_encoder(void** fn) {
   static std::once_flag once;
   static void* encoder = nullptr;
@@ -83,6 +101,7 @@ static void release_device(Device* d) {
   if (d->stream) cudaStreamSynchronize(d->stream);
   if (d->scratch) cudaFreeAsync(d->scratch, d->stream);
   if (d->counters) cudaFreeAsync(d->counters, d->stream);
+  if (d->tags) cudaFreeAsync(d->tags, d->stream);
   if (d->stream) cudaStreamSynchronize(d->stream);
   if (d->t0) cudaEventDestroy(d->t0);
   if (d->t1) cudaEventDestroy(d->t1);
@@ -91,6 +110,8 @@ static void release_device(Device* d) {
   if (d->pool) cudaMemPoolTrimTo(d->pool, 0);
   d->scratch = nullptr;
   d->counters = nullptr;
+  d->tags = nullptr;
+  d->tags_n = 0;
   d->err_host = d->err_dev = nullptr;
   d->stream = nullptr;
 }
@@ -100,6 +121,9 @@ static int check_kernel_error(Device* d) {
   if (d->err_host && *(volatile int*)d->err_host != KERR_NONE) {
     int code = *(volatile int*)d->err_host;
     *(volatile int*)d->err_host = KERR_NONE;
+    // An aborted kernel may have left arrival counters or marks behind; the
+    // stream is idle here, so zero them before the next launch reads them.
+    if (d->counters) cudaMemsetAsync(d->counters, 0, d->counters_n * sizeof(unsigned int), d->stream);
     PB_FAIL(PB_ERR_DEVICE, "kernel reported error %d (%s)", code,
             code == KERR_WAIT_TIMEOUT ? "bounded wait timed out" : "bad argument");
   }
@@ -329,6 +353,9 @@ int pb_trim(pb_ctx* ctx, int dev) {
   if (d->scratch) PB_CUDA(cudaFreeAsync(d->scratch, d->stream));
   d->scratch = nullptr;
   d->scratch_bytes = 0;
+  if (d->tags) PB_CUDA(cudaFreeAsync(d->tags, d->stream));
+  d->tags = nullptr;
+  d->tags_n = 0;
   PB_CUDA(cudaStreamSynchronize(d->stream));
   PB_CUDA(cudaMemPoolTrimTo(d->pool, 0));
   return PB_OK;

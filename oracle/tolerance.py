@@ -1,7 +1,12 @@
 """Acceptance bounds of the b200 path against the NumPy-backend oracle.
 
 * GEMM/GEMV/DOT, elementwise: |C - C_ref| <= 4 * K * u * (|A| |B|)_ij with
-  u = 2^-24 (float32) or 2^-53 (float64); |A||B| is formed in float64.
+  u = 2^-24 (float32) or 2^-53 (float64); |A||B| is formed in float64.  Plus
+  the underflow term of the same error analysis, K * eta with eta the
+  smallest subnormal: a product in the subnormal range is rounded to
+  multiples of eta (an error of up to eta/2 that no relative bound covers),
+  so two correct implementations can differ by K * eta there.  For outputs
+  in the normal range the term is below 1e-41 (float32).
 * Norm, relative: |n - n_ref| <= 8 * u * |n_ref| (NaN matches NaN, Inf Inf).
   Where the NumPy reference is itself further than that from the exact value
   (float32 normalisation and squaring, src/openpacho/_norm.py:47-49), an
@@ -25,11 +30,12 @@ def unit_roundoff(dtype) -> float:
 
 
 def gemm_bound(a: np.ndarray, b: np.ndarray, dtype=None, extra_u: float = 0.0) -> np.ndarray:
-    """Elementwise (4*K + extra_u)*u*(|A||B|) for ``a @ b`` (broadcasting like matmul)."""
+    """Elementwise (4*K + extra_u)*u*(|A||B|) + K*eta for ``a @ b`` (broadcasting like matmul)."""
     dtype = np.dtype(dtype or np.result_type(a.dtype, b.dtype))
     k = a.shape[-1]
     absprod = np.abs(a.astype(np.float64)) @ np.abs(b.astype(np.float64))
-    return (4.0 * max(k, 1) + extra_u) * unit_roundoff(dtype) * absprod
+    eta = float(np.finfo(dtype).smallest_subnormal)
+    return (4.0 * max(k, 1) + extra_u) * unit_roundoff(dtype) * absprod + max(k, 1) * eta
 
 
 def gemm_violations(c: np.ndarray, c_ref: np.ndarray, a: np.ndarray, b: np.ndarray,

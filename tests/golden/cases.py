@@ -117,6 +117,37 @@ def cancellation_case():
     return "cancel941_float32", left, right
 
 
+# tests/test_rectangular_gemm.py:88-101 (Inf, NaN and the smallest subnormal
+# against [0, 1, -1] through a skinny GEMM), then the same kinds of special
+# values at tensor-core shapes: Inf * 0, Inf - Inf, a NaN row, a signed-Inf
+# column, a broadcast batch, and an operand at the largest finite magnitude.
+def special_value_cases():
+    for dtype in DTYPES:
+        left = np.zeros((33, 4081), dtype=dtype)
+        right = np.zeros((4081, 257), dtype=dtype)
+        left[0, 0], left[1, 0] = np.inf, np.nan
+        left[2, 0] = np.nextafter(dtype(0), dtype(1))
+        right[0, :3] = [0, 1, -1]
+        yield f"special_rect_{np.dtype(dtype).name}", left, right
+    for dtype in DTYPES:
+        rng = np.random.default_rng(12)
+        a = rng.standard_normal((260, 96)).astype(dtype)
+        b = rng.standard_normal((96, 140)).astype(dtype)
+        a[0, 5], b[5, 7] = np.inf, 0.0           # row 0 +-Inf; (0, 7) is Inf * 0
+        b[9, 3], a[4, 9] = -np.inf, 0.0          # column 3 +-Inf; (4, 3) is 0 * -Inf
+        a[11, 2] = np.nan                        # row 11 NaN
+        a[13, 20], a[13, 21] = np.inf, -np.inf   # row 13 Inf - Inf where both b > 0
+        b[20, :] = np.abs(b[20, :]) + 0.5
+        b[21, :] = np.abs(b[21, :]) + 0.5
+        a[17, 30], b[30, :] = np.finfo(dtype).max, 2.0**-10  # finite products near the top
+        yield f"special_tc_{np.dtype(dtype).name}", a, b
+        a = rng.standard_normal((3, 130, 64)).astype(dtype)
+        b = rng.standard_normal((64, 136)).astype(dtype)
+        a[1, 7, 3], a[2, 129, 0] = np.inf, np.nan
+        b[10, 135] = -np.inf
+        yield f"special_batched_{np.dtype(dtype).name}", a, b
+
+
 # tests/test_cuda_gemv.py:195-222 (exact cancellation, signed zero, Inf/NaN rows).
 def signed_cases():
     for dtype in DTYPES:

@@ -39,7 +39,7 @@ def main() -> int:
         meta[name] = {"kind": "matmul", "inputs": cases.digest(a, b)}
 
     for gen in (cases.matmul_cases, cases.empty_cases, cases.batched_cases, cases.gemv_cases,
-                cases.dot_cases, cases.signed_cases):
+                cases.dot_cases, cases.signed_cases, cases.special_value_cases):
         for name, a, b in gen():
             record_matmul(name, a, b)
     name, a, b = cases.cancellation_case()

@@ -23,7 +23,8 @@ pytestmark = pytest.mark.gpu
 
 
 def _matmul_cases():
-    for gen in (cases.matmul_cases, cases.batched_cases, cases.gemv_cases, cases.dot_cases):
+    for gen in (cases.matmul_cases, cases.batched_cases, cases.gemv_cases, cases.dot_cases,
+                cases.special_value_cases):
         yield from gen()
     yield cases.cancellation_case()
 
@@ -122,6 +123,7 @@ def _gemm_shapes():
     for name, a, b in cases.batched_cases():
         if a.ndim >= 2 and b.ndim >= 2 and a.size and b.size:
             yield name, a, b
+    yield from cases.special_value_cases()
     rng = np.random.default_rng(11)
     for m, n, k in ((128, 128, 32), (129, 255, 33), (300, 520, 97), (1, 300, 64), (257, 1, 40),
                     (64, 64, 1), (200, 136, 1000)):
@@ -143,7 +145,8 @@ def test_every_gemm_kernel_on_every_shape(b200, algo, case):
     if algo == _lib.PB_GEMM_DMMA:
         a, b = a.astype(np.float64), b.astype(np.float64)
     got = _call_gemm_ex(b200, a, b, algo)
-    want = numpy_backend.matmul(a, b)
+    with np.errstate(all="ignore"):
+        want = numpy_backend.matmul(a, b)
     # Forced 3xTF32 below K=32 carries the split error model (auto sends it to SIMT).
     extra = 16.0 if algo in tf32 and a.shape[-1] < 32 else 0.0
     assert tolerance.gemm_violations(got, want, a, b, extra_u=extra) == 0
@@ -185,6 +188,67 @@ def test_tf32x3_error_does_not_grow_with_k(b200, algo):
         got = _call_gemm_ex(b200, a, b, algo).astype(np.float64)
         errs.append(np.linalg.norm(got - ref) / np.linalg.norm(ref))
     assert errs[1] < 1e-6 and errs[1] < 3 * errs[0], errs
+
+
+@pytest.mark.parametrize("algo", [_lib.PB_GEMM_TF32X3_PRESPLIT, _lib.PB_GEMM_TF32X3_FUSED],
+                         ids=["presplit", "fused"])
+@pytest.mark.parametrize("shape", [(2048, 2048, 256), (2048, 1024, 256), (2, 600, 300, 1024)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_tf32x3_special_values_match_ieee(b200, algo, shape):
+    """Inf/NaN operands give the IEEE classes of the reference's float32 GEMM.
+
+    The 3xTF32 split turns some +-Inf results into NaN (0 * Inf cross terms);
+    those tiles are recomputed.  The first two shapes fill every SM without
+    splitting K, so the marks come from the tcgen05 epilogues; the batched
+    shape splits K, so they come from the split reduction."""
+    *batch, m, n, k = shape
+    rng = np.random.default_rng(21)
+    a = rng.standard_normal((*batch, m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    lead = (0,) * len(batch)
+    a[lead + (0, 5)], b[5, 7] = np.inf, 0.0
+    b[9, 3], a[lead + (4, 9)] = -np.inf, 0.0
+    a[lead + (m - 1, 2)] = np.nan
+    a[lead + (300, 20)], a[lead + (300, 21)] = np.inf, -np.inf
+    b[20, :] = np.abs(b[20, :]) + 0.5
+    b[21, :] = np.abs(b[21, :]) + 0.5
+    a[lead + (517, 30)], b[30, :] = np.finfo(np.float32).max, 2.0**-10
+    b[40, n - 1] = np.inf
+    if batch:
+        a[(batch[0] - 1, 77, 11)] = -np.inf
+    got = _call_gemm_ex(b200, a, b, algo)
+    with np.errstate(all="ignore"):
+        want = numpy_backend.matmul(a, b)
+    assert np.isnan(want).any() and np.isinf(want).any()
+    assert tolerance.gemm_violations(got, want, a, b) == 0
+    # The repair leaves its marks at zero: a clean product right after is exact.
+    a2 = rng.standard_normal((256, 128)).astype(np.float32)
+    b2 = rng.standard_normal((128, 256)).astype(np.float32)
+    assert tolerance.gemm_violations(_call_gemm_ex(b200, a2, b2, algo),
+                                     numpy_backend.matmul(a2, b2), a2, b2) == 0
+
+
+@pytest.mark.parametrize("algo", [_lib.PB_GEMM_TF32X3_PRESPLIT, _lib.PB_GEMM_TF32X3_FUSED],
+                         ids=["presplit", "fused"])
+@pytest.mark.parametrize("shape", [(2048, 2048, 256), (2048, 1024, 256), (2, 600, 300, 1024)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_tf32x3_tiny_operands_keep_float32_accuracy(b200, algo, shape):
+    """Operands below 2^-57 (products that would be subnormal on the tensor
+    core, subnormal inputs) still meet the float32 GEMM bound."""
+    *batch, m, n, k = shape
+    rng = np.random.default_rng(22)
+    a = rng.standard_normal((*batch, m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    lead = (0,) * len(batch)
+    a[lead + (5,)] *= np.float32(2.0**-70)         # tiny row ...
+    b[:, 9] *= np.float32(2.0**-70)                # ... times tiny column: subnormal products
+    a[lead + (m - 3,)] = (rng.standard_normal(k) * 2.0**-135).astype(np.float32)  # subnormals
+    b[17, n - 2] = np.float32(2.0**-140)
+    a[lead + (200, 17)] = np.float32(3.0)
+    got = _call_gemm_ex(b200, a, b, algo)
+    want = numpy_backend.matmul(a, b)
+    assert want[lead + (5, 9)] != 0 and abs(want[lead + (5, 9)]) < 2.0**-126
+    assert tolerance.gemm_violations(got, want, a, b) == 0
 
 
 def test_products_overwrite_nan_and_inf_destinations(b200, monkeypatch):

@@ -17,7 +17,7 @@ from oracle import exact, numpy_backend, tolerance
 
 def _matmul_inputs():
     for gen in (cases.matmul_cases, cases.empty_cases, cases.batched_cases, cases.gemv_cases,
-                cases.dot_cases, cases.signed_cases):
+                cases.dot_cases, cases.signed_cases, cases.special_value_cases):
         yield from gen()
     yield cases.cancellation_case()
 
