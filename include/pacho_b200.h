@@ -119,7 +119,8 @@ int pb_gemm(pb_ctx* ctx, int dev, int dtype, int batch_ndim, const int64_t* batc
  * PB_GEMM_SIMT (register-tiled CUDA-core FFMA/DFMA kernel), PB_GEMM_TF32X3
  * (float32; picks one of the two 3xTF32 kernels by size),
  * PB_GEMM_TF32X3_PRESPLIT (operands split into hi/lo copies in HBM first),
- * PB_GEMM_TF32X3_FUSED (A split in shared memory; needs K % 4 == 0) or
+ * PB_GEMM_TF32X3_FUSED (A split inside the kernel, into tensor memory;
+ * needs K % 4 == 0) or
  * PB_GEMM_DMMA (float64 only, FP64 tensor cores).  The
  * reference exposes the same kind of provider choice as
  * CUDABackend(blas="custom"|"cublas")

@@ -87,39 +87,78 @@ __global__ void split_a_kernel(const float* __restrict__ A, float* __restrict__ 
   }
 }
 
-// B (nmat x K x N) -> B't, transposed to K-major via a 32x32 shared tile so
-// both the read (along N) and the write (along K) coalesce.  SEGS = 3 writes
-// [hi | lo | hi] (nmat*N x 3Kp, for the pre-split GEMM), SEGS = 2 writes
-// [hi | lo] (nmat*N x 2Kp, for the GEMM that splits A in shared memory).
+// B (nmat x K x N) -> B't, transposed to K-major through shared memory.
+// SEGS = 3 writes [hi | lo | hi] (nmat*N x 3Kp, for the pre-split GEMM),
+// SEGS = 2 writes [hi | lo] (nmat*N x 2Kp, for the GEMM that splits A in
+// tensor memory).  A 256-thread block moves a 32 (k) x 64 (n) tile: float4
+// loads along n, and float4 stores along k, eight lanes per 128-byte row
+// segment, so both sides coalesce; the transposing shared-memory reads are
+// conflict-free (row pitch 65 words).  Grid: (ceil(N/64), Kp/32, nmat).
+constexpr int SPLIT_TK = 32, SPLIT_TN = 64;
+
 template <int SEGS>
-__global__ void split_bt_kernel(const float* __restrict__ B, float* __restrict__ Bt, int64_t K,
-                                int64_t N, int64_t Kp, unsigned int* coltag, int64_t groups,
-                                unsigned int* tagany, unsigned int gen) {
-  __shared__ float tile[32][33];
+__global__ void __launch_bounds__(256) split_bt_kernel(const float* __restrict__ B, float* __restrict__ Bt,
+                                                       int64_t K, int64_t N, int64_t Kp,
+                                                       unsigned int* coltag, int64_t groups,
+                                                       unsigned int* tagany, unsigned int gen) {
+  __shared__ float tile[SPLIT_TK][SPLIT_TN + 1];
   const int64_t mat = blockIdx.z;
-  const int64_t k0 = (int64_t)blockIdx.y * 32, n0 = (int64_t)blockIdx.x * 32;
+  const int64_t k0 = (int64_t)blockIdx.y * SPLIT_TK, n0 = (int64_t)blockIdx.x * SPLIT_TN;
   const float* src = B + mat * K * N;
-  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
-    const int64_t k = k0 + j, n = n0 + threadIdx.x;
-    const float x = (k < K && n < N) ? __ldg(src + k * N + n) : 0.0f;
-    if (tiny(x)) {
-      coltag[mat * groups + n / kTagCols] = gen;
-      tagany[0] = gen;
+  const int t = threadIdx.x;
+  const bool vec = (N % 4) == 0 && n0 + SPLIT_TN <= N && ((uintptr_t)src & 15) == 0;
+  bool tiny_seen = false;
+#pragma unroll
+  for (int pass = 0; pass < 2; ++pass) {
+    const int r = pass * 16 + (t >> 4), c = (t & 15) * 4;  // 16 float4 per 64-wide row
+    const int64_t k = k0 + r;
+    float v[4];
+    if (k < K && vec) {
+      const float4 q = __ldg(reinterpret_cast<const float4*>(src + k * N + n0 + c));
+      v[0] = q.x, v[1] = q.y, v[2] = q.z, v[3] = q.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = (k < K && n0 + c + j < N) ? __ldg(src + k * N + n0 + c + j) : 0.0f;
     }
-    tile[j][threadIdx.x] = x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      tile[r][c + j] = v[j];
+      tiny_seen |= tiny(v[j]);
+    }
+  }
+  if (tiny_seen) {
+    // Column group of each tiny value (rare: re-read the four values).
+    for (int pass = 0; pass < 2; ++pass) {
+      const int r = pass * 16 + (t >> 4), c = (t & 15) * 4;
+      for (int j = 0; j < 4; ++j)
+        if (tiny(tile[r][c + j])) {
+          coltag[mat * groups + (n0 + c + j) / kTagCols] = gen;
+          tagany[0] = gen;
+        }
+    }
   }
   __syncthreads();
   const int64_t KS = SEGS * Kp;
-  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
-    const int64_t n = n0 + j, k = k0 + threadIdx.x;
-    if (n < N && k < Kp) {
+  const int kq = t & 7;  // float4 along k: k = 4*kq .. 4*kq+3
+#pragma unroll
+  for (int pass = 0; pass < 2; ++pass) {
+    const int nl = pass * 32 + (t >> 3);
+    const int64_t n = n0 + nl;
+    if (n >= N) continue;
+    float4 h, l;
+    float* hp = &h.x;
+    float* lp = &l.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
       float hi, lo;
-      split(tile[threadIdx.x][j], hi, lo);  // tiny values were tagged on load
-      float* o = Bt + (mat * N + n) * KS + k;
-      o[0] = hi;
-      o[Kp] = lo;
-      if (SEGS == 3) o[2 * Kp] = hi;
+      split(tile[4 * kq + j][nl], hi, lo);
+      hp[j] = hi;
+      lp[j] = lo;
     }
+    float* o = Bt + (mat * N + n) * KS + k0 + 4 * kq;
+    *reinterpret_cast<float4*>(o) = h;
+    *reinterpret_cast<float4*>(o + Kp) = l;
+    if (SEGS == 3) *reinterpret_cast<float4*>(o + 2 * Kp) = h;
   }
 }
 
@@ -602,35 +641,42 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
 }
 
-// --------------------------------------------- GEMM with A split in smem --
+// ------------------------------------------ GEMM with A split into TMEM --
 //
 // Variant used when A's rows are 16-byte aligned (K % 4 == 0): A is loaded
-// raw by TMA and split into hi/lo inside shared memory, so A's bytes cross
-// HBM and L2 once (the pre-split path writes and re-reads A three times).
-// B keeps a pre-split K-major copy [hi | lo].  Per raw 32-element K-slice the
-// MMA thread issues lo*hi, hi*lo, hi*hi (small terms first) into the TMEM
-// accumulator, promoted to fp32 registers every FCHUNK slices (36 MMA steps).
-// Warps: 0 TMA producer, 1 MMA issuer, 2..11 split each landed A tile (raw A
-// -> hi in place + lo copy; the map is elementwise, so the 128-byte swizzle
-// needs no special handling), and 2..9 also promote and store (as the
-// accumulator warps of the pre-split kernel).
+// raw by TMA, and each 128 x 32 slice is split into hi/lo by the eight
+// accumulator warps straight into tensor memory, from where the MMAs read it
+// (A operand in TMEM, B in shared memory).  A's bytes cross HBM and L2 once;
+// shared memory holds only what TMA delivers (raw A and the pre-split B
+// [hi | lo], K-major), so FBN = 128 fits 4 stages and FBN = 64 fits 6.
+// Per slice the MMA thread issues lo*hi, hi*lo, hi*hi (small terms first)
+// into the TMEM accumulator, promoted to fp32 registers every FCHUNK slices
+// (36 MMA steps).
+// Warps: 0 TMA producer, 1 MMA issuer, 2..9 split A (warp w owns TMEM lanes
+// 32*(w%4).. and K half (w-2)/4 of each slice), promote and store.
+// TMEM columns: accumulators [0, 2*FBN), then for stage s A hi at
+// 2*FBN + 64*s and A lo 32 columns further.  A stage's A columns are free
+// once its full barrier fires: the TMA for slice g is only issued after the
+// MMAs of slice g - STAGES (the previous user of the columns) completed.
 
-constexpr int FBN = 128;
-constexpr int FSTAGES = 3;
 #ifndef PB_TF32_FCHUNK
 #define PB_TF32_FCHUNK 3
 #endif
 constexpr int FCHUNK = PB_TF32_FCHUNK;
-constexpr int F_ACC_WARPS = 8;
-constexpr int F_XFORM_WARPS = 2;
-constexpr int FUSED_THREADS = 32 * (2 + F_ACC_WARPS + F_XFORM_WARPS);
+constexpr int T_THREADS = 32 * (2 + 8);
 
-struct FSmem {
-  static constexpr int TILE = BM * BK * 4;  // 16 KiB: a 128 x 32 fp32 tile
-  static constexpr int A = 0, ALO = TILE, BHI = 2 * TILE, BLO = 3 * TILE;
-  static constexpr int STAGE = 4 * TILE;    // 64 KiB
-  static constexpr int TX_BYTES = 3 * TILE; // what TMA delivers per stage
-  static constexpr int TOTAL = FSTAGES * STAGE + 1024 + 256;
+template <int FBN>
+struct TSmem {
+  static constexpr int A_BYTES = BM * BK * 4;   // 16 KiB raw A slice
+  static constexpr int B_BYTES = FBN * BK * 4;  // B hi or B lo slice
+  static constexpr int A = 0, BHI = A_BYTES, BLO = A_BYTES + B_BYTES;
+  static constexpr int STAGE = A_BYTES + 2 * B_BYTES;
+  static constexpr int STAGES = FBN == 128 ? 4 : 6;
+  static constexpr int TOTAL = STAGES * STAGE + 1024 + 256;
+  static constexpr uint32_t ACOL = 2 * FBN;     // first A column in TMEM
+  static constexpr uint32_t TMEM_COLS = 512;
+  static_assert(ACOL + 64 * STAGES <= TMEM_COLS, "TMEM columns");
+  static_assert(8 * (3 * STAGES + 4) + 8 <= 256, "barrier area");
 };
 
 // hi = round-to-nearest tf32 of x (ties away), lo = tf32(x - hi), in
@@ -638,39 +684,61 @@ struct FSmem {
 // A non-finite x gives hi = x and lo = NaN, and a magnitude within 2^-12 of
 // FLT_MAX rounds hi up to Inf: both make every output they touch non-finite,
 // and the epilogue recomputes those.
-__device__ __forceinline__ void split_bits(float x, float& hi, float& lo) {
+__device__ __forceinline__ void split_bits(float x, uint32_t& hi, uint32_t& lo) {
   const uint32_t b = __float_as_uint(x);
-  hi = __uint_as_float((b + 0x1000u) & 0xffffe000u);
-  lo = __uint_as_float((__float_as_uint(x - hi) + 0x1000u) & 0xffffe000u);
+  hi = (b + 0x1000u) & 0xffffe000u;
+  lo = (__float_as_uint(x - __uint_as_float(hi)) + 0x1000u) & 0xffffe000u;
 }
 
-__global__ void __launch_bounds__(FUSED_THREADS, 1)
-    tf32x3_fused_kernel(const __grid_constant__ CUtensorMap map_a,
-                        const __grid_constant__ CUtensorMap map_b, Tf32Params p, int Kp) {
+// D (TMEM) += A (TMEM, 128 lanes x 8 columns at tmem_a) * B (smem descriptor).
+__device__ __forceinline__ void umma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+// 16 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+template <int FBN>
+__global__ void __launch_bounds__(T_THREADS, 1)
+    tf32x3_tmem_kernel(const __grid_constant__ CUtensorMap map_a,
+                       const __grid_constant__ CUtensorMap map_b, Tf32Params p, int Kp) {
+  using L = TSmem<FBN>;
+  constexpr int S = L::STAGES;
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023) & ~1023u;
   unsigned char* gbase = smem_raw + (base - raw);
-  const uint32_t bars = base + FSTAGES * FSmem::STAGE;
-  uint64_t* bar_ptr = reinterpret_cast<uint64_t*>(gbase + FSTAGES * FSmem::STAGE);
-  // full[S] (TMA landed), ready[S] (A split), empty[S] (MMAs done), accf[2], acce[2]
-  const uint32_t full0 = bars, ready0 = bars + 8 * FSTAGES, empty0 = bars + 16 * FSTAGES;
-  const uint32_t accf0 = bars + 24 * FSTAGES, acce0 = accf0 + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 3 * FSTAGES + 4);
+  const uint32_t bars = base + S * L::STAGE;
+  uint64_t* bar_ptr = reinterpret_cast<uint64_t*>(gbase + S * L::STAGE);
+  // full[S] (TMA landed), ready[S] (A split into TMEM), empty[S] (MMAs done), accf[2], acce[2]
+  const uint32_t full0 = bars, ready0 = bars + 8 * S, empty0 = bars + 16 * S;
+  const uint32_t accf0 = bars + 24 * S, acce0 = accf0 + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 3 * S + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr uint32_t TMEM_COLS = 2 * FBN;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < FSTAGES; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(full0 + 8 * s, 1);
-      mbar_init(ready0 + 8 * s, F_ACC_WARPS + F_XFORM_WARPS);
+      mbar_init(ready0 + 8 * s, 8);
       mbar_init(empty0 + 8 * s, 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(accf0 + 8 * b, 1);
-      mbar_init(acce0 + 8 * b, F_ACC_WARPS);
+      mbar_init(acce0 + 8 * b, 8);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -679,7 +747,7 @@ __global__ void __launch_bounds__(FUSED_THREADS, 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(TMEM_COLS));
+                 "r"(L::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -703,20 +771,19 @@ __global__ void __launch_bounds__(FUSED_THREADS, 1)
         const int32_t a_row = (int32_t)(ao * p.M + tc.m_tile * BM);
         const int32_t b_row = (int32_t)(bo * p.N + tc.n_tile * FBN);
         for (int kb = kb0; kb < kb1; ++kb, ++g) {
-          const int s = (int)(g % FSTAGES);
-          if (!mbar_wait(empty0 + 8 * s, (uint32_t)(((g / FSTAGES) & 1) ^ 1), abort_flag, p.err))
-            break;
-          const uint32_t st = base + s * FSmem::STAGE;
-          mbar_expect_tx(full0 + 8 * s, FSmem::TX_BYTES);
-          tma_load_2d(st + FSmem::A, &map_a, kb * BK, a_row, full0 + 8 * s);
-          tma_load_2d(st + FSmem::BHI, &map_b, kb * BK, b_row, full0 + 8 * s);
-          tma_load_2d(st + FSmem::BLO, &map_b, Kp + kb * BK, b_row, full0 + 8 * s);
+          const int s = (int)(g % S);
+          if (!mbar_wait(empty0 + 8 * s, (uint32_t)(((g / S) & 1) ^ 1), abort_flag, p.err)) break;
+          const uint32_t st = base + s * L::STAGE;
+          mbar_expect_tx(full0 + 8 * s, L::STAGE);
+          tma_load_2d(st + L::A, &map_a, kb * BK, a_row, full0 + 8 * s);
+          tma_load_2d(st + L::BHI, &map_b, kb * BK, b_row, full0 + 8 * s);
+          tma_load_2d(st + L::BLO, &map_b, Kp + kb * BK, b_row, full0 + 8 * s);
         }
       }
       if (*abort_flag) {
-        for (int64_t q = (g > FSTAGES ? g - FSTAGES : 0); q < g; ++q) {
+        for (int64_t q = (g > S ? g - S : 0); q < g; ++q) {
           const uint64_t t0 = globaltimer();
-          while (!mbar_try_wait(full0 + 8 * (int)(q % FSTAGES), (uint32_t)((q / FSTAGES) & 1)) &&
+          while (!mbar_try_wait(full0 + 8 * (int)(q % S), (uint32_t)((q / S) & 1)) &&
                  globaltimer() - t0 < kTimeoutNs) {
           }
         }
@@ -741,21 +808,21 @@ __global__ void __launch_bounds__(FUSED_THREADS, 1)
           const int kb_start = kb0 + c * FCHUNK;
           const int kb_end = min(kb1, kb_start + FCHUNK);
           for (int kb = kb_start; kb < kb_end; ++kb, ++g) {
-            const int s = (int)(g % FSTAGES);
-            ok = mbar_wait(ready0 + 8 * s, (uint32_t)((g / FSTAGES) & 1), abort_flag, p.err);
+            const int s = (int)(g % S);
+            ok = mbar_wait(ready0 + 8 * s, (uint32_t)((g / S) & 1), abort_flag, p.err);
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t st = base + s * FSmem::STAGE;
-            const uint64_t ahi = smem_desc(st + FSmem::A), alo = smem_desc(st + FSmem::ALO);
-            const uint64_t bhi = smem_desc(st + FSmem::BHI), blo = smem_desc(st + FSmem::BLO);
+            const uint32_t st = base + s * L::STAGE;
+            const uint32_t ahi = tmem + L::ACOL + 64u * s, alo = ahi + 32u;
+            const uint64_t bhi = smem_desc(st + L::BHI), blo = smem_desc(st + L::BLO);
             const bool first = kb == kb_start;
 #pragma unroll
             for (int k = 0; k < BK / 8; ++k)
-              umma_tf32(d, alo + 2 * k, bhi + 2 * k, idesc, (!first || k > 0) ? 1u : 0u);
+              umma_tf32_ts(d, alo + 8 * k, bhi + 2 * k, idesc, (!first || k > 0) ? 1u : 0u);
 #pragma unroll
-            for (int k = 0; k < BK / 8; ++k) umma_tf32(d, ahi + 2 * k, blo + 2 * k, idesc, 1u);
+            for (int k = 0; k < BK / 8; ++k) umma_tf32_ts(d, ahi + 8 * k, blo + 2 * k, idesc, 1u);
 #pragma unroll
-            for (int k = 0; k < BK / 8; ++k) umma_tf32(d, ahi + 2 * k, bhi + 2 * k, idesc, 1u);
+            for (int k = 0; k < BK / 8; ++k) umma_tf32_ts(d, ahi + 8 * k, bhi + 2 * k, idesc, 1u);
             umma_commit(empty0 + 8 * s);
           }
           umma_commit(accf0 + 8 * buf);
@@ -763,18 +830,17 @@ __global__ void __launch_bounds__(FUSED_THREADS, 1)
       }
     }
   } else {
-    // ------------------------------ transform (warps 2..11) + accumulators (2..9)
-    // Every one of these 10 warps splits its share of each landed A tile; the
-    // 8 accumulator warps also promote chunk c-1 right after splitting the last
-    // slice of chunk c (the tensor pipe is then busy with chunk c), promote the
-    // final chunk at the end of the tile and store it.
+    // ------------------------------------ split A + accumulators (warps 2..9)
+    // Each warp splits its lanes' K half of every landed A slice into TMEM;
+    // after splitting the last slice of chunk c it promotes chunk c-1 (the
+    // tensor pipe is then busy with chunk c), and it promotes the final
+    // chunk at the end of the tile and stores it.
     constexpr int COLS = FBN / 2;
-    constexpr int XT = 32 * (F_ACC_WARPS + F_XFORM_WARPS);
-    const bool is_acc = warp < 2 + F_ACC_WARPS;
-    const int xt = (warp - 2) * 32 + lane;
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
-    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * COLS);
+    const int row = quad * 32 + lane;  // row of the tile (TMEM lane)
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t acc_base = tmem + lane_off + (uint32_t)(half * COLS);
     int64_t g = 0, gc = 0;
     bool ok = true;
     float acc[COLS];
@@ -787,15 +853,22 @@ __global__ void __launch_bounds__(FUSED_THREADS, 1)
         ok = false;
         return;
       }
+      if constexpr (COLS == 32) {
+        uint32_t r[32];
+        tmem_ld32(acc_base + (uint32_t)(buf * FBN), r);
 #pragma unroll
-      for (int piece = 0; piece < COLS / 32; piece += 2) {
-        uint32_t r0[32], r1[32];
-        tmem_ld32x2(lane_base + (uint32_t)(buf * FBN + piece * 32),
-                    lane_base + (uint32_t)(buf * FBN + piece * 32 + 32), r0, r1);
+        for (int i = 0; i < 32; ++i) acc[i] += __uint_as_float(r[i]);
+      } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          acc[piece * 32 + i] += __uint_as_float(r0[i]);
-          acc[piece * 32 + 32 + i] += __uint_as_float(r1[i]);
+        for (int piece = 0; piece < COLS / 32; piece += 2) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32x2(acc_base + (uint32_t)(buf * FBN + piece * 32),
+                      acc_base + (uint32_t)(buf * FBN + piece * 32 + 32), r0, r1);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            acc[piece * 32 + i] += __uint_as_float(r0[i]);
+            acc[piece * 32 + 32 + i] += __uint_as_float(r1[i]);
+          }
         }
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -811,52 +884,59 @@ __global__ void __launch_bounds__(FUSED_THREADS, 1)
       split_range(p, split, kb0, kb1);
       int64_t ao, bo;
       batch_offsets(p.map, tc.bz, &ao, &bo);
-      // Row of A (over all matrices) of the first row of this tile.
-      const int64_t arow0 = ao * p.M + tc.m_tile * BM;
+      const int64_t arow = ao * p.M + tc.m_tile * BM + row;  // row of A over all matrices
 #pragma unroll
       for (int i = 0; i < COLS; ++i) acc[i] = 0.0f;
       for (int kb = kb0; kb < kb1 && ok; ++kb, ++g) {
-        const int s = (int)(g % FSTAGES);
-        const bool got = mbar_wait(full0 + 8 * s, (uint32_t)((g / FSTAGES) & 1), abort_flag, p.err);
+        const int s = (int)(g % S);
+        const bool got = mbar_wait(full0 + 8 * s, (uint32_t)((g / S) & 1), abort_flag, p.err);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
-        float4* a = reinterpret_cast<float4*>(gbase + s * FSmem::STAGE + FSmem::A);
-        float4* alo = reinterpret_cast<float4*>(gbase + s * FSmem::STAGE + FSmem::ALO);
-        for (int i = xt; i < FSmem::TILE / 16; i += XT) {
-          const float4 v = a[i];
-          float4 h, l;
-          split_bits(v.x, h.x, l.x);
-          split_bits(v.y, h.y, l.y);
-          split_bits(v.z, h.z, l.z);
-          split_bits(v.w, h.w, l.w);
-          a[i] = h;
-          alo[i] = l;
-          // Zero or tiny among the four (smallest exponent field below 2^-57):
-          // tag the row if one is a nonzero tiny value.  128-byte tile rows;
-          // the swizzle only moves 16-byte chunks within a row.
-          const uint32_t e = min(min(__float_as_uint(v.x) & 0x7f800000u, __float_as_uint(v.y) & 0x7f800000u),
-                                 min(__float_as_uint(v.z) & 0x7f800000u, __float_as_uint(v.w) & 0x7f800000u));
-          if (e < (kTinyExp << 23) && (tiny(v.x) || tiny(v.y) || tiny(v.z) || tiny(v.w))) {
-            p.rowtag[arow0 + i / (BK / 4)] = p.gen;
+        // This lane's row is 128 bytes; the 128-byte swizzle stores its 16-byte
+        // chunk j at position j ^ (row % 8).
+        const float4* src = reinterpret_cast<const float4*>(gbase + s * L::STAGE + L::A + row * 128);
+        uint32_t hi[16], lo[16], emin = 0xffffffffu;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float4 v = src[(4 * half + t) ^ (row & 7)];
+          split_bits(v.x, hi[4 * t], lo[4 * t]);
+          split_bits(v.y, hi[4 * t + 1], lo[4 * t + 1]);
+          split_bits(v.z, hi[4 * t + 2], lo[4 * t + 2]);
+          split_bits(v.w, hi[4 * t + 3], lo[4 * t + 3]);
+          emin = min(emin, min(min(__float_as_uint(v.x) & 0x7f800000u, __float_as_uint(v.y) & 0x7f800000u),
+                               min(__float_as_uint(v.z) & 0x7f800000u, __float_as_uint(v.w) & 0x7f800000u)));
+        }
+        if (emin < (kTinyExp << 23)) {
+          // A zero or tiny value: tag the row if one of the sixteen is tiny.
+          bool t = false;
+#pragma unroll
+          for (int t4 = 0; t4 < 4; ++t4) {
+            const float4 v = src[(4 * half + t4) ^ (row & 7)];
+            t |= tiny(v.x) | tiny(v.y) | tiny(v.z) | tiny(v.w);
+          }
+          if (t) {
+            p.rowtag[arow] = p.gen;
             p.tagany[0] = p.gen;
-            __threadfence();  // visible before this slice is marked ready
+            __threadfence();
           }
         }
-        // Generic-proxy stores must be visible to the tensor core (async proxy).
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        const uint32_t acol = tmem + lane_off + L::ACOL + 64u * s + 16u * half;
+        __syncwarp();  // converged for the .aligned TMEM stores
+        tmem_st16(acol, hi);
+        tmem_st16(acol + 32u, lo);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(ready0 + 8 * s);
         const int c = (kb - kb0) / FCHUNK;
         const bool chunk_end = (kb - kb0) % FCHUNK == FCHUNK - 1 || kb == kb1 - 1;
-        if (is_acc && chunk_end && c >= 1) promote();  // chunk c-1
+        if (chunk_end && c >= 1) promote();  // chunk c-1
       }
-      if (!is_acc) continue;
       if (ok) promote();  // the tile's last chunk
       if (!ok || *abort_flag) break;
-      finish_item<COLS>(p, tc, split, tc.m_tile * BM + quad * 32 + lane,
-                        tc.n_tile * FBN + half * COLS, acc);
+      finish_item<COLS>(p, tc, split, tc.m_tile * BM + row, tc.n_tile * FBN + half * COLS, acc);
     }
   }
 
@@ -870,7 +950,7 @@ __global__ void __launch_bounds__(FUSED_THREADS, 1)
       }
     }
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(TMEM_COLS));
+                 "r"(L::TMEM_COLS));
   }
 }
 
@@ -989,16 +1069,38 @@ int64_t matrices_used(const BatchMap& m, bool a) {
   return last + 1;
 }
 
+template <int FBN>
+int launch_tmem(Device* d, const CUtensorMap& ma, const CUtensorMap& mb, const Tf32Params& p,
+                int64_t Kp) {
+  const int smem = TSmem<FBN>::TOTAL;
+  static bool configured = false;
+  if (!configured) {
+    PB_CUDA(cudaFuncSetAttribute(tf32x3_tmem_kernel<FBN>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured = true;
+  }
+  const int64_t items = p.tiles * p.ksplit;
+  const int64_t grid = items < d->sm_count ? items : d->sm_count;
+  tf32x3_tmem_kernel<FBN><<<(unsigned)grid, T_THREADS, smem, d->stream>>>(ma, mb, p, (int)Kp);
+  PB_LAUNCHED(d);
+  return PB_OK;
+}
+
 }  // namespace
 
-// 3xTF32 with A split in shared memory (K % 4 == 0): B -> [hi | lo] K-major
-// once, then the fused kernel (and the split reduction when K is split).
+// 3xTF32 with A split into tensor memory (K % 4 == 0): B -> [hi | lo]
+// K-major once, then the TMEM-split kernel (and the split reduction when K
+// is split).
 int gemm_f32_fused(Device* d, const BatchMap& map, int64_t batch, int64_t M, int64_t N, int64_t K,
                    int64_t Kp, int64_t nA, int64_t nB, const float* A, const float* B, float* C) {
   const int64_t rows_a = nA * M, rows_b = nB * N;
   const size_t bytes_b = (size_t)rows_b * 2 * Kp * sizeof(float);
   const int tiles_m = (int)ceil_div(M, (int64_t)BM);
-  const int tiles_n = (int)ceil_div(N, (int64_t)FBN);
+  // 128-wide tiles (split K when they are few): at 128 x 64 the A split per
+  // slice costs as much as the slice's MMAs (1024^3 on B200: 57.0 TFLOP/s
+  // against 59.7 with 128 x 128 and a 2-way split).
+  const int fbn = N <= 64 ? 64 : 128;
+  const int tiles_n = (int)ceil_div(N, (int64_t)fbn);
   const int64_t tiles = (int64_t)tiles_m * tiles_n * batch;
   const int kblocks = (int)(Kp / BK);
   int ksplit = 1;
@@ -1014,16 +1116,16 @@ int gemm_f32_fused(Device* d, const BatchMap& map, int64_t batch, int64_t M, int
   float* Bt = (float*)ws;
   Tf32Params p;
   PB_CHECK(tag_setup(d, p, rows_a, nB, N));
-  const int64_t gx = ceil_div(N, (int64_t)32), gy = ceil_div(Kp, (int64_t)32);
+  const int64_t gx = ceil_div(N, (int64_t)SPLIT_TN), gy = Kp / SPLIT_TK;
   if (gx > INT32_MAX || gy > 65535 || nB > 65535)
     PB_FAIL(PB_ERR_UNSUPPORTED, "B operand too large for the split grid");
-  split_bt_kernel<2><<<dim3((unsigned)gx, (unsigned)gy, (unsigned)nB), dim3(32, 8), 0, d->stream>>>(
+  split_bt_kernel<2><<<dim3((unsigned)gx, (unsigned)gy, (unsigned)nB), 256, 0, d->stream>>>(
       B, Bt, K, N, Kp, p.coltag, p.cgroups, p.tagany, p.gen);
   PB_LAUNCHED(d);
 
   CUtensorMap ma, mb;
   PB_CHECK(encode_kmajor(&ma, A, rows_a, K, BM));
-  PB_CHECK(encode_kmajor(&mb, Bt, rows_b, 2 * Kp, FBN));
+  PB_CHECK(encode_kmajor(&mb, Bt, rows_b, 2 * Kp, fbn));
   p.C = C;
   p.partial = ksplit > 1 ? (float*)((char*)ws + bytes_b) : nullptr;
   p.M = M;
@@ -1036,33 +1138,24 @@ int gemm_f32_fused(Device* d, const BatchMap& map, int64_t batch, int64_t M, int
   p.map = map;
   p.err = d->err_dev;
   PB_CHECK(finish_setup(d, p, batch, M, N, K, A, B));
-  const int smem = FSmem::TOTAL;
-  static bool configured = false;
-  if (!configured) {
-    PB_CUDA(cudaFuncSetAttribute(tf32x3_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 smem));
-    configured = true;
-  }
-  const int64_t items = tiles * ksplit;
-  const int64_t grid = items < d->sm_count ? items : d->sm_count;
-  tf32x3_fused_kernel<<<(unsigned)grid, FUSED_THREADS, smem, d->stream>>>(ma, mb, p, (int)Kp);
-  PB_LAUNCHED(d);
+  PB_CHECK(fbn == 128 ? launch_tmem<128>(d, ma, mb, p, Kp) : launch_tmem<64>(d, ma, mb, p, Kp));
   if (ksplit > 1) PB_CHECK(launch_reduce(d, p, batch * M * N));
   if (p.repair_inline) return PB_OK;
   return gemm_nonfinite_repair_f32(d, map, batch, M, N, K, A, B, C, p.nf);
 }
 
-// Products with at most this many columns take the shared-memory split
-// kernel.  The pre-split kernel's extra pass over A costs about 12*M*K bytes,
-// i.e. a share of the GEMM that shrinks as 1/N, and its 256-wide tiles waste
-// more of a narrow C.  Measured on B200 (effective TFLOP/s, pre-split vs fused):
-// 1024^3 51 vs 64, (8,16)x512x384x256 53 vs 72, 16384x1024x4096 149 vs 178,
-// 2048^3 138 vs 123, 4096^3 179 vs 170, 8192^3 212 vs 170.
+// Products with at most this many columns take the kernel that splits A in
+// tensor memory.  The pre-split kernel's extra pass over A costs about
+// 12*M*K bytes, a share of the GEMM that shrinks as 1/N, while its 256-wide
+// tiles (TMEM holds no A slices there) need half the A work per MMA.
+// Measured on B200 (effective TFLOP/s, pre-split vs TMEM split): 1024^3 51
+// vs 57-60, (8,16)x512x384x256 52 vs 70, 16384x1024x4096 148 vs 199, 2048^3
+// 137 vs 141, 4096^3 177 vs 187, 6144^3 210 vs 193, 8192^3 218 vs 195.
 #ifndef PB_TF32_FUSED_MAX_N
-#define PB_TF32_FUSED_MAX_N 1024
+#define PB_TF32_FUSED_MAX_N 4096
 #endif
 
-// algo: 0 auto, 1 SIMT, 2 3xTF32 (kernel by size), 4 pre-split, 5 A split in smem.
+// algo: 0 auto, 1 SIMT, 2 3xTF32 (kernel by size), 4 pre-split, 5 A split in TMEM.
 int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int64_t N, int64_t K,
                   const float* A, const float* B, float* C, int algo) {
   if (algo == 0) algo = (M >= 64 && N >= 64 && K >= 32) ? 2 : 1;
@@ -1073,12 +1166,12 @@ int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
   const int64_t Kp = ceil_div(K, (int64_t)BK) * BK;
   const int64_t K3 = 3 * Kp;
   const int64_t nA = matrices_used(map, true), nB = matrices_used(map, false);
-  // Two 3xTF32 kernels: A split in shared memory (TMA needs 16-byte aligned
+  // Two 3xTF32 kernels: A split in tensor memory (TMA needs 16-byte aligned
   // rows of A: K % 4 == 0) or both operands split in HBM first.
   const bool can_fuse = K % 4 == 0 && (uintptr_t)A % 16 == 0 && nA * M <= INT32_MAX &&
                         nB * N <= INT32_MAX && Kp / BK <= INT32_MAX;
   if (algo == PB_GEMM_TF32X3_FUSED && !can_fuse)
-    PB_FAIL(PB_ERR_UNSUPPORTED, "the shared-memory split needs K %% 4 == 0 and aligned A");
+    PB_FAIL(PB_ERR_UNSUPPORTED, "the in-kernel A split needs K %% 4 == 0 and aligned A");
   if (algo == PB_GEMM_TF32X3_FUSED || (algo == PB_GEMM_TF32X3 && can_fuse && N <= PB_TF32_FUSED_MAX_N))
     return gemm_f32_fused(d, map, batch, M, N, K, Kp, nA, nB, A, B, C);
   const int64_t rows_a = nA * M, rows_b = nB * N;
@@ -1118,10 +1211,10 @@ int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
     split_a_kernel<<<(unsigned)blocks, 256, 0, d->stream>>>(A, Ap, rows_a, K, Kp, p.rowtag,
                                                             p.tagany, p.gen);
     PB_LAUNCHED(d);
-    const int64_t gx = ceil_div(N, (int64_t)32), gy = ceil_div(Kp, (int64_t)32);
+    const int64_t gx = ceil_div(N, (int64_t)SPLIT_TN), gy = Kp / SPLIT_TK;
     if (gx > INT32_MAX || gy > 65535 || nB > 65535)
       PB_FAIL(PB_ERR_UNSUPPORTED, "B operand too large for the split grid");
-    split_bt_kernel<3><<<dim3((unsigned)gx, (unsigned)gy, (unsigned)nB), dim3(32, 8), 0, d->stream>>>(
+    split_bt_kernel<3><<<dim3((unsigned)gx, (unsigned)gy, (unsigned)nB), 256, 0, d->stream>>>(
         B, Bt, K, N, Kp, p.coltag, p.cgroups, p.tagany, p.gen);
     PB_LAUNCHED(d);
   }

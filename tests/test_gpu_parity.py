@@ -141,7 +141,7 @@ def test_every_gemm_kernel_on_every_shape(b200, algo, case):
     if algo in tf32 and a.dtype != np.float32:
         pytest.skip("3xTF32 is the float32 kernel")
     if algo == _lib.PB_GEMM_TF32X3_FUSED and a.shape[-1] % 4:
-        pytest.skip("the shared-memory split needs K % 4 == 0")
+        pytest.skip("the in-kernel A split needs K % 4 == 0")
     if algo == _lib.PB_GEMM_DMMA:
         a, b = a.astype(np.float64), b.astype(np.float64)
     got = _call_gemm_ex(b200, a, b, algo)
