@@ -120,8 +120,9 @@ int pb_gemm(pb_ctx* ctx, int dev, int dtype, int batch_ndim, const int64_t* batc
  * (float32; picks one of the two 3xTF32 kernels by size),
  * PB_GEMM_TF32X3_PRESPLIT (operands split into hi/lo copies in HBM first),
  * PB_GEMM_TF32X3_FUSED (A split inside the kernel, into tensor memory;
- * needs K % 4 == 0) or
- * PB_GEMM_DMMA (float64 only, FP64 tensor cores).  The
+ * needs K % 4 == 0), PB_GEMM_DMMA (float64 only, FP64 tensor cores) or
+ * PB_GEMM_SKINNY (M <= 8: one pass over B with 16-byte loads along N; what
+ * pb_gemm uses for M <= 8, vector @ matrix included).  The
  * reference exposes the same kind of provider choice as
  * CUDABackend(blas="custom"|"cublas")
  * (src/openpacho/_cuda.py:138-141). */
@@ -131,7 +132,8 @@ enum {
   PB_GEMM_TF32X3 = 2,
   PB_GEMM_DMMA = 3,
   PB_GEMM_TF32X3_PRESPLIT = 4,
-  PB_GEMM_TF32X3_FUSED = 5
+  PB_GEMM_TF32X3_FUSED = 5,
+  PB_GEMM_SKINNY = 6
 };
 int pb_gemm_ex(pb_ctx* ctx, int dev, int dtype, int batch_ndim, const int64_t* batch_shape,
                const int64_t* a_bstride, const int64_t* b_bstride, int64_t M, int64_t N,

@@ -2,9 +2,10 @@
 //
 // Reference routing: CUDABackend.matmul (src/openpacho/_cuda.py:493-637):
 // K == 0 -> zeros; float32 tiles -> register GEMM; everything else a direct
-// kernel or cuBLAS.  Here: K == 0 -> zeros; float64 -> DMMA tensor-core tiles;
-// float32 -> 3xTF32 tcgen05 when the output has at least one 64x64 block and
-// K >= 32, else the float32 SIMT tile kernel.
+// kernel or cuBLAS.  Here: K == 0 -> zeros; at most 8 rows (vector @ matrix
+// and the like) -> the skinny kernel, one pass over B; float64 -> DMMA
+// tensor-core tiles; float32 -> 3xTF32 tcgen05 when the output has at least
+// one 64x64 block and K >= 32, else the float32 SIMT tile kernel.
 #include "pb_internal.cuh"
 
 namespace pb {
@@ -16,6 +17,8 @@ int gemm_simt_f64(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
 int gemm_dmma_f64(Device* d, const BatchMap& map, int64_t batch, int64_t M, int64_t N, int64_t K,
                   const double* A, const double* B, double* C);
 int fill_device(Device* d, int dtype, void* dst, size_t count, double value);
+int gemm_skinny(Device* d, int dtype, const BatchMap& map, int64_t batch, int64_t M, int64_t N,
+                int64_t K, const void* A, const void* B, void* C);
 
 static int build_map(int batch_ndim, const int64_t* shape, const int64_t* as, const int64_t* bs,
                      BatchMap* map, int64_t* batch) {
@@ -51,6 +54,10 @@ int gemm_dispatch(pb_ctx* ctx, int dev, int dtype, int batch_ndim, const int64_t
   PB_CHECK(enter(ctx, dev, &d));
   if (!K) return fill_device(d, dtype, C, (size_t)count, 0.0);
   if (!A || !B) PB_FAIL(PB_ERR_INVALID, "null input");
+  if (algo == PB_GEMM_SKINNY || (algo == PB_GEMM_AUTO && M <= 8)) {
+    if (M > 8) PB_FAIL(PB_ERR_UNSUPPORTED, "the skinny kernel takes at most 8 rows");
+    return gemm_skinny(d, dtype, map, batch, M, N, K, A, B, C);
+  }
   if (dtype == PB_F64) {
     if (algo == PB_GEMM_SIMT)
       return gemm_simt_f64(d, map, batch, M, N, K, (const double*)A, (const double*)B, (double*)C);

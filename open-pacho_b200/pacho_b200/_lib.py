@@ -33,6 +33,7 @@ PB_GEMM_TF32X3 = 2
 PB_GEMM_DMMA = 3
 PB_GEMM_TF32X3_PRESPLIT = 4
 PB_GEMM_TF32X3_FUSED = 5
+PB_GEMM_SKINNY = 6
 
 LIBRARY_NAME = "libpacho_b200.so"
 

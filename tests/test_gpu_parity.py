@@ -126,14 +126,15 @@ def _gemm_shapes():
     yield from cases.special_value_cases()
     rng = np.random.default_rng(11)
     for m, n, k in ((128, 128, 32), (129, 255, 33), (300, 520, 97), (1, 300, 64), (257, 1, 40),
-                    (64, 64, 1), (200, 136, 1000)):
+                    (64, 64, 1), (200, 136, 1000), (1, 4099, 3000), (3, 1001, 20000),
+                    (8, 64, 5), (5, 2, 70000)):
         yield (f"rand{m}x{n}x{k}", rng.standard_normal((m, k)).astype(np.float32),
                rng.standard_normal((k, n)).astype(np.float32))
 
 
 @pytest.mark.parametrize("algo", [_lib.PB_GEMM_SIMT, _lib.PB_GEMM_TF32X3, _lib.PB_GEMM_TF32X3_PRESPLIT,
-                                  _lib.PB_GEMM_TF32X3_FUSED, _lib.PB_GEMM_DMMA],
-                         ids=["simt", "tf32x3", "tf32x3_presplit", "tf32x3_fused", "dmma"])
+                                  _lib.PB_GEMM_TF32X3_FUSED, _lib.PB_GEMM_DMMA, _lib.PB_GEMM_SKINNY],
+                         ids=["simt", "tf32x3", "tf32x3_presplit", "tf32x3_fused", "dmma", "skinny"])
 @pytest.mark.parametrize("case", list(_gemm_shapes()), ids=lambda c: c[0])
 def test_every_gemm_kernel_on_every_shape(b200, algo, case):
     name, a, b = case
@@ -142,6 +143,8 @@ def test_every_gemm_kernel_on_every_shape(b200, algo, case):
         pytest.skip("3xTF32 is the float32 kernel")
     if algo == _lib.PB_GEMM_TF32X3_FUSED and a.shape[-1] % 4:
         pytest.skip("the in-kernel A split needs K % 4 == 0")
+    if algo == _lib.PB_GEMM_SKINNY and a.shape[-2] > 8:
+        pytest.skip("the skinny kernel takes at most 8 rows")
     if algo == _lib.PB_GEMM_DMMA:
         a, b = a.astype(np.float64), b.astype(np.float64)
     got = _call_gemm_ex(b200, a, b, algo)
@@ -248,6 +251,25 @@ def test_tf32x3_tiny_operands_keep_float32_accuracy(b200, algo, shape):
     got = _call_gemm_ex(b200, a, b, algo)
     want = numpy_backend.matmul(a, b)
     assert want[lead + (5, 9)] != 0 and abs(want[lead + (5, 9)]) < 2.0**-126
+    assert tolerance.gemm_violations(got, want, a, b) == 0
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("shapes", [((16384,), (16384, 4096)), ((3000,), (5, 3000, 777)),
+                                    ((4, 513), (513, 9000)), ((2, 7, 2000), (2000, 130)),
+                                    ((1, 65536), (3, 65536, 12))],
+                         ids=lambda s: "@".join("x".join(map(str, t)) for t in s))
+def test_vector_and_few_row_products(b200, dtype, shapes):
+    """Vector @ matrix and products with at most 8 rows (the skinny kernel),
+    broadcast batches, unaligned N and K split over blocks, via pb.matmul."""
+    rng = np.random.default_rng(23)
+    a = rng.standard_normal(shapes[0]).astype(dtype)
+    b = rng.standard_normal(shapes[1]).astype(dtype)
+    a.flat[7] = np.inf
+    got = _gpu_matmul(b200, a, b)
+    with np.errstate(all="ignore"):
+        want = numpy_backend.matmul(a, b)
+    assert got.shape == want.shape
     assert tolerance.gemm_violations(got, want, a, b) == 0
 
 
