@@ -21,6 +21,7 @@
 //  kernel raises the device error word, stops issuing, waits (bounded) for
 //  its own copies, frees TMEM and returns.
 #include <cfloat>
+#include <utility>
 #include <cudaTypedefs.h>
 
 #include "pb_internal.cuh"
@@ -102,6 +103,7 @@ __global__ void __launch_bounds__(256) split_bt_kernel(const float* __restrict__
                                                        unsigned int* coltag, int64_t groups,
                                                        unsigned int* tagany, unsigned int gen) {
   __shared__ float tile[SPLIT_TK][SPLIT_TN + 1];
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the GEMM may start its prologue
   const int64_t mat = blockIdx.z;
   const int64_t k0 = (int64_t)blockIdx.y * SPLIT_TK, n0 = (int64_t)blockIdx.x * SPLIT_TN;
   const float* src = B + mat * K * N;
@@ -498,7 +500,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   const int64_t items = p.tiles * p.ksplit;
-  // The non-finite repair launch may be scheduled now; it waits for this grid.
+  // Launched as a programmatic dependent of the split pass: the prologue above
+  // overlapped its tail; nothing it wrote is read before this wait.  The next
+  // launch (split reduction or repair) may be scheduled from now on; it waits
+  // for this grid in turn.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
@@ -755,7 +761,11 @@ __global__ void __launch_bounds__(T_THREADS, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   const int64_t items = p.tiles * p.ksplit;
-  // The non-finite repair launch may be scheduled now; it waits for this grid.
+  // Launched as a programmatic dependent of the split pass: the prologue above
+  // overlapped its tail; nothing it wrote is read before this wait.  The next
+  // launch (split reduction or repair) may be scheduled from now on; it waits
+  // for this grid in turn.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
@@ -957,6 +967,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
 // C = sum over splits of the partial tiles, in split order (deterministic);
 // flagged outputs (non-finite, or touching a tagged operand) are recomputed.
 __global__ void splitk_reduce_kernel(const Tf32Params p, int64_t count) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the GEMM's partial tiles
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const bool tags = __ldcg(p.tagany) == p.gen;
@@ -996,13 +1007,32 @@ __global__ void splitk_reduce_kernel(const Tf32Params p, int64_t count) {
   }
 }
 
+// Launch as a programmatic dependent of the previous kernel on the stream: it
+// may be scheduled before that kernel finishes and must execute
+// griddepcontrol.wait before reading anything the previous kernel wrote.
+template <typename... Params, typename... Args>
+int launch_dependent(Device* d, void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                     Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = d->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  PB_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+  PB_LAUNCHED(d);
+  return PB_OK;
+}
+
 int launch_reduce(Device* d, const Tf32Params& p, int64_t count) {
   int64_t blocks = ceil_div(count / 4 + 1, (int64_t)256);
   const int64_t cap = (int64_t)d->sm_count * 8;
   if (blocks > cap) blocks = cap;
-  splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, d->stream>>>(p, count);
-  PB_LAUNCHED(d);
-  return PB_OK;
+  return launch_dependent(d, splitk_reduce_kernel, dim3((unsigned)blocks), dim3(256), 0, p, count);
 }
 
 int encode_kmajor(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols, int box_rows) {
@@ -1032,9 +1062,8 @@ int launch_tf32(Device* d, const CUtensorMap& ma, const CUtensorMap& mb, const T
   // Persistent: one CTA per SM (shared memory allows no more), work items strided.
   const int64_t items = p.tiles * p.ksplit;
   const int64_t grid = items < d->sm_count ? items : d->sm_count;
-  tf32x3_gemm_kernel<BN><<<(unsigned)grid, GEMM_THREADS, smem, d->stream>>>(ma, mb, p);
-  PB_LAUNCHED(d);
-  return PB_OK;
+  return launch_dependent(d, tf32x3_gemm_kernel<BN>, dim3((unsigned)grid), dim3(GEMM_THREADS),
+                          (size_t)smem, ma, mb, p);
 }
 
 // Operands and non-finite handling of a launch (after p.ksplit is set); the
@@ -1081,9 +1110,8 @@ int launch_tmem(Device* d, const CUtensorMap& ma, const CUtensorMap& mb, const T
   }
   const int64_t items = p.tiles * p.ksplit;
   const int64_t grid = items < d->sm_count ? items : d->sm_count;
-  tf32x3_tmem_kernel<FBN><<<(unsigned)grid, T_THREADS, smem, d->stream>>>(ma, mb, p, (int)Kp);
-  PB_LAUNCHED(d);
-  return PB_OK;
+  return launch_dependent(d, tf32x3_tmem_kernel<FBN>, dim3((unsigned)grid), dim3(T_THREADS),
+                          (size_t)smem, ma, mb, p, (int)Kp);
 }
 
 }  // namespace
@@ -1115,17 +1143,6 @@ int gemm_f32_fused(Device* d, const BatchMap& map, int64_t batch, int64_t M, int
   PB_CHECK(scratch(d, bytes_b + bytes_p, &ws));
   float* Bt = (float*)ws;
   Tf32Params p;
-  PB_CHECK(tag_setup(d, p, rows_a, nB, N));
-  const int64_t gx = ceil_div(N, (int64_t)SPLIT_TN), gy = Kp / SPLIT_TK;
-  if (gx > INT32_MAX || gy > 65535 || nB > 65535)
-    PB_FAIL(PB_ERR_UNSUPPORTED, "B operand too large for the split grid");
-  split_bt_kernel<2><<<dim3((unsigned)gx, (unsigned)gy, (unsigned)nB), 256, 0, d->stream>>>(
-      B, Bt, K, N, Kp, p.coltag, p.cgroups, p.tagany, p.gen);
-  PB_LAUNCHED(d);
-
-  CUtensorMap ma, mb;
-  PB_CHECK(encode_kmajor(&ma, A, rows_a, K, BM));
-  PB_CHECK(encode_kmajor(&mb, Bt, rows_b, 2 * Kp, fbn));
   p.C = C;
   p.partial = ksplit > 1 ? (float*)((char*)ws + bytes_b) : nullptr;
   p.M = M;
@@ -1137,7 +1154,20 @@ int gemm_f32_fused(Device* d, const BatchMap& map, int64_t batch, int64_t M, int
   p.ksplit = ksplit;
   p.map = map;
   p.err = d->err_dev;
+  // Everything that may enqueue a memset goes first: the GEMM launch has to
+  // follow the split kernel directly (it is that kernel's programmatic
+  // dependent).
+  PB_CHECK(tag_setup(d, p, rows_a, nB, N));
   PB_CHECK(finish_setup(d, p, batch, M, N, K, A, B));
+  CUtensorMap ma, mb;
+  PB_CHECK(encode_kmajor(&ma, A, rows_a, K, BM));
+  PB_CHECK(encode_kmajor(&mb, Bt, rows_b, 2 * Kp, fbn));
+  const int64_t gx = ceil_div(N, (int64_t)SPLIT_TN), gy = Kp / SPLIT_TK;
+  if (gx > INT32_MAX || gy > 65535 || nB > 65535)
+    PB_FAIL(PB_ERR_UNSUPPORTED, "B operand too large for the split grid");
+  split_bt_kernel<2><<<dim3((unsigned)gx, (unsigned)gy, (unsigned)nB), 256, 0, d->stream>>>(
+      B, Bt, K, N, Kp, p.coltag, p.cgroups, p.tagany, p.gen);
+  PB_LAUNCHED(d);
   PB_CHECK(fbn == 128 ? launch_tmem<128>(d, ma, mb, p, Kp) : launch_tmem<64>(d, ma, mb, p, Kp));
   if (ksplit > 1) PB_CHECK(launch_reduce(d, p, batch * M * N));
   if (p.repair_inline) return PB_OK;
@@ -1201,7 +1231,23 @@ int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
   float* Ap = (float*)ws;
   float* Bt = (float*)((char*)ws + bytes_a);
   Tf32Params p;
+  p.C = C;
+  p.partial = ksplit > 1 ? (float*)((char*)ws + bytes_a + bytes_b) : nullptr;
+  p.M = M;
+  p.N = N;
+  p.kblocks = kblocks;
+  p.tiles_m = tiles_m;
+  p.tiles_n = (int)ceil_div(N, (int64_t)BN);
+  p.tiles = tiles;
+  p.ksplit = ksplit;
+  p.map = map;
+  p.err = d->err_dev;
+  // Memsets first: the GEMM is the split kernel's programmatic dependent.
   PB_CHECK(tag_setup(d, p, rows_a, nB, N));
+  PB_CHECK(finish_setup(d, p, batch, M, N, K, A, B));
+  CUtensorMap ma, mb;
+  PB_CHECK(encode_kmajor(&ma, Ap, rows_a, K3, BM));
+  PB_CHECK(encode_kmajor(&mb, Bt, rows_b, K3, BN));
 
   {
     const int64_t total = rows_a * Kp;
@@ -1218,22 +1264,6 @@ int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
         B, Bt, K, N, Kp, p.coltag, p.cgroups, p.tagany, p.gen);
     PB_LAUNCHED(d);
   }
-
-  CUtensorMap ma, mb;
-  PB_CHECK(encode_kmajor(&ma, Ap, rows_a, K3, BM));
-  PB_CHECK(encode_kmajor(&mb, Bt, rows_b, K3, BN));
-  p.C = C;
-  p.partial = ksplit > 1 ? (float*)((char*)ws + bytes_a + bytes_b) : nullptr;
-  p.M = M;
-  p.N = N;
-  p.kblocks = kblocks;
-  p.tiles_m = tiles_m;
-  p.tiles_n = (int)ceil_div(N, (int64_t)BN);
-  p.tiles = tiles;
-  p.ksplit = ksplit;
-  p.map = map;
-  p.err = d->err_dev;
-  PB_CHECK(finish_setup(d, p, batch, M, N, K, A, B));
   PB_CHECK(BN == 256 ? launch_tf32<256>(d, ma, mb, p) : launch_tf32<128>(d, ma, mb, p));
   if (ksplit > 1) PB_CHECK(launch_reduce(d, p, batch * M * N));
   if (p.repair_inline) return PB_OK;
