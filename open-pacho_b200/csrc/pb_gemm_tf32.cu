@@ -21,6 +21,7 @@
 //  kernel raises the device error word, stops issuing, waits (bounded) for
 //  its own copies, frees TMEM and returns.
 #include <cfloat>
+#include <cstring>
 #include <utility>
 #include <cudaTypedefs.h>
 
@@ -224,6 +225,23 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// Bulk tensor store of a box from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int32_t x,
+                                             int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(x), "r"(y), "r"(z)
+      : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// The source buffers of this thread's bulk stores may be overwritten.
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// This thread's bulk stores have completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (SBO), leading offset unused (1), sm_100 version 1.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
@@ -325,6 +343,7 @@ struct Tf32Params {
   unsigned int* nf;          // non-finite tile marks (pb_internal.cuh)
   int64_t nf_tm, nf_tn;      // kNonFiniteTile tiles along M and N
   int repair_inline;         // recompute flagged outputs where they are written
+  int tma_store;             // epilogue stores through the output tensor map
   unsigned int* tagany;      // generation if any operand of this launch is tagged
   unsigned int* rowtag;      // per row of A (all matrices): generation if tiny
   unsigned int* coltag;      // per kTagCols columns of each B matrix
@@ -678,7 +697,9 @@ struct TSmem {
   static constexpr int A = 0, BHI = A_BYTES, BLO = A_BYTES + B_BYTES;
   static constexpr int STAGE = A_BYTES + 2 * B_BYTES;
   static constexpr int STAGES = FBN == 128 ? 4 : 6;
-  static constexpr int TOTAL = STAGES * STAGE + 1024 + 256;
+  // Epilogue staging: a 32 x 32 fp32 box (4 KiB, 128-byte swizzle) per warp.
+  static constexpr int OUT = STAGES * STAGE, OUT_BYTES = 8 * 4096;
+  static constexpr int TOTAL = OUT + OUT_BYTES + 1024 + 256;
   static constexpr uint32_t ACOL = 2 * FBN;     // first A column in TMEM
   static constexpr uint32_t TMEM_COLS = 512;
   static_assert(ACOL + 64 * STAGES <= TMEM_COLS, "TMEM columns");
@@ -716,18 +737,64 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
       : "memory");
 }
 
+// Epilogue of one work item through the output tensor map: the warp's 32
+// rows x COLS columns go out as COLS/32 boxes of 32 x 32, staged in the warp's
+// 4 KiB buffer with the 128-byte swizzle (16-byte chunk j of row r at j ^ r%8)
+// and stored by lane 0 with cp.async.bulk.tensor; rows past M and columns
+// past N are clipped by the map.  With K split, the box goes to the split's
+// partial plane (z = split * batch + bz).  Flagged outputs are recomputed after
+// the warp's stores complete.
+template <int COLS>
+__device__ __forceinline__ void store_tma(const Tf32Params& p, const CUtensorMap* map_c,
+                                          const TileCoord& tc, int split, int quad, int64_t col0,
+                                          const float (&acc)[COLS], float4* stage,
+                                          uint32_t stage_u32) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = tc.m_tile * BM + quad * 32 + lane;
+  const int64_t batch = p.tiles / ((int64_t)p.tiles_m * p.tiles_n);
+  const int32_t z = (int32_t)(p.ksplit > 1 ? split * batch + tc.bz : tc.bz);
+  bool bad = false;
+  if (p.ksplit == 1 && row < p.M) {
+#pragma unroll
+    for (int j = 0; j < COLS; ++j) bad |= nonfinite(acc[j]);
+  }
+#pragma unroll
+  for (int c = 0; c < COLS / 32; ++c) {
+    if (lane == 0) bulk_wait_read();  // the previous box has left the buffer
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      stage[lane * 8 + (j ^ (lane & 7))] =
+          make_float4(acc[c * 32 + 4 * j], acc[c * 32 + 4 * j + 1], acc[c * 32 + 4 * j + 2],
+                      acc[c * 32 + 4 * j + 3]);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0)
+      tma_store_3d(map_c, stage_u32, (int32_t)(col0 + c * 32), (int32_t)(tc.m_tile * BM + quad * 32),
+                   z);
+  }
+  if (p.ksplit > 1) return;
+  if (row < p.M && __ldcg(p.tagany) == p.gen) bad |= tagged<COLS>(p, tc.bz, row, col0);
+  if (__any_sync(0xffffffffu, bad)) {
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+    if (bad) handle_nonfinite(p, tc.bz, row, col0, COLS);
+  }
+}
+
 template <int FBN>
 __global__ void __launch_bounds__(T_THREADS, 1)
     tf32x3_tmem_kernel(const __grid_constant__ CUtensorMap map_a,
-                       const __grid_constant__ CUtensorMap map_b, Tf32Params p, int Kp) {
+                       const __grid_constant__ CUtensorMap map_b,
+                       const __grid_constant__ CUtensorMap map_c, Tf32Params p, int Kp) {
   using L = TSmem<FBN>;
   constexpr int S = L::STAGES;
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023) & ~1023u;
   unsigned char* gbase = smem_raw + (base - raw);
-  const uint32_t bars = base + S * L::STAGE;
-  uint64_t* bar_ptr = reinterpret_cast<uint64_t*>(gbase + S * L::STAGE);
+  const uint32_t bars = base + L::OUT + L::OUT_BYTES;
+  uint64_t* bar_ptr = reinterpret_cast<uint64_t*>(gbase + L::OUT + L::OUT_BYTES);
   // full[S] (TMA landed), ready[S] (A split into TMEM), empty[S] (MMAs done), accf[2], acce[2]
   const uint32_t full0 = bars, ready0 = bars + 8 * S, empty0 = bars + 16 * S;
   const uint32_t accf0 = bars + 24 * S, acce0 = accf0 + 16;
@@ -946,8 +1013,15 @@ __global__ void __launch_bounds__(T_THREADS, 1)
       }
       if (ok) promote();  // the tile's last chunk
       if (!ok || *abort_flag) break;
-      finish_item<COLS>(p, tc, split, tc.m_tile * BM + row, tc.n_tile * FBN + half * COLS, acc);
+      const int64_t col0 = tc.n_tile * FBN + half * COLS;
+      if (p.tma_store)
+        store_tma<COLS>(p, &map_c, tc, split, quad, col0, acc,
+                        reinterpret_cast<float4*>(gbase + L::OUT + (warp - 2) * 4096),
+                        base + L::OUT + (warp - 2) * 4096);
+      else
+        finish_item<COLS>(p, tc, split, tc.m_tile * BM + row, col0, acc);
     }
+    if (lane == 0) bulk_wait_all();  // staging buffers are read before the CTA exits
   }
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -1035,6 +1109,24 @@ int launch_reduce(Device* d, const Tf32Params& p, int64_t count) {
   return launch_dependent(d, splitk_reduce_kernel, dim3((unsigned)blocks), dim3(256), 0, p, count);
 }
 
+// Output planes (z x rows x cols, row-major) stored in 32 x 32 boxes with the
+// 128-byte swizzle.  Needs cols % 4 == 0 (16-byte row pitch) and a 16-byte
+// aligned base.
+int encode_out(CUtensorMap* map, float* ptr, int64_t z, int64_t rows, int64_t cols) {
+  void* fn;
+  PB_CHECK(tensor_map_encoder(&fn));
+  auto encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)z};
+  cuuint64_t strides[2] = {(cuuint64_t)cols * sizeof(float), (cuuint64_t)(rows * cols) * sizeof(float)};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)ptr, dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) PB_FAIL(PB_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
+  return PB_OK;
+}
+
 int encode_kmajor(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols, int box_rows) {
   void* fn;
   PB_CHECK(tensor_map_encoder(&fn));
@@ -1099,8 +1191,8 @@ int64_t matrices_used(const BatchMap& m, bool a) {
 }
 
 template <int FBN>
-int launch_tmem(Device* d, const CUtensorMap& ma, const CUtensorMap& mb, const Tf32Params& p,
-                int64_t Kp) {
+int launch_tmem(Device* d, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
+                const Tf32Params& p, int64_t Kp) {
   const int smem = TSmem<FBN>::TOTAL;
   static bool configured = false;
   if (!configured) {
@@ -1111,7 +1203,7 @@ int launch_tmem(Device* d, const CUtensorMap& ma, const CUtensorMap& mb, const T
   const int64_t items = p.tiles * p.ksplit;
   const int64_t grid = items < d->sm_count ? items : d->sm_count;
   return launch_dependent(d, tf32x3_tmem_kernel<FBN>, dim3((unsigned)grid), dim3(T_THREADS),
-                          (size_t)smem, ma, mb, p, (int)Kp);
+                          (size_t)smem, ma, mb, mc, p, (int)Kp);
 }
 
 }  // namespace
@@ -1159,16 +1251,21 @@ int gemm_f32_fused(Device* d, const BatchMap& map, int64_t batch, int64_t M, int
   // dependent).
   PB_CHECK(tag_setup(d, p, rows_a, nB, N));
   PB_CHECK(finish_setup(d, p, batch, M, N, K, A, B));
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, mc;
   PB_CHECK(encode_kmajor(&ma, A, rows_a, K, BM));
   PB_CHECK(encode_kmajor(&mb, Bt, rows_b, 2 * Kp, fbn));
+  float* out = ksplit > 1 ? p.partial : C;
+  p.tma_store = N % 4 == 0 && ((uintptr_t)out & 15) == 0;
+  memset(&mc, 0, sizeof(mc));
+  if (p.tma_store) PB_CHECK(encode_out(&mc, out, ksplit * batch, M, N));
   const int64_t gx = ceil_div(N, (int64_t)SPLIT_TN), gy = Kp / SPLIT_TK;
   if (gx > INT32_MAX || gy > 65535 || nB > 65535)
     PB_FAIL(PB_ERR_UNSUPPORTED, "B operand too large for the split grid");
   split_bt_kernel<2><<<dim3((unsigned)gx, (unsigned)gy, (unsigned)nB), 256, 0, d->stream>>>(
       B, Bt, K, N, Kp, p.coltag, p.cgroups, p.tagany, p.gen);
   PB_LAUNCHED(d);
-  PB_CHECK(fbn == 128 ? launch_tmem<128>(d, ma, mb, p, Kp) : launch_tmem<64>(d, ma, mb, p, Kp));
+  PB_CHECK(fbn == 128 ? launch_tmem<128>(d, ma, mb, mc, p, Kp)
+                      : launch_tmem<64>(d, ma, mb, mc, p, Kp));
   if (ksplit > 1) PB_CHECK(launch_reduce(d, p, batch * M * N));
   if (p.repair_inline) return PB_OK;
   return gemm_nonfinite_repair_f32(d, map, batch, M, N, K, A, B, C, p.nf);
@@ -1242,6 +1339,7 @@ int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
   p.ksplit = ksplit;
   p.map = map;
   p.err = d->err_dev;
+  p.tma_store = 0;
   // Memsets first: the GEMM is the split kernel's programmatic dependent.
   PB_CHECK(tag_setup(d, p, rows_a, nB, N));
   PB_CHECK(finish_setup(d, p, batch, M, N, K, A, B));
