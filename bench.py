@@ -1,7 +1,7 @@
 """Benchmark of the b200 linear-algebra path (driver contract: one JSON line).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload gemv_dot|gemm1024|batched|norm|norm_rows|gemm_f32|gemm_f64]
+                    [--workload gemv_dot|gemm1024|batched|norm|norm_rows|gemm_f32|gemm_f64|vecmat]
 
 Default workload = BASELINE config 2 (the metric's memory-bound BLAS-1/2
 config): one step is y = A @ x with A 16384x16384 float32 plus one DOT of two
@@ -9,7 +9,8 @@ config): one step is y = A @ x with A 16384x16384 float32 plus one DOT of two
 two DOT vectors from the same stream).  value = algorithmic bytes / time
 (GB/s), whole job over all ranks; inputs (1.6 GB) are far larger than L2.
 
-Other workloads are BASELINE configs 1, 3, 4 and 5 (TFLOP/s or GB/s).  Sharded
+Other workloads are BASELINE configs 1, 3, 4 and 5 (TFLOP/s or GB/s), and
+vecmat: x @ A (vector @ matrix, float32 16384^2, GB/s).  Sharded
 ones split across ranks (batch dim for config 3, row blocks of A for config 5,
 contiguous slices + NCCL merge for config 4); config 1 and 2 run one replica
 per rank.  Multi-GPU: one process per GPU under torchrun; barriers and the
@@ -400,6 +401,46 @@ def run_gemm(gpu: Gpu, args, dist: Dist, result: dict, which: str):
     })
 
 
+def run_vecmat(gpu: Gpu, args, dist: Dist, result: dict):
+    """x @ A (vector @ matrix, float32): the skinny kernel, HBM bound."""
+    raw, ctx = gpu.raw, gpu.ctx
+    n = args.n or 16384
+    rng = np.random.default_rng(5)
+    A = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+    x = rng.uniform(-1, 1, n).astype(np.float32)
+    dx, dA = gpu.upload(x), gpu.upload(A)
+    dy = gpu.empty((n,), np.float32)
+    ns = gpu.lib.i64_array([])
+    F32 = gpu.lib.PB_F32
+
+    def step():
+        gpu.check(raw.pb_gemm(ctx, 0, F32, 0, ns, ns, ns, 1, n, n, p_(dx), p_(dA), p_(dy)), "gemm")
+
+    for _ in range(args.warmup):
+        step()
+    dist.barrier()
+    with Clocks(gpu.backend.ordinal) as clocks:
+        gpu.busy(step, dist)
+        l0 = gpu.launches()
+        seconds = gpu.timer(step, args.steps)
+    launches = gpu.launches() - l0
+    seconds = dist.max(seconds)
+    step_bytes = 4 * (n * n + 2 * n)
+    y = np.empty(n, np.float32)
+    gpu.check(raw.pb_d2h(ctx, 0, C.c_void_p(y.ctypes.data), p_(dy), y.nbytes), "d2h")
+    result.update({
+        "metric": f"vector @ matrix ({n} @ {n}x{n}) float32 HBM throughput",
+        "value": step_bytes * args.steps * dist.world / seconds / 1e9, "unit": "GB/s",
+        "ms_per_step": seconds / args.steps * 1e3, "scaling": "weak", "dtype": "f32",
+        "config": {"workload": f"x @ A, A {n}x{n} f32, U[-1,1], default_rng(5)",
+                   "step_bytes": step_bytes, "parallelism": f"replicas x{dist.world}",
+                   "l2": "A (1.07 GB) larger than the 126 MB L2; no flush needed"},
+        "clocks": clocks.summary(), "gpu_launches": launches,
+        "roofline_kernel": ("skinny", step_bytes, seconds / args.steps),
+        "_check": ("gemm", x.reshape(1, n), A, y.reshape(1, n)),
+    })
+
+
 def run_batched(gpu: Gpu, args, dist: Dist, result: dict):
     raw, ctx = gpu.raw, gpu.ctx
     A, B = gen_batched()
@@ -598,7 +639,7 @@ def main(argv=None):
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--workload", default="gemv_dot",
                         choices=("gemv_dot", "gemm1024", "batched", "norm", "norm_rows", "gemm_f32",
-                                 "gemm_f64"))
+                                 "gemm_f64", "vecmat"))
     parser.add_argument("--dtype", choices=("f32", "f64"), default="f32", help="norm workloads")
     parser.add_argument("--n", type=int, default=0,
                         help="GEMM size override (profiling captures); 0 = the BASELINE size")
@@ -618,6 +659,8 @@ def main(argv=None):
             run_gemm(gpu, args, dist, result, args.workload)
         elif args.workload == "batched":
             run_batched(gpu, args, dist, result)
+        elif args.workload == "vecmat":
+            run_vecmat(gpu, args, dist, result)
         else:
             run_norm(gpu, args, dist, result, rows=args.workload == "norm_rows")
         check = result.pop("_check")
@@ -626,7 +669,7 @@ def main(argv=None):
         bad = parity_check(check) if dist.rank == 0 else None
         if dist.rank != 0:
             return 0
-        if result["unit"] == "GB/s" or name in ("gemv", "norm"):
+        if result["unit"] == "GB/s" or name in ("gemv", "norm", "skinny"):
             achieved = work / sec / 1e9
             roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                     "frac": achieved / pk["hbm_gbs"], "kernel": name, "peak_source": pk["source"],
