@@ -47,9 +47,10 @@ enum {
   PB_ERR_UNAVAILABLE = 7  /* no usable device / driver                           */
 };
 
-/* Element types (the reference supports float32 and float64 on this path:
- * src/openpacho/_cuda.py:226-230). */
-enum { PB_F32 = 0, PB_F64 = 1 };
+/* Element types (the reference supports float32 and float64 on this path,
+ * plus bool storage for comparisons and masks: src/openpacho/_cuda.py:226-230).
+ * PB_BOOL is one byte per element, 0 or 1 (nonzero reads as true). */
+enum { PB_F32 = 0, PB_F64 = 1, PB_BOOL = 2 };
 
 typedef struct pb_ctx pb_ctx;
 
@@ -84,7 +85,8 @@ int pb_d2h(pb_ctx* ctx, int dev, void* dst, const void* src, size_t bytes);
 /* Asynchronous device -> host copy into pinned memory (no synchronisation). */
 int pb_d2h_async(pb_ctx* ctx, int dev, void* dst, const void* src, size_t bytes);
 int pb_d2d(pb_ctx* ctx, int dev, void* dst, const void* src, size_t bytes);
-/* Fill `count` elements with `value` (CUDABackend.full, _cuda.py:399-409). */
+/* Fill `count` elements with `value` (CUDABackend.full, _cuda.py:404-414);
+ * PB_BOOL stores value != 0. */
 int pb_fill(pb_ctx* ctx, int dev, int dtype, void* dst, size_t count, double value);
 /* Wait for all submitted work; reports kernel-side error flags. */
 int pb_sync(pb_ctx* ctx, int dev);
@@ -183,6 +185,66 @@ int pb_norm(pb_ctx* ctx, int dev, int dtype, int64_t outer, int64_t reduced, int
 int pb_norm_strided(pb_ctx* ctx, int dev, int dtype, int out_ndim, const int64_t* out_shape,
                     const int64_t* out_strides, int red_ndim, const int64_t* red_shape,
                     const int64_t* red_strides, const void* x, void* out);
+
+/* ---- around the path: elementwise, gather, reductions ----------------- */
+
+/* Elementwise operations, in the names of the reference's expression table
+ * (src/openpacho/_cuda.py:21-46) and ufunc list (src/openpacho/_ops.py:5-29). */
+enum {
+  PB_EW_ADD = 0,
+  PB_EW_SUBTRACT,
+  PB_EW_MULTIPLY,
+  PB_EW_DIVIDE, /* true_divide and divide */
+  PB_EW_POWER,
+  PB_EW_NEGATIVE,
+  PB_EW_POSITIVE,
+  PB_EW_ABSOLUTE,
+  PB_EW_SQRT,
+  PB_EW_EXP,
+  PB_EW_LOG,
+  PB_EW_SIN,
+  PB_EW_COS,
+  PB_EW_TANH,
+  PB_EW_EQUAL,
+  PB_EW_NOT_EQUAL,
+  PB_EW_LESS,
+  PB_EW_LESS_EQUAL,
+  PB_EW_GREATER,
+  PB_EW_GREATER_EQUAL,
+  PB_EW_ISFINITE,
+  PB_EW_CAST,
+  PB_EW_WHERE /* a != 0 ? b : c */
+};
+
+/* out[i] = op(args...) over the output shape `shape[0..ndim)` (C order).
+ * Operand j has dtype arg_dtypes[j] and element strides
+ * arg_strides[j*ndim + d] per output dimension (0 = broadcast).  Values are
+ * computed in float64 and rounded once to out_dtype (bool: != 0).  Binary ops
+ * take 2 operands, where 3, the rest 1.  Replaces CUDABackend.elementwise
+ * (src/openpacho/_cuda.py:416-434); oracle NumpyBackend.elementwise
+ * (src/openpacho/backends.py:109-116). */
+int pb_elementwise(pb_ctx* ctx, int dev, int op, int nargs, const void* const* args,
+                   const int* arg_dtypes, const int64_t* arg_strides, int ndim,
+                   const int64_t* shape, int out_dtype, void* out);
+
+/* out[i] = src[offset + sum_d idx_d(i) * strides[d]] (element units, strides
+ * may be negative): the strided copy behind transpose, diag and slicing.
+ * Replaces CUDABackend.gather (src/openpacho/_cuda.py:436-447); oracle
+ * NumpyBackend.gather (src/openpacho/backends.py:118-128). */
+int pb_gather(pb_ctx* ctx, int dev, int dtype, const void* src, int ndim, const int64_t* shape,
+              int64_t offset, const int64_t* strides, void* out);
+
+/* Reductions over the axes set in axes_mask (bit d = axis d) of a C-order
+ * array of shape[0..ndim); output in the order of the kept axes.  Sums
+ * accumulate in float64 (bool input counts trues; a bool output sum is
+ * unsupported, as in the reference); min/max propagate NaN and prefer -0 /
+ * +0 on zero ties (src/openpacho/_reductions.py:45-72).  An empty sum
+ * writes zeros; an empty extremum is an error.  Replaces CUDABackend.reduce
+ * (src/openpacho/_cuda.py:449-492); oracle NumpyBackend.reduce
+ * (src/openpacho/backends.py:130-136). */
+enum { PB_REDUCE_SUM = 0, PB_REDUCE_MIN = 1, PB_REDUCE_MAX = 2 };
+int pb_reduce(pb_ctx* ctx, int dev, int op, int in_dtype, const void* src, int ndim,
+              const int64_t* shape, uint32_t axes_mask, int out_dtype, void* out);
 
 /* ---- multi-GPU (one process per GPU; NCCL loaded on first use) --------- */
 

@@ -400,6 +400,8 @@ int launch_fill(Device* d, T* out, size_t n, T value) {
 int fill_device(Device* d, int dtype, void* dst, size_t count, double value) {
   if (dtype == PB_F32) return launch_fill<float>(d, (float*)dst, count, (float)value);
   if (dtype == PB_F64) return launch_fill<double>(d, (double*)dst, count, value);
+  if (dtype == PB_BOOL)
+    return launch_fill<unsigned char>(d, (unsigned char*)dst, count, value != 0.0 ? 1 : 0);
   PB_FAIL(PB_ERR_INVALID, "unknown dtype %d", dtype);
 }
 

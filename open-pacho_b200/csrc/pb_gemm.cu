@@ -16,7 +16,6 @@ int gemm_simt_f64(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
                   const double* A, const double* B, double* C);
 int gemm_dmma_f64(Device* d, const BatchMap& map, int64_t batch, int64_t M, int64_t N, int64_t K,
                   const double* A, const double* B, double* C);
-int fill_device(Device* d, int dtype, void* dst, size_t count, double value);
 int gemm_skinny(Device* d, int dtype, const BatchMap& map, int64_t batch, int64_t M, int64_t N,
                 int64_t K, const void* A, const void* B, void* C);
 

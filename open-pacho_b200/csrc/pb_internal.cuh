@@ -105,6 +105,8 @@ int enter(pb_ctx* ctx, int dev, Device** out);
 int scratch(Device* d, size_t bytes, void** out);
 // Ensure at least `n` zeroed counters; returns the pointer.
 int counters(Device* d, size_t n, unsigned int** out);
+// Fill `count` elements of dtype PB_F32 / PB_F64 / PB_BOOL with `value`.
+int fill_device(Device* d, int dtype, void* dst, size_t count, double value);
 // Ensure at least `n` operand tag words; returns them and a fresh generation.
 int operand_tags(Device* d, size_t n, unsigned int** out, unsigned int* gen);
 // Driver entry point for cuTensorMapEncodeTiled (resolved once).

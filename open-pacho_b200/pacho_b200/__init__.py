@@ -5,28 +5,61 @@
   library ``libpacho_b200.so`` (hand-written CUDA for sm_100a).
 * :func:`register` -- adds ``"b200"`` to an installed OpenPacho's dispatch.
 * ``asarray``/``asnumpy``/``matmul``/``dot``/``linalg.norm``/``set_backend``/
-  ``use_backend`` -- the same public API for environments without OpenPacho.
+  ``use_backend``, the elementwise ufuncs, ``where``, ``sum``/``mean``/
+  ``amin``/``amax``, ``transpose``/``diag`` -- the same public API for
+  environments without OpenPacho.
 * :mod:`pacho_b200.distributed` -- sharded GEMM and norm across GPUs (NCCL).
 """
 
 from . import linalg
 from .api import (
+    absolute,
+    add,
+    amax,
+    amin,
     array,
     asarray,
     asnumpy,
+    cos,
+    diag,
+    divide,
     dot,
     empty,
+    equal,
+    exp,
     full,
     get_backend,
+    greater,
+    greater_equal,
+    isfinite,
+    less,
+    less_equal,
+    log,
     matmul,
+    mean,
+    multiply,
     ndarray,
+    negative,
+    not_equal,
     ones,
+    ones_like,
+    positive,
+    power,
     reshape,
     set_backend,
+    sin,
+    sqrt,
+    subtract,
+    sum,
     synchronize,
+    tanh,
     to_backend,
+    transpose,
+    true_divide,
     use_backend,
+    where,
     zeros,
+    zeros_like,
 )
 from .backend import B200Backend, DeviceBuffer
 from .exceptions import BackendMismatchError, BackendUnavailableError, UnsupportedDtypeError

@@ -26,6 +26,7 @@ PB_ERR_UNAVAILABLE = 7
 
 PB_F32 = 0
 PB_F64 = 1
+PB_BOOL = 2
 
 PB_GEMM_AUTO = 0
 PB_GEMM_SIMT = 1
@@ -34,6 +35,19 @@ PB_GEMM_DMMA = 3
 PB_GEMM_TF32X3_PRESPLIT = 4
 PB_GEMM_TF32X3_FUSED = 5
 PB_GEMM_SKINNY = 6
+
+# Elementwise operation codes (pacho_b200.h PB_EW_*), by the reference's
+# operation names (src/openpacho/_cuda.py:21-46).
+EW_OPS = {name: code for code, name in enumerate((
+    "add", "subtract", "multiply", "true_divide", "power", "negative", "positive", "absolute",
+    "sqrt", "exp", "log", "sin", "cos", "tanh", "equal", "not_equal", "less", "less_equal",
+    "greater", "greater_equal", "isfinite", "cast", "where"))}
+EW_OPS["divide"] = EW_OPS["true_divide"]
+
+PB_REDUCE_SUM = 0
+PB_REDUCE_MIN = 1
+PB_REDUCE_MAX = 2
+REDUCE_OPS = {"sum": PB_REDUCE_SUM, "min": PB_REDUCE_MIN, "max": PB_REDUCE_MAX}
 
 LIBRARY_NAME = "libpacho_b200.so"
 
@@ -69,6 +83,9 @@ PROTOTYPES = {
     "pb_gemm": [_ctx, _i, _i, _i, _pi64, _pi64, _pi64, _i64, _i64, _i64, _p, _p, _p],
     "pb_gemm_ex": [_ctx, _i, _i, _i, _pi64, _pi64, _pi64, _i64, _i64, _i64, _p, _p, _p, _i],
     "pb_gemv": [_ctx, _i, _i, _i64, _i64, _p, _p, _p],
+    "pb_elementwise": [_ctx, _i, _i, _i, C.POINTER(_p), C.POINTER(_i), _pi64, _i, _pi64, _i, _p],
+    "pb_gather": [_ctx, _i, _i, _p, _i, _pi64, _i64, _pi64, _p],
+    "pb_reduce": [_ctx, _i, _i, _i, _p, _i, _pi64, C.c_uint32, _i, _p],
     "pb_dot": [_ctx, _i, _i, _i64, _p, _p, _p],
     "pb_dot_noalloc": [_ctx, _i, _i, _i64, _p, _p, _p],
     "pb_norm": [_ctx, _i, _i, _i64, _i64, _i64, _p, _p],
@@ -155,7 +172,9 @@ def dtype_code(dtype) -> int:
         return PB_F32
     if dtype == np.float64:
         return PB_F64
-    raise _exc.UnsupportedDtypeError(f"b200 backend supports float32 and float64, not {dtype}")
+    if dtype == np.bool_:
+        return PB_BOOL
+    raise _exc.UnsupportedDtypeError(f"b200 backend supports bool, float32 and float64, not {dtype}")
 
 
 def i64_array(values):

@@ -9,6 +9,10 @@ hot path, with the same names, argument meaning and errors:
 * ``array``/``asarray``/``asnumpy``/``to_backend``/``empty``/``full``/
   ``zeros``/``ones`` (:205-319), ``reshape`` (:337-352);
 * ``matmul(a, b, *, padding=False)`` and ``dot`` (:457-491);
+* the elementwise ufuncs of src/openpacho/_ops.py:5-29 (``+ - * / **``,
+  comparisons, ``sqrt``/``exp``/... and ``where``, :241-281), ``astype``,
+  ``sum``/``mean``/``amin``/``amax`` (:389-454), ``transpose``/``diag``
+  (:355-366, 494-503), ``zeros_like``/``ones_like`` (:312-319);
 * backend selection ``get_backend``/``set_backend``/``use_backend``/
   ``synchronize`` (src/openpacho/backends.py:153-235) for ``"b200"``.
 
@@ -32,6 +36,16 @@ from .backend import B200Backend
 from . import exceptions as _exc
 
 _FUNCTIONS = {}
+
+# src/openpacho/_ops.py:5-29
+UFUNCS = {
+    name: getattr(np, name)
+    for name in (
+        "add", "subtract", "multiply", "true_divide", "power", "negative", "positive",
+        "absolute", "sqrt", "exp", "log", "sin", "cos", "tanh", "equal", "not_equal", "less",
+        "less_equal", "greater", "greater_equal", "isfinite",
+    )
+}
 
 
 # ------------------------------------------------------------ backends --
@@ -139,7 +153,11 @@ class ndarray(NDArrayOperatorsMixin):
         kwargs.pop("out", None)
         if ufunc is np.matmul:
             return matmul(*inputs, **kwargs)
-        return NotImplemented
+        if ufunc not in UFUNCS.values():
+            return NotImplemented
+        if kwargs:
+            raise NotImplementedError(f"ufunc options {tuple(kwargs)} are not supported")
+        return _elementwise(ufunc, *inputs)
 
     def __array_function__(self, func, types, args, kwargs):
         if func not in _FUNCTIONS or not all(issubclass(t, (ndarray, np.ndarray)) for t in types):
@@ -231,7 +249,7 @@ def reshape(a, shape, order="C"):
         raise NotImplementedError("Only C order is supported")
     shape = (shape,) if isinstance(shape, (int, np.integer)) else tuple(shape)
     shape = tuple(operator.index(d) for d in shape)
-    if sum(d == -1 for d in shape) > 1 or any(d < -1 for d in shape):
+    if shape.count(-1) > 1 or any(d < -1 for d in shape):
         raise ValueError("Invalid reshape dimensions")
     if -1 in shape:
         known = prod(d for d in shape if d != -1)
@@ -281,12 +299,12 @@ def matmul(a, b, *, padding=False):
 
 
 def dot(a, b):
-    """src/openpacho/_array.py:482-491 (0-d operands need elementwise multiply,
-    which is outside this backend's path)."""
+    """src/openpacho/_array.py:482-491: 0-d operands multiply elementwise,
+    vectors and matrices go through matmul."""
     if (a.ndim if isinstance(a, ndarray) else np.ndim(a)) == 0 or (
         b.ndim if isinstance(b, ndarray) else np.ndim(b)
     ) == 0:
-        raise NotImplementedError("0-d dot is an elementwise multiply; not on the b200 path")
+        return multiply(a, b)
     if (a.ndim if isinstance(a, ndarray) else np.ndim(a)) > 2 or (
         b.ndim if isinstance(b, ndarray) else np.ndim(b)
     ) > 2:
@@ -314,5 +332,172 @@ def _axes(axis, ndim):
     return tuple(sorted(values))
 
 
-for _name in ("reshape", "dot"):
+# ---------------------------------------------------------- elementwise --
+
+def resolve_elementwise(ufunc, inputs):
+    """Per-operand and result dtypes, and the broadcast shape
+    (src/openpacho/_ops.py:42-76, without the graph-capture weak types)."""
+    if ufunc is np.where:
+        branches = [value if type(value) in (bool, int, float, complex)
+                     else value.dtype if hasattr(value, "dtype") else np.asarray(value).dtype
+                     for value in inputs[1:]]
+        dtype = np.result_type(*branches)
+        shape = np.broadcast_shapes(*(value.shape if hasattr(value, "shape") else np.shape(value)
+                                      for value in inputs))
+        return (np.dtype("bool"), dtype, dtype, dtype), shape
+    if ufunc not in UFUNCS.values():
+        raise NotImplementedError(f"Unsupported elementwise operation {ufunc.__name__}")
+    types = tuple(type(a) if type(a) in (int, float, complex)
+                  else a.dtype if hasattr(a, "dtype") else np.asarray(a).dtype for a in inputs)
+    resolved = ufunc.resolve_dtypes(types + (None,))
+    if ufunc is np.power and resolved[-1].kind in "iu":
+        raise NotImplementedError("Integer power is not supported; cast to float or multiply explicitly")
+    shape = np.broadcast_shapes(*(getattr(a, "shape", ()) for a in inputs))
+    return resolved, shape
+
+
+def _elementwise(ufunc, *inputs):
+    """src/openpacho/_array.py:241-258: operands cast to their resolved
+    dtypes on the common backend (host scalars uploaded as 0-d arrays)."""
+    backend = _common_backend(inputs)
+    resolved, shape = resolve_elementwise(ufunc, inputs)
+    for dtype in resolved:
+        backend.validate_dtype(dtype)
+    args = [asarray(a, dtype=dt, backend=backend) for a, dt in zip(inputs, resolved)]
+    shape = np.broadcast_shapes(*(a.shape for a in args))
+    data = backend.elementwise(ufunc.__name__, args, shape, resolved[-1])
+    return ndarray._wrap(data, shape, resolved[-1], backend)
+
+
+def _unary_or_binary(ufunc):
+    def call(*args):
+        return _elementwise(ufunc, *args)
+
+    call.__name__ = ufunc.__name__
+    return call
+
+
+globals().update({name: _unary_or_binary(ufunc) for name, ufunc in UFUNCS.items()})
+divide = globals()["true_divide"]
+
+_WHERE_MISSING = object()
+
+
+def where(condition, x=_WHERE_MISSING, y=_WHERE_MISSING):
+    """src/openpacho/_array.py:274-281: both branches are evaluated."""
+    if x is _WHERE_MISSING and y is _WHERE_MISSING:
+        raise NotImplementedError("One-argument where (nonzero indices) is not supported")
+    if x is _WHERE_MISSING or y is _WHERE_MISSING:
+        raise TypeError("where requires both x and y")
+    return _elementwise(np.where, condition, x, y)
+
+
+# ------------------------------------------------------- reductions, views --
+
+_UNSET = object()
+
+
+def sum(a, axis=None, dtype=None, out=None, keepdims=False):  # noqa: A001 - NumPy's name
+    """src/openpacho/_array.py:389-409."""
+    if out is not None:
+        raise NotImplementedError("out= is not supported")
+    a = asarray(a)
+    axes = _axes(axis, a.ndim)
+    if dtype is None:
+        dtype = (np.dtype("int64") if a.dtype.kind in "bi"
+                 else np.dtype("uint64") if a.dtype.kind == "u" else a.dtype)
+    dtype = a._backend.validate_dtype(dtype)
+    shape = (tuple(1 if i in axes else d for i, d in enumerate(a.shape)) if keepdims
+             else tuple(d for i, d in enumerate(a.shape) if i not in axes))
+    data = a._backend.reduce(a, axes, keepdims, dtype)
+    return ndarray._wrap(data, shape, dtype, a._backend)
+
+
+def _extreme(a, axis, out, keepdims, initial, where, operation):
+    """src/openpacho/_array.py:412-431."""
+    if out is not None:
+        raise NotImplementedError("out= is not supported")
+    if initial is not _UNSET:
+        raise NotImplementedError("initial= is not supported")
+    if where is not _UNSET:
+        raise NotImplementedError("where= is not supported")
+    a = asarray(a)
+    axes = _axes(axis, a.ndim)
+    if prod(a.shape[i] for i in axes) == 0:
+        raise ValueError(f"zero-size array to reduction operation {operation} which has no identity")
+    shape = (tuple(1 if i in axes else d for i, d in enumerate(a.shape)) if keepdims
+             else tuple(d for i, d in enumerate(a.shape) if i not in axes))
+    data = a._backend.reduce(a, axes, keepdims, a.dtype, operation=operation)
+    return ndarray._wrap(data, shape, a.dtype, a._backend)
+
+
+def amin(a, axis=None, out=None, keepdims=False, initial=_UNSET, where=_UNSET):
+    """Minimum preserving dtype, propagating NaNs and preferring negative zero ties."""
+    return _extreme(a, axis, out, keepdims, initial, where, "min")
+
+
+def amax(a, axis=None, out=None, keepdims=False, initial=_UNSET, where=_UNSET):
+    """Maximum preserving dtype, propagating NaNs and preferring positive zero ties."""
+    return _extreme(a, axis, out, keepdims, initial, where, "max")
+
+
+def mean(a, axis=None, dtype=None, out=None, keepdims=False):
+    """src/openpacho/_array.py:444-454."""
+    a = asarray(a)
+    if a.ndim == 0 and axis is not None and not isinstance(axis, tuple):
+        raise ValueError("axis out of bounds for scalar mean")
+    dtype = np.dtype(dtype or (a.dtype if a.dtype.kind == "f" else np.float64))
+    if dtype.kind != "f":
+        raise NotImplementedError("mean supports floating point accumulation only")
+    axes = _axes(axis, a.ndim)
+    count = prod(a.shape[i] for i in axes)
+    return sum(a, axis=axis, dtype=dtype, out=out, keepdims=keepdims) / count
+
+
+def _strides(shape):
+    return tuple(prod(shape[i + 1 :]) for i in range(len(shape)))
+
+
+def transpose(a, axes=None):
+    """src/openpacho/_array.py:355-366 (a gather with permuted strides)."""
+    a = asarray(a)
+    axes = tuple(reversed(range(a.ndim))) if axes is None else tuple(axes)
+    if len(axes) != a.ndim:
+        raise ValueError("axes don't match array")
+    axes = tuple(_axis(i, a.ndim) for i in axes)
+    if len(set(axes)) != a.ndim:
+        raise ValueError("repeated axis in transpose")
+    shape = tuple(a.shape[i] for i in axes)
+    strides = tuple(_strides(a.shape)[i] for i in axes)
+    data = a._backend.gather(a, shape, 0, strides)
+    return ndarray._wrap(data, shape, a.dtype, a._backend)
+
+
+def diag(a, k=0):
+    """src/openpacho/_array.py:494-503 (matrix diagonals only)."""
+    a = asarray(a)
+    k = operator.index(k)
+    if a.ndim != 2:
+        raise NotImplementedError("diag currently extracts matrix diagonals only")
+    rows, cols = a.shape
+    start_row, start_col = max(0, -k), max(0, k)
+    length = max(0, min(rows - start_row, cols - start_col))
+    data = a._backend.gather(a, (length,), start_row * cols + start_col, (cols + 1,))
+    return ndarray._wrap(data, (length,), a.dtype, a._backend)
+
+
+def zeros_like(a, dtype=None):
+    a = asarray(a)
+    return zeros(a.shape, dtype=dtype or a.dtype, backend=a._backend)
+
+
+def ones_like(a, dtype=None):
+    a = asarray(a)
+    return ones(a.shape, dtype=dtype or a.dtype, backend=a._backend)
+
+
+for _name in ("reshape", "dot", "sum", "amin", "amax", "mean", "transpose", "diag", "zeros_like",
+              "ones_like", "where"):
     _FUNCTIONS[getattr(np, _name)] = globals()[_name]
+_FUNCTIONS[np.min] = amin
+_FUNCTIONS[np.max] = amax

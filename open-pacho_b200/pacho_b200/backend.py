@@ -5,9 +5,10 @@ The object plugs in where OpenPacho's ``NumpyBackend``/``CUDABackend`` do
 front end calls ``validate_dtype``, ``upload``, ``download``, ``empty``,
 ``full``, ``matmul(a, b, shape, dtype)``, ``norm(a, axes, keepdims, dtype)``
 and ``synchronize`` with operands that expose ``shape``, ``ndim``, ``dtype``
-and ``_data``.  Storage is a :class:`DeviceBuffer` (flat, C-contiguous).
-Operations outside the linear-algebra hot path raise ``NotImplementedError``;
-nothing ever runs on the host CPU instead.
+and ``_data``; around the path, ``elementwise``, ``gather`` and ``reduce``
+(astype, solver arithmetic, sum/mean/min/max, transpose/diag).  Storage is a
+:class:`DeviceBuffer` (flat, C-contiguous).  Unsupported requests raise
+``NotImplementedError``; nothing ever runs on the host CPU instead.
 """
 
 from __future__ import annotations
@@ -23,7 +24,8 @@ import numpy as np
 from . import _lib
 from . import exceptions as _exc
 
-SUPPORTED = (np.dtype(np.float32), np.dtype(np.float64))
+SUPPORTED = (np.dtype(np.float32), np.dtype(np.float64), np.dtype(np.bool_))
+MAX_DIMS = 8  # per operand, for elementwise / gather / reduce
 
 
 class DeviceBuffer:
@@ -52,6 +54,17 @@ class DeviceBuffer:
             self.release()
         except Exception:  # noqa: BLE001 - interpreter shutdown
             pass
+
+
+def _broadcast_strides(shape, own):
+    """Element strides of a C-contiguous operand of shape ``own`` seen through
+    NumPy broadcasting to ``shape`` (0 along broadcast dimensions)."""
+    padded = (1,) * (len(shape) - len(own)) + tuple(own)
+    strides, step = [0] * len(shape), 1
+    for d in range(len(shape) - 1, -1, -1):
+        strides[d] = 0 if padded[d] == 1 and shape[d] != 1 else step
+        step *= padded[d]
+    return strides
 
 
 def _matrix_strides(batch, own):
@@ -114,13 +127,15 @@ class B200Backend:
             raise RuntimeError("b200 backend is closed")
 
     def validate_dtype(self, dtype):
-        """float32 and float64 only (the dtypes of the hot path)."""
+        """bool, float32 and float64, as the reference CUDA backend
+        (src/openpacho/_cuda.py:226-230); matmul and norm take the floats."""
         try:
             dtype = np.dtype(dtype)
         except TypeError as exc:
             raise _exc.UnsupportedDtypeError(str(exc)) from exc
         if dtype not in SUPPORTED or not dtype.isnative:
-            raise _exc.UnsupportedDtypeError(f"b200 backend supports float32 and float64, not {dtype}")
+            raise _exc.UnsupportedDtypeError(
+                f"b200 backend supports bool, float32 and float64, not {dtype}")
         return dtype
 
     @contextmanager
@@ -201,6 +216,8 @@ class B200Backend:
         vector is a GEMV over the flattened rows of ``a``, everything else one
         batched GEMM launch with per-operand batch strides (0 = broadcast)."""
         dtype = self.validate_dtype(dtype)
+        if dtype.kind != "f":
+            raise NotImplementedError("b200 matmul requires float32 or float64")
         if a.dtype != dtype or b.dtype != dtype:
             raise NotImplementedError("b200 matmul needs operands already in the result dtype")
         code = _lib.dtype_code(dtype)
@@ -235,6 +252,8 @@ class B200Backend:
         """Euclidean/Frobenius norm over ``axes`` (norm_data,
         src/openpacho/_norm.py:39-118); ``keepdims`` only shapes the wrapper."""
         dtype = self.validate_dtype(dtype)
+        if dtype.kind != "f":
+            raise NotImplementedError("b200 norm requires float32 or float64")
         if a.dtype != dtype:
             raise NotImplementedError("b200 norm needs its input in the result dtype")
         code = _lib.dtype_code(dtype)
@@ -274,15 +293,91 @@ class B200Backend:
         zero-fills ragged tiles, so padded copies would only add traffic."""
         return None
 
-    # ------------------------------------------------ outside the hot path
+    # ------------------------------------------------------ around the path
     def elementwise(self, name, args, shape, dtype):
-        raise NotImplementedError(f"b200 backend implements the linear-algebra path only ({name})")
+        """``name`` over broadcast operands into a new ``shape`` array of
+        ``dtype`` (CUDABackend.elementwise, src/openpacho/_cuda.py:416-434;
+        operation names of _EXPRESSIONS, :21-46).  Operands are arrays of
+        this backend, or host scalars (``_host_scalar``), uploaded once."""
+        dtype = self.validate_dtype(dtype)
+        op = _lib.EW_OPS.get(name)
+        if op is None:
+            raise NotImplementedError(f"b200 elementwise has no operation {name!r}")
+        shape = tuple(int(d) for d in shape)
+        if len(shape) > MAX_DIMS:
+            raise NotImplementedError(f"b200 elementwise supports at most {MAX_DIMS} dimensions")
+        out = self.empty(shape, dtype)
+        if not prod(shape):
+            return out
+        ptrs, codes, strides, keep = [], [], [], []
+        for a in args:
+            if getattr(a, "_host_scalar", False):
+                data = self.upload(np.asarray(a._data, dtype=a.dtype).reshape(1))
+                keep.append(data)
+                own = ()
+            else:
+                data, own = a._data, tuple(a.shape)
+            ptrs.append(data.ptr)
+            codes.append(_lib.dtype_code(a.dtype))
+            strides.extend(_broadcast_strides(shape, own))
+        with self._lock:
+            self._require_open()
+            self._check(
+                self._lib.pb_elementwise(
+                    self._ctx, 0, op, len(args), (C.c_void_p * len(ptrs))(*ptrs),
+                    (C.c_int * len(codes))(*codes), _lib.i64_array(strides), len(shape),
+                    _lib.i64_array(shape), _lib.dtype_code(dtype), C.c_void_p(out.ptr)),
+                f"pb_elementwise({name})",
+            )
+        return out
 
     def gather(self, a, shape, offset, strides):
-        raise NotImplementedError("b200 backend implements the linear-algebra path only (gather)")
+        """Strided copy out of ``a``'s flat storage (CUDABackend.gather,
+        src/openpacho/_cuda.py:436-447): element offset and strides."""
+        shape = tuple(int(d) for d in shape)
+        if len(shape) > MAX_DIMS:
+            raise NotImplementedError(f"b200 gather supports at most {MAX_DIMS} dimensions")
+        out = self.empty(shape, a.dtype)
+        if not prod(shape):
+            return out
+        with self._lock:
+            self._require_open()
+            self._check(
+                self._lib.pb_gather(self._ctx, 0, _lib.dtype_code(a.dtype), C.c_void_p(a._data.ptr),
+                                    len(shape), _lib.i64_array(shape), int(offset),
+                                    _lib.i64_array(int(s) for s in strides), C.c_void_p(out.ptr)),
+                "pb_gather",
+            )
+        return out
 
     def reduce(self, a, axes, keepdims, dtype, *, operation="sum"):
-        raise NotImplementedError(f"b200 backend implements the linear-algebra path only ({operation})")
+        """sum/min/max over ``axes`` into ``prod(kept)`` values of ``dtype``
+        (CUDABackend.reduce, src/openpacho/_cuda.py:449-492)."""
+        dtype = self.validate_dtype(dtype)
+        if operation not in _lib.REDUCE_OPS:
+            raise ValueError(f"Unknown reduction operation: {operation}")
+        if dtype.kind == "b" and operation == "sum":
+            raise NotImplementedError("Boolean reduction is not implemented on b200")
+        shape = tuple(a.shape)
+        if len(shape) > MAX_DIMS:
+            raise NotImplementedError(f"b200 reduce supports at most {MAX_DIMS} dimensions")
+        axes = tuple(sorted(axes))
+        count = prod(d for i, d in enumerate(shape) if i not in axes)
+        out = self.empty((count,), dtype)
+        if not count:
+            return out
+        mask = 0
+        for i in axes:
+            mask |= 1 << i
+        with self._lock:
+            self._require_open()
+            self._check(
+                self._lib.pb_reduce(self._ctx, 0, _lib.REDUCE_OPS[operation], _lib.dtype_code(a.dtype),
+                                    C.c_void_p(a._data.ptr), len(shape), _lib.i64_array(shape), mask,
+                                    _lib.dtype_code(dtype), C.c_void_p(out.ptr)),
+                f"pb_reduce({operation})",
+            )
+        return out
 
     # --------------------------------------------------------------- timing
     def launch_count(self) -> int:

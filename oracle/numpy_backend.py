@@ -1,8 +1,10 @@
-"""Restatement of OpenPacho's NumPy backend for matmul and norm (test oracle).
+"""Restatement of OpenPacho's NumPy backend (test oracle): matmul and norm on
+the path, and the elementwise, gather and reduce operations around it.
 
 Each function cites the reference lines it follows.  Inputs and outputs are
 NumPy arrays; shapes and dtypes follow the reference's front end
-(src/openpacho/_array.py:457-479, src/openpacho/linalg.py:8-35).
+(src/openpacho/_array.py:241-281, 389-479, src/openpacho/linalg.py:8-35).
+Test infrastructure only: nothing in the product imports this module.
 """
 
 from __future__ import annotations
@@ -79,3 +81,53 @@ def norm(x: np.ndarray, axis=None, keepdims=False) -> np.ndarray:
         else tuple(d for i, d in enumerate(x.shape) if i not in axes)
     )
     return norm_data(x, axes, x.dtype).reshape(shape)
+
+
+def elementwise(name: str, args, dtype) -> np.ndarray:
+    """src/openpacho/backends.py:109-116: ``cast`` is astype, ``where`` is
+    np.where, everything else the NumPy ufunc of that name, with floating
+    point warnings silenced, then converted to the result dtype."""
+    values = [np.asarray(a) for a in args]
+    if name == "cast":
+        value = values[0].astype(dtype)
+    else:
+        with np.errstate(all="ignore"):
+            value = getattr(np, name)(*values)
+    return np.asarray(value, dtype=dtype)
+
+
+def gather(a: np.ndarray, shape, offset: int, strides) -> np.ndarray:
+    """src/openpacho/backends.py:118-128: a strided view of the flat storage,
+    copied."""
+    flat = np.ascontiguousarray(a).reshape(-1)
+    if not prod(shape):
+        return np.empty(tuple(shape), dtype=a.dtype)
+    view = np.lib.stride_tricks.as_strided(flat[offset:], shape=tuple(shape),
+                                           strides=tuple(s * a.dtype.itemsize for s in strides),
+                                           writeable=False)
+    return np.array(view, copy=True)
+
+
+def _extreme(value: np.ndarray, axes, keepdims, operation) -> np.ndarray:
+    """src/openpacho/_reductions.py:75-90: NumPy extrema, with zero ties
+    resolved to -0 for min and +0 for max."""
+    function = np.min if operation == "min" else np.max
+    result = function(value, axis=axes, keepdims=keepdims)
+    if value.dtype.kind == "f" and np.any(result == 0):
+        negative = np.signbit(value)
+        if operation == "min":
+            sign = np.any((value == 0) & negative, axis=axes, keepdims=keepdims)
+        else:
+            sign = ~np.any((value == 0) & ~negative, axis=axes, keepdims=keepdims)
+        zero = np.copysign(np.zeros_like(result), np.where(sign, -1, 1))
+        result = np.where(result == 0, zero, result).astype(value.dtype, copy=False)
+    return np.asarray(result, dtype=value.dtype)
+
+
+def reduce(a: np.ndarray, axes, keepdims, dtype, operation="sum") -> np.ndarray:
+    """src/openpacho/backends.py:130-136: np.sum with the requested dtype, or
+    the extrema above."""
+    axes = tuple(axes)
+    if operation != "sum":
+        return _extreme(a, axes, keepdims, operation)
+    return np.asarray(np.sum(a, axis=axes, keepdims=keepdims, dtype=dtype))

@@ -139,7 +139,8 @@ def test_validate_dtype(backend):
     from pacho_b200.exceptions import UnsupportedDtypeError
 
     assert backend.validate_dtype("float32") == np.float32
-    for bad in ("int32", "float16", "bool", ">f4"):
+    assert backend.validate_dtype("bool") == np.bool_
+    for bad in ("int32", "float16", "complex64", ">f4"):
         with pytest.raises(UnsupportedDtypeError):
             backend.validate_dtype(bad)
 
@@ -148,10 +149,46 @@ def test_padding_hint_is_declined(backend):
     assert backend.prepare_padded_matmul((33, 17), (17, 65), (33, 65), np.float32) is None
 
 
-def test_off_path_operations_raise(backend):
+def test_elementwise_broadcast_strides_and_codes(backend):
+    a = Operand((4, 1, 3), np.float32, 0x100)
+    b = Operand((5, 1), np.float64, 0x200)
+    backend.elementwise("add", [a, b], (4, 5, 3), np.float64)
+    (name, args), = [c for c in backend._lib.calls if c[0] == "pb_elementwise"]
+    assert args[2] == _lib.EW_OPS["add"] and args[3] == 2
+    assert [args[5][i] for i in range(2)] == [_lib.PB_F32, _lib.PB_F64]
+    # a: (4,1,3) -> strides (3, 0, 1); b: (5,1) padded (1,5,1) -> (0, 1, 0)
+    assert [args[6][i] for i in range(6)] == [3, 0, 1, 0, 1, 0]
+    assert args[7] == 3 and [args[8][i] for i in range(3)] == [4, 5, 3]
+    assert args[9] == _lib.PB_F64
+
+
+def test_elementwise_names_and_limits(backend):
+    assert _lib.EW_OPS["divide"] == _lib.EW_OPS["true_divide"]
+    assert len(set(_lib.EW_OPS.values())) == 23
     with pytest.raises(NotImplementedError):
-        backend.elementwise("add", [], (1,), np.float32)
+        backend.elementwise("arctan2", [], (1,), np.float32)
     with pytest.raises(NotImplementedError):
-        backend.reduce(None, (0,), False, np.float32)
+        backend.elementwise("add", [], (1,) * 9, np.float32)
+    assert backend.elementwise("add", [], (0, 3), np.float32) is not None  # empty: no launch
+    assert not [c for c in backend._lib.calls if c[0] == "pb_elementwise"]
+
+
+def test_reduce_mask_gather_and_float_only_paths(backend):
+    x = Operand((2, 3, 4), np.bool_, 0x300)
+    backend.reduce(x, (0, 2), False, np.float32)
+    (name, args), = [c for c in backend._lib.calls if c[0] == "pb_reduce"]
+    assert args[2] == _lib.PB_REDUCE_SUM and args[3] == _lib.PB_BOOL and args[7] == 0b101
+    assert args[8] == _lib.PB_F32
     with pytest.raises(NotImplementedError):
-        backend.gather(None, (1,), 0, (1,))
+        backend.reduce(x, (0,), False, np.bool_)  # boolean sums, as in the reference
+    with pytest.raises(ValueError):
+        backend.reduce(x, (0,), False, np.float32, operation="prod")
+    backend.gather(Operand((5, 5), np.float32, 0x400), (5,), 0, (6,))
+    (name, args), = [c for c in backend._lib.calls if c[0] == "pb_gather"]
+    assert args[4] == 1 and args[6] == 0 and args[7][0] == 6
+    m = Operand((4, 4), np.bool_, 0x500)
+    with pytest.raises(NotImplementedError):
+        backend.matmul(m, m, (4, 4), np.bool_)
+    with pytest.raises(NotImplementedError):
+        backend.norm(m, (0, 1), False, np.bool_)
+
