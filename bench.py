@@ -1,7 +1,8 @@
 """Benchmark of the b200 linear-algebra path (driver contract: one JSON line).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload gemv_dot|gemm1024|batched|norm|norm_rows|gemm_f32|gemm_f64|vecmat]
+                    [--workload gemv_dot|gemm1024|batched|norm|norm_rows|gemm_f32|gemm_f64|vecmat
+                                |elementwise|reduce]
 
 Default workload = BASELINE config 2 (the metric's memory-bound BLAS-1/2
 config): one step is y = A @ x with A 16384x16384 float32 plus one DOT of two
@@ -10,7 +11,8 @@ two DOT vectors from the same stream).  value = algorithmic bytes / time
 (GB/s), whole job over all ranks; inputs (1.6 GB) are far larger than L2.
 
 Other workloads are BASELINE configs 1, 3, 4 and 5 (TFLOP/s or GB/s), and
-vecmat: x @ A (vector @ matrix, float32 16384^2, GB/s).  Sharded
+vecmat: x @ A (vector @ matrix, float32 16384^2, GB/s), and the operations
+around the path on 2^28 float32 values: elementwise (x + y) and reduce (sum).  Sharded
 ones split across ranks (batch dim for config 3, row blocks of A for config 5,
 contiguous slices + NCCL merge for config 4); config 1 and 2 run one replica
 per rank.  Multi-GPU: one process per GPU under torchrun; barriers and the
@@ -441,6 +443,62 @@ def run_vecmat(gpu: Gpu, args, dist: Dist, result: dict):
     })
 
 
+def run_around(gpu: Gpu, args, dist: Dist, result: dict, which: str):
+    """Operations around the path on 2^28 float32 values (HBM bound):
+    elementwise add of two arrays (pb_elementwise) or their full sum (pb_reduce)."""
+    raw, ctx = gpu.raw, gpu.ctx
+    n = args.n or (1 << 28)
+    rng = np.random.default_rng(6)
+    x = rng.standard_normal(n, dtype=np.float32)
+    dx = gpu.upload(x)
+    F32 = gpu.lib.PB_F32
+    y = None
+    if which == "elementwise":
+        y = rng.standard_normal(n, dtype=np.float32)
+        dy, dz = gpu.upload(y), gpu.empty((n,), np.float32)
+        ptrs = (C.c_void_p * 2)(dx.ptr, dy.ptr)
+        codes = (C.c_int * 2)(F32, F32)
+        strides, shape = gpu.lib.i64_array([1, 1]), gpu.lib.i64_array([n])
+        add = gpu.lib.EW_OPS["add"]
+
+        def step():
+            gpu.check(raw.pb_elementwise(ctx, 0, add, 2, ptrs, codes, strides, 1, shape, F32,
+                                         p_(dz)), "elementwise")
+        step_bytes = 12 * n
+    else:
+        dz = gpu.empty((1,), np.float32)
+        shape = gpu.lib.i64_array([n])
+
+        def step():
+            gpu.check(raw.pb_reduce(ctx, 0, gpu.lib.PB_REDUCE_SUM, F32, p_(dx), 1, shape, 1, F32,
+                                    p_(dz)), "reduce")
+        step_bytes = 4 * n + 4
+
+    for _ in range(args.warmup):
+        step()
+    dist.barrier()
+    with Clocks(gpu.backend.ordinal) as clocks:
+        gpu.busy(step, dist)
+        l0 = gpu.launches()
+        seconds = gpu.timer(step, args.steps)
+    launches = gpu.launches() - l0
+    seconds = dist.max(seconds)
+    z = np.empty(n if which == "elementwise" else 1, np.float32)
+    gpu.check(raw.pb_d2h(ctx, 0, C.c_void_p(z.ctypes.data), p_(dz), z.nbytes), "d2h")
+    what = "elementwise add of two float32 arrays" if which == "elementwise" else "sum of float32 values"
+    result.update({
+        "metric": f"{what} (n = {n}) HBM throughput",
+        "value": step_bytes * args.steps * dist.world / seconds / 1e9, "unit": "GB/s",
+        "ms_per_step": seconds / args.steps * 1e3, "scaling": "weak", "dtype": "f32",
+        "config": {"workload": f"{which}, n = {n} float32, N(0,1), default_rng(6)",
+                   "step_bytes": step_bytes, "parallelism": f"replicas x{dist.world}",
+                   "l2": "operands (1 GB each) larger than the 126 MB L2; no flush needed"},
+        "clocks": clocks.summary(), "gpu_launches": launches,
+        "roofline_kernel": (which, step_bytes, seconds / args.steps),
+        "_check": (which, x, y, z),
+    })
+
+
 def run_batched(gpu: Gpu, args, dist: Dist, result: dict):
     raw, ctx = gpu.raw, gpu.ctx
     A, B = gen_batched()
@@ -624,6 +682,15 @@ def parity_check(check):
         rows = np.random.default_rng(0).choice(A.shape[-2], size=min(64, A.shape[-2]), replace=False)
         a = A[..., rows, :]
         return tolerance.gemm_violations(Cm[..., rows, :], numpy_backend.matmul(a, B), a, B)
+    if kind == "elementwise":
+        _, x, y, z = check
+        return int(np.sum(numpy_backend.elementwise("add", (x, y), np.float32).view(np.uint32)
+                          != z.view(np.uint32)))
+    if kind == "reduce":
+        _, x, _, z = check
+        want = numpy_backend.reduce(x, (0,), False, np.float32)
+        bound = 4 * x.size * tolerance.unit_roundoff(np.float32) * float(np.sum(np.abs(x), dtype=np.float64))
+        return int(abs(float(z[0]) - float(want)) > bound)
     if kind == "norm_rows":
         _, x, out = check
         sel = np.arange(0, x.shape[0], max(1, x.shape[0] // 256))
@@ -639,7 +706,7 @@ def main(argv=None):
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--workload", default="gemv_dot",
                         choices=("gemv_dot", "gemm1024", "batched", "norm", "norm_rows", "gemm_f32",
-                                 "gemm_f64", "vecmat"))
+                                 "gemm_f64", "vecmat", "elementwise", "reduce"))
     parser.add_argument("--dtype", choices=("f32", "f64"), default="f32", help="norm workloads")
     parser.add_argument("--n", type=int, default=0,
                         help="GEMM size override (profiling captures); 0 = the BASELINE size")
@@ -661,6 +728,8 @@ def main(argv=None):
             run_batched(gpu, args, dist, result)
         elif args.workload == "vecmat":
             run_vecmat(gpu, args, dist, result)
+        elif args.workload in ("elementwise", "reduce"):
+            run_around(gpu, args, dist, result, args.workload)
         else:
             run_norm(gpu, args, dist, result, rows=args.workload == "norm_rows")
         check = result.pop("_check")
@@ -669,7 +738,7 @@ def main(argv=None):
         bad = parity_check(check) if dist.rank == 0 else None
         if dist.rank != 0:
             return 0
-        if result["unit"] == "GB/s" or name in ("gemv", "norm", "skinny"):
+        if result["unit"] == "GB/s" or name in ("gemv", "norm", "skinny", "elementwise", "reduce"):
             achieved = work / sec / 1e9
             roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                     "frac": achieved / pk["hbm_gbs"], "kernel": name, "peak_source": pk["source"],

@@ -15,6 +15,9 @@
 // transcendental functions come out within an ulp of the float32 ones.
 // Broadcast operands carry per-dimension element strides (0 = broadcast);
 // contiguous and one-element operands skip the index arithmetic.
+#include <array>
+#include <utility>
+
 #include "pb_internal.cuh"
 
 namespace pb {
@@ -101,6 +104,83 @@ __global__ void __launch_bounds__(kThreads) elementwise_kernel(const EwParams p)
   }
 }
 
+// Every operand contiguous like the output or a single element: groups of
+// four elements, 16-byte loads and stores where the type allows (float32
+// operands, float32 output), two groups in flight per thread.
+__device__ __forceinline__ void load4(const void* p, int dtype, int kind, int64_t i, double (&v)[4]) {
+  if (kind == 2) {
+    v[0] = v[1] = v[2] = v[3] = load(p, dtype, 0);
+  } else if (dtype == PB_F32) {
+    const float4 q = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p) + i));
+    v[0] = q.x, v[1] = q.y, v[2] = q.z, v[3] = q.w;
+  } else if (dtype == PB_F64) {
+    const double2 a = __ldg(reinterpret_cast<const double2*>(static_cast<const double*>(p) + i));
+    const double2 b = __ldg(reinterpret_cast<const double2*>(static_cast<const double*>(p) + i + 2));
+    v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
+  } else {
+    const uchar4 q = *reinterpret_cast<const uchar4*>(static_cast<const unsigned char*>(p) + i);
+    v[0] = q.x ? 1.0 : 0.0, v[1] = q.y ? 1.0 : 0.0, v[2] = q.z ? 1.0 : 0.0, v[3] = q.w ? 1.0 : 0.0;
+  }
+}
+
+__device__ __forceinline__ void store4(void* p, int dtype, int64_t i, const double (&v)[4]) {
+  if (dtype == PB_F32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(p) + i) =
+        make_float4((float)v[0], (float)v[1], (float)v[2], (float)v[3]);
+  } else if (dtype == PB_F64) {
+    double2* d = reinterpret_cast<double2*>(static_cast<double*>(p) + i);
+    d[0] = make_double2(v[0], v[1]);
+    d[1] = make_double2(v[2], v[3]);
+  } else {
+    *reinterpret_cast<uchar4*>(static_cast<unsigned char*>(p) + i) =
+        make_uchar4(v[0] != 0.0, v[1] != 0.0, v[2] != 0.0, v[3] != 0.0);
+  }
+}
+
+constexpr int operands(int op) {
+  return op == PB_EW_WHERE ? 3
+         : (op <= PB_EW_POWER || (op >= PB_EW_EQUAL && op <= PB_EW_GREATER_EQUAL)) ? 2 : 1;
+}
+
+// One instantiation per operation: the operand count is a compile-time
+// constant (operands stay in registers) and only OP's arithmetic is compiled.
+template <int OP>
+__global__ void __launch_bounds__(kThreads) elementwise_dense_kernel(const EwParams p) {
+  constexpr int NA = operands(OP);
+  const int64_t groups = p.count / 4;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  auto group = [&](int64_t g) {
+    double v[3][4] = {};
+#pragma unroll
+    for (int j = 0; j < NA; ++j) load4(p.arg[j], p.dtype[j], p.kind[j], 4 * g, v[j]);
+    double r[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) r[e] = apply(OP, v[0][e], v[1][e], v[2][e]);
+    store4(p.out, p.out_dtype, 4 * g, r);
+  };
+  int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; g + step < groups; g += 2 * step) {
+    group(g);
+    group(g + step);
+  }
+  if (g < groups) group(g);
+  // The last count % 4 elements.
+  const int64_t tail = groups * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (tail < p.count) {
+    double v[3] = {0.0, 0.0, 0.0};
+#pragma unroll
+    for (int j = 0; j < NA; ++j) v[j] = load(p.arg[j], p.dtype[j], p.kind[j] == 2 ? 0 : tail);
+    store(p.out, p.out_dtype, tail, apply(OP, v[0], v[1], v[2]));
+  }
+}
+
+using DenseKernel = void (*)(const EwParams);
+template <int... OPS>
+constexpr auto dense_table(std::integer_sequence<int, OPS...>) {
+  return std::array<DenseKernel, sizeof...(OPS)>{&elementwise_dense_kernel<OPS>...};
+}
+constexpr auto kDense = dense_table(std::make_integer_sequence<int, PB_EW_WHERE + 1>{});
+
 struct GatherParams {
   const unsigned char* src;
   unsigned char* out;
@@ -135,6 +215,7 @@ struct ReduceParams {
   int64_t oshape[kMaxDims], ostride[kMaxDims];  // kept dims: extents, input strides
   int64_t rshape[kMaxDims], rstride[kMaxDims];  // reduced dims
   int64_t count, reduced;
+  int trailing;      // the reduced axes are the last ones: offset = base + r
   int chunks;        // reduced range split into chunks (block per output x chunk)
   int64_t chunk;     // reduced indices per chunk
   double* partial;   // count x chunks when chunks > 1
@@ -178,8 +259,42 @@ __global__ void __launch_bounds__(kThreads) reduce_blocks_kernel(const ReducePar
   const int64_t base = offset_of(p.oshape, p.ostride, p.ondim, o);
   const int64_t r0 = (int64_t)c * p.chunk, r1 = min(p.reduced, r0 + p.chunk);
   double acc = identity(p.op);
-  for (int64_t r = r0 + threadIdx.x; r < r1; r += kThreads)
-    acc = combine(p.op, acc, load(p.src, p.in_dtype, base + offset_of(p.rshape, p.rstride, p.rndim, r)));
+  if (p.trailing && p.in_dtype == PB_F32) {
+    // The reduced axes are the trailing ones: [base + r0, base + r1) is
+    // contiguous.  Scalar head up to 16-byte alignment, float4 body, tail.
+    const float* x = static_cast<const float*>(p.src) + base;
+    int64_t r = r0;
+    const int64_t head = min(r1, r0 + (int64_t)((4 - ((uintptr_t)(x + r0) >> 2 & 3)) & 3));
+    if (r + threadIdx.x < head) acc = combine(p.op, acc, (double)__ldg(x + r + threadIdx.x));
+    r = head;
+    const int64_t body = r + (r1 - r) / 4 * 4;
+    // Four accumulator lanes (one per float4 component), two loads in flight.
+    double lane[4] = {identity(p.op), identity(p.op), identity(p.op), identity(p.op)};
+    int64_t q = r + 4 * (int64_t)threadIdx.x;
+    for (; q + 4 * kThreads < body; q += 8 * kThreads) {
+      const float4 u = __ldg(reinterpret_cast<const float4*>(x + q));
+      const float4 v = __ldg(reinterpret_cast<const float4*>(x + q + 4 * kThreads));
+      lane[0] = combine(p.op, combine(p.op, lane[0], (double)u.x), (double)v.x);
+      lane[1] = combine(p.op, combine(p.op, lane[1], (double)u.y), (double)v.y);
+      lane[2] = combine(p.op, combine(p.op, lane[2], (double)u.z), (double)v.z);
+      lane[3] = combine(p.op, combine(p.op, lane[3], (double)u.w), (double)v.w);
+    }
+    if (q < body) {
+      const float4 u = __ldg(reinterpret_cast<const float4*>(x + q));
+      lane[0] = combine(p.op, lane[0], (double)u.x);
+      lane[1] = combine(p.op, lane[1], (double)u.y);
+      lane[2] = combine(p.op, lane[2], (double)u.z);
+      lane[3] = combine(p.op, lane[3], (double)u.w);
+    }
+    acc = combine(p.op, acc, combine(p.op, combine(p.op, lane[0], lane[1]), combine(p.op, lane[2], lane[3])));
+    if (body + threadIdx.x < r1) acc = combine(p.op, acc, (double)__ldg(x + body + threadIdx.x));
+  } else if (p.trailing) {
+    for (int64_t r = r0 + threadIdx.x; r < r1; r += kThreads)
+      acc = combine(p.op, acc, load(p.src, p.in_dtype, base + r));
+  } else {
+    for (int64_t r = r0 + threadIdx.x; r < r1; r += kThreads)
+      acc = combine(p.op, acc, load(p.src, p.in_dtype, base + offset_of(p.rshape, p.rstride, p.rndim, r)));
+  }
   for (int s = 16; s > 0; s >>= 1) acc = combine(p.op, acc, __shfl_down_sync(0xffffffffu, acc, s));
   if ((threadIdx.x & 31) == 0) warp_part[threadIdx.x >> 5] = acc;
   __syncthreads();
@@ -216,6 +331,17 @@ int64_t grid_for(Device* d, int64_t count) {
   int64_t blocks = ceil_div(count, (int64_t)kThreads);
   const int64_t cap = (int64_t)d->sm_count * 16;
   return blocks < 1 ? 1 : blocks > cap ? cap : blocks;
+}
+
+// Blocks of kThreads that fit on the device at once (one wave), for a
+// grid-stride kernel: more would leave a second, partial wave.
+template <typename K>
+int64_t wave(Device* d, K kernel) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  return (int64_t)per_sm * d->sm_count;
 }
 
 bool valid_dtype(int t) { return t == PB_F32 || t == PB_F64 || t == PB_BOOL; }
@@ -270,7 +396,15 @@ int pb_elementwise(pb_ctx* ctx, int dev, int op, int nargs, const void* const* a
   std::lock_guard<std::recursive_mutex> g(ctx->mu);
   Device* d;
   PB_CHECK(enter(ctx, dev, &d));
-  elementwise_kernel<<<(unsigned)grid_for(d, p.count), kThreads, 0, d->stream>>>(p);
+  bool dense = ((uintptr_t)out & 15) == 0;
+  for (int j = 0; j < nargs; ++j) dense &= p.kind[j] != 0 && ((uintptr_t)p.arg[j] & 15) == 0;
+  if (dense) {
+    int64_t blocks = ceil_div(p.count / 4 + 1, (int64_t)kThreads);
+    const int64_t cap = wave(d, kDense[op]);
+    kDense[op]<<<(unsigned)(blocks < cap ? blocks : cap), kThreads, 0, d->stream>>>(p);
+  } else {
+    elementwise_kernel<<<(unsigned)grid_for(d, p.count), kThreads, 0, d->stream>>>(p);
+  }
   PB_LAUNCHED(d);
   return PB_OK;
 }
@@ -333,6 +467,11 @@ int pb_reduce(pb_ctx* ctx, int dev, int op, int in_dtype, const void* src, int n
     strides[k] = stride;
     stride *= shape[k];
   }
+  int first_reduced = ndim;
+  for (int k = 0; k < ndim; ++k)
+    if ((axes_mask >> k & 1u) && first_reduced == ndim) first_reduced = k;
+  p.trailing = 1;
+  for (int k = first_reduced; k < ndim; ++k) p.trailing &= (int)(axes_mask >> k & 1u);
   for (int k = 0; k < ndim; ++k) {
     if (axes_mask >> k & 1u) {
       p.rshape[p.rndim] = shape[k];
@@ -360,8 +499,8 @@ int pb_reduce(pb_ctx* ctx, int dev, int op, int in_dtype, const void* src, int n
     PB_LAUNCHED(d);
     return PB_OK;
   }
-  // Enough blocks for a wave, at least 4096 reduced indices each.
-  int64_t chunks = ceil_div((int64_t)d->sm_count * 8, p.count);
+  // One wave of blocks, at least 4096 reduced indices each.
+  int64_t chunks = wave(d, reduce_blocks_kernel) / p.count;
   const int64_t most = ceil_div(p.reduced, (int64_t)4096);
   if (chunks > most) chunks = most;
   if (chunks < 1) chunks = 1;
