@@ -65,6 +65,9 @@ int pb_abi_version(void);
 int pb_device_count(int* count);
 int pb_device_info(int ordinal, char* name, size_t name_len, size_t* total_bytes,
                    int* sm_count, int* cc_major, int* cc_minor);
+/* CUDA driver version (e.g. 13000), the `driver` field of the reference's
+ * DeviceInfo records (src/openpacho/_cuda.py:68-94). */
+int pb_driver_version(int* version);
 
 /* ---- context / memory (CUDABackend.__init__/empty/upload/download/close,
  *      src/openpacho/_cuda.py:138-199, 232-311, 644-673) ------------------ */

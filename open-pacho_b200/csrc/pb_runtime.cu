@@ -152,6 +152,14 @@ int pb_device_count(int* count) {
   return PB_OK;
 }
 
+int pb_driver_version(int* version) {
+  if (!version) PB_FAIL(PB_ERR_INVALID, "null version");
+  *version = 0;
+  cudaError_t e = cudaDriverGetVersion(version);
+  if (e != cudaSuccess) PB_FAIL(PB_ERR_UNAVAILABLE, "no CUDA driver: %s", cudaGetErrorString(e));
+  return PB_OK;
+}
+
 int pb_device_info(int ordinal, char* name, size_t name_len, size_t* total_bytes, int* sm_count,
                    int* cc_major, int* cc_minor) {
   cudaDeviceProp p;

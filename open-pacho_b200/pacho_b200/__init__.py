@@ -9,6 +9,8 @@
   ``amin``/``amax``, ``transpose``/``diag`` -- the same public API for
   environments without OpenPacho.
 * :mod:`pacho_b200.distributed` -- sharded GEMM and norm across GPUs (NCCL).
+* ``devices()`` and ``python -m pacho_b200 devices|benchmark`` -- discovery and
+  the synchronized benchmark of OpenPacho's ``pacho`` command.
 """
 
 from . import linalg
@@ -62,6 +64,7 @@ from .api import (
     zeros_like,
 )
 from .backend import B200Backend, DeviceBuffer
+from .discovery import DeviceInfo, devices
 from .exceptions import BackendMismatchError, BackendUnavailableError, UnsupportedDtypeError
 from .register import register, unregister
 
@@ -72,10 +75,12 @@ __all__ = [
     "BackendMismatchError",
     "BackendUnavailableError",
     "DeviceBuffer",
+    "DeviceInfo",
     "UnsupportedDtypeError",
     "array",
     "asarray",
     "asnumpy",
+    "devices",
     "dot",
     "empty",
     "full",

@@ -62,6 +62,7 @@ _ctx = C.c_void_p
 PROTOTYPES = {
     "pb_abi_version": [],
     "pb_device_count": [C.POINTER(C.c_int)],
+    "pb_driver_version": [C.POINTER(C.c_int)],
     "pb_device_info": [_i, C.c_char_p, _sz, C.POINTER(C.c_size_t), C.POINTER(C.c_int),
                        C.POINTER(C.c_int), C.POINTER(C.c_int)],
     "pb_init": [_i, C.POINTER(C.c_int), C.POINTER(_ctx)],

@@ -185,6 +185,30 @@ class ndarray(NDArrayOperatorsMixin):
             shape = shape[0]
         return reshape(self, shape, order=order)
 
+    # src/openpacho/_array.py:84-86, 145-160
+    @property
+    def T(self):
+        return transpose(self)
+
+    def transpose(self, *axes):
+        if len(axes) == 1 and (axes[0] is None or isinstance(axes[0], (tuple, list))):
+            axes = axes[0]
+        return transpose(self, axes or None)
+
+    def sum(self, axis=None, dtype=None, out=None, keepdims=False):
+        return sum(self, axis=axis, dtype=dtype, out=out, keepdims=keepdims)
+
+    def mean(self, axis=None, dtype=None, out=None, keepdims=False):
+        return mean(self, axis=axis, dtype=dtype, out=out, keepdims=keepdims)
+
+    def min(self, axis=None, out=None, keepdims=False, initial=None, where=None):
+        return amin(self, axis, out, keepdims, _UNSET if initial is None else initial,
+                    _UNSET if where is None else where)
+
+    def max(self, axis=None, out=None, keepdims=False, initial=None, where=None):
+        return amax(self, axis, out, keepdims, _UNSET if initial is None else initial,
+                    _UNSET if where is None else where)
+
 
 def array(obj, dtype=None, *, copy=True, order="C", backend=None):
     if order != "C":

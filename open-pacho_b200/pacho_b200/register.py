@@ -75,6 +75,7 @@ def register(openpacho=None):
     get_backend.__wrapped__ = original
     get_backend.__doc__ = original.__doc__
     backends.get_backend = get_backend
+    _wrap_devices(openpacho, backends)
     for name in ("_array", "random"):
         try:
             module = importlib.import_module(f"{openpacho.__name__}.{name}")
@@ -85,6 +86,41 @@ def register(openpacho=None):
     if getattr(openpacho, "get_backend", None) is original:
         openpacho.get_backend = get_backend
     return openpacho
+
+
+def _wrap_devices(openpacho, backends):
+    """``devices("b200")`` (src/openpacho/backends.py:50-60, bound by name in
+    the package and its CLI) lists b200 devices as OpenPacho's DeviceInfo."""
+    import importlib
+
+    from .discovery import devices as b200_devices
+
+    original = backends.devices
+
+    def devices(backend="opencl"):
+        if backend == "b200":
+            return [backends.DeviceInfo(**vars(d)) for d in b200_devices("b200")]
+        return original(backend)
+
+    setattr(devices, _MARK, True)
+    devices.__wrapped__ = original
+    devices.__doc__ = original.__doc__
+    backends.devices = devices
+    for module in (openpacho, importlib.import_module(openpacho.__name__ + ".cli")):
+        if getattr(module, "devices", None) is original:
+            module.devices = devices
+
+
+def _unwrap_devices(openpacho, backends):
+    import importlib
+
+    wrapped = backends.devices
+    if not getattr(wrapped, _MARK, False):
+        return
+    backends.devices = wrapped.__wrapped__
+    for module in (openpacho, importlib.import_module(openpacho.__name__ + ".cli")):
+        if getattr(module, "devices", None) is wrapped:
+            module.devices = wrapped.__wrapped__
 
 
 def unregister(openpacho=None):
@@ -108,3 +144,4 @@ def unregister(openpacho=None):
             module.get_backend = original
     if getattr(openpacho, "get_backend", None) is wrapped:
         openpacho.get_backend = original
+    _unwrap_devices(openpacho, backends)

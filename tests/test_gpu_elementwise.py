@@ -187,3 +187,17 @@ def test_conjugate_gradient_through_the_api(b200):
     assert residual < 1e-8
     assert np.allclose(x_gpu, x_cpu, rtol=1e-9, atol=1e-10)
     assert pb.linalg.norm(db - dA @ pb.asarray(x_gpu, backend=b200)).item() / np.linalg.norm(b) < 1e-8
+
+
+def test_cli_benchmark_and_devices(b200, capsys):
+    from pacho_b200 import cli
+
+    for dtype in ("float32", "float64"):
+        report = cli.benchmark(size=256, repeat=2, dtype=dtype)
+        assert report["schema_version"] == 1 and report["backend"] == "b200"
+        assert [c["operation"] for c in report["cases"]] == ["add", "matmul", "sum"]
+        assert report["all_valid"], report["cases"]
+    assert cli.main(["devices", "--json"]) == 0
+    listed = __import__("json").loads(capsys.readouterr().out)
+    assert listed and all(d["vendor"] == "NVIDIA" and d["fp64"] for d in listed)
+    assert any("B200" in d["name"] for d in listed)
