@@ -954,6 +954,26 @@ __global__ void __launch_bounds__(T_THREADS, 1)
       ++gc;
     };
 
+    // The epilogue of a tile (its last promote and the store) is deferred
+    // until the first chunk of the next tile has been split, so the tensor
+    // pipe works on that chunk (the other TMEM buffer) meanwhile.  Promotes
+    // stay in chunk order.
+    int64_t pending = -1;  // work item whose epilogue is deferred
+    auto epilogue = [&]() {
+      promote();  // the pending tile's last chunk
+      if (!ok || *abort_flag) return;
+      const TileCoord ptc = tile_coord(p, pending / p.ksplit);
+      const int psplit = (int)(pending % p.ksplit);
+      const int64_t col0 = ptc.n_tile * FBN + half * COLS;
+      if (p.tma_store)
+        store_tma<COLS>(p, &map_c, ptc, psplit, quad, col0, acc,
+                        reinterpret_cast<float4*>(gbase + L::OUT + (warp - 2) * 4096),
+                        base + L::OUT + (warp - 2) * 4096);
+      else
+        finish_item<COLS>(p, ptc, psplit, ptc.m_tile * BM + row, col0, acc);
+    };
+#pragma unroll
+    for (int i = 0; i < COLS; ++i) acc[i] = 0.0f;
     for (int64_t w = blockIdx.x; w < items && ok; w += gridDim.x) {
       const TileCoord tc = tile_coord(p, w / p.ksplit);
       const int split = (int)(w % p.ksplit);
@@ -962,8 +982,6 @@ __global__ void __launch_bounds__(T_THREADS, 1)
       int64_t ao, bo;
       batch_offsets(p.map, tc.bz, &ao, &bo);
       const int64_t arow = ao * p.M + tc.m_tile * BM + row;  // row of A over all matrices
-#pragma unroll
-      for (int i = 0; i < COLS; ++i) acc[i] = 0.0f;
       for (int kb = kb0; kb < kb1 && ok; ++kb, ++g) {
         const int s = (int)(g % S);
         const bool got = mbar_wait(full0 + 8 * s, (uint32_t)((g / S) & 1), abort_flag, p.err);
@@ -1009,18 +1027,22 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         if (lane == 0) mbar_arrive(ready0 + 8 * s);
         const int c = (kb - kb0) / FCHUNK;
         const bool chunk_end = (kb - kb0) % FCHUNK == FCHUNK - 1 || kb == kb1 - 1;
-        if (chunk_end && c >= 1) promote();  // chunk c-1
+        if (chunk_end) {
+          if (c >= 1) {
+            promote();  // chunk c-1 of this tile
+          } else if (pending >= 0) {
+            epilogue();  // the previous tile, now that this tile's first chunk is split
+            pending = -1;
+            if (!ok || *abort_flag) break;
+#pragma unroll
+            for (int i = 0; i < COLS; ++i) acc[i] = 0.0f;
+          }
+        }
       }
-      if (ok) promote();  // the tile's last chunk
       if (!ok || *abort_flag) break;
-      const int64_t col0 = tc.n_tile * FBN + half * COLS;
-      if (p.tma_store)
-        store_tma<COLS>(p, &map_c, tc, split, quad, col0, acc,
-                        reinterpret_cast<float4*>(gbase + L::OUT + (warp - 2) * 4096),
-                        base + L::OUT + (warp - 2) * 4096);
-      else
-        finish_item<COLS>(p, tc, split, tc.m_tile * BM + row, col0, acc);
+      pending = w;
     }
+    if (pending >= 0 && ok && !*abort_flag) epilogue();
     if (lane == 0) bulk_wait_all();  // staging buffers are read before the CTA exits
   }
 
