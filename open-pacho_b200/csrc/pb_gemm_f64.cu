@@ -1,4 +1,4 @@
-// float64 GEMM on the FP64 tensor path (DMMA, mma.sync m16n8k4 .f64).
+// float64 GEMM on the FP64 tensor path (DMMA, mma.sync m16n8k4 .f64; m16n8k8 selectable).
 //
 // Reference: the custom CUDA provider computes every float64 product with one
 // thread per output and a serial K loop (src/openpacho/_cuda.py:619-636); the
@@ -17,7 +17,19 @@
 namespace pb {
 namespace {
 
-constexpr int TM = 128, TN = 128, TK = 16, PITCH = TK + 4, NSTAGE = 4, NT = 256;
+// Measured on B200 (8192^3, TFLOP/s): m16n8k4, TK 16, 4 stages 28.5; m16n8k8
+// 27.9; TK 32 with 3 stages 22.2 (k4) / 22.8 (k8).  The defaults are the best.
+#ifndef PB_DMMA_K
+#define PB_DMMA_K 4  // DMMA shape m16n8k4 or m16n8k8
+#endif
+#ifndef PB_DMMA_TK
+#define PB_DMMA_TK 16  // K per shared-memory stage
+#endif
+#ifndef PB_DMMA_STAGES
+#define PB_DMMA_STAGES 4
+#endif
+constexpr int TM = 128, TN = 128, TK = PB_DMMA_TK, PITCH = TK + 4, NSTAGE = PB_DMMA_STAGES, NT = 256;
+static_assert(TK % PB_DMMA_K == 0 && (TM * TK) % NT == 0, "stage shape");
 constexpr int STAGE_DOUBLES = (TM + TN) * PITCH;
 
 struct DmmaParams {
@@ -54,6 +66,15 @@ __device__ __forceinline__ void dmma(double (&c)[4], double a0, double a1, doubl
       : "d"(a0), "d"(a1), "d"(b0));
 }
 
+// m16n8k8: a = (g, t), (g+8, t), (g, t+4), (g+8, t+4); b = (t, g), (t+4, g).
+__device__ __forceinline__ void dmma8(double (&c)[4], const double (&a)[4], const double (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f64.f64.f64.f64 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+d"(c[0]), "+d"(c[1]), "+d"(c[2]), "+d"(c[3])
+      : "d"(a[0]), "d"(a[1]), "d"(a[2]), "d"(a[3]), "d"(b[0]), "d"(b[1]));
+}
+
 __global__ void __launch_bounds__(NT, 1) dmma_gemm_kernel(DmmaParams p) {
   extern __shared__ __align__(16) double smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -80,20 +101,18 @@ __global__ void __launch_bounds__(NT, 1) dmma_gemm_kernel(DmmaParams p) {
       double* sa = smem + stage * STAGE_DOUBLES;
       double* sb = sa + TM * PITCH;
       const int64_t k0 = kt * TK;
-      const int kk = lane & 15;
-      const int64_t gk = k0 + kk;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int r = warp * 16 + 2 * i + (lane >> 4);
-        const int64_t gr = m0 + r;
+      for (int i = 0; i < TM * TK / NT; ++i) {
+        const int idx = i * NT + tid, r = idx / TK, kk = idx % TK;
+        const int64_t gr = m0 + r, gk = k0 + kk;
         const bool ok = gr < M && gk < K;
         cp_async8(smem_u32(sa + r * PITCH + kk), ok ? (const void*)(A + gr * K + gk) : (const void*)A,
                   ok ? 8 : 0);
       }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int n = warp * 16 + 2 * i + (lane >> 4);
-        const int64_t gn = n0 + n;
+      for (int i = 0; i < TN * TK / NT; ++i) {
+        const int idx = i * NT + tid, n = idx / TK, kk = idx % TK;
+        const int64_t gn = n0 + n, gk = k0 + kk;
         const bool ok = gk < K && gn < N;
         cp_async8(smem_u32(sb + n * PITCH + kk), ok ? (const void*)(B + gk * N + gn) : (const void*)B,
                   ok ? 8 : 0);
@@ -121,6 +140,28 @@ __global__ void __launch_bounds__(NT, 1) dmma_gemm_kernel(DmmaParams p) {
       cp_async_commit();
       const double* sa = smem + (kt % NSTAGE) * STAGE_DOUBLES + (wm * 64) * PITCH;
       const double* sb = smem + (kt % NSTAGE) * STAGE_DOUBLES + TM * PITCH + (wn * 32) * PITCH;
+#if PB_DMMA_K == 8
+#pragma unroll
+      for (int k8 = 0; k8 < TK; k8 += 8) {
+        double a[4][4], b[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          a[i][0] = sa[(i * 16 + g) * PITCH + k8 + t];
+          a[i][1] = sa[(i * 16 + g + 8) * PITCH + k8 + t];
+          a[i][2] = sa[(i * 16 + g) * PITCH + k8 + t + 4];
+          a[i][3] = sa[(i * 16 + g + 8) * PITCH + k8 + t + 4];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          b[j][0] = sb[(j * 8 + g) * PITCH + k8 + t];
+          b[j][1] = sb[(j * 8 + g) * PITCH + k8 + t + 4];
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dmma8(acc[i][j], a[i], b[j]);
+      }
+#else
 #pragma unroll
       for (int k4 = 0; k4 < TK; k4 += 4) {
         double a[4][2], b[4];
@@ -136,6 +177,7 @@ __global__ void __launch_bounds__(NT, 1) dmma_gemm_kernel(DmmaParams p) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) dmma(acc[i][j], a[i][0], a[i][1], b[j]);
       }
+#endif
     }
     cp_async_wait<0>();
     __syncthreads();
