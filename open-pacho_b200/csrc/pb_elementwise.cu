@@ -174,12 +174,92 @@ __global__ void __launch_bounds__(kThreads) elementwise_dense_kernel(const EwPar
   }
 }
 
+// Correctly rounded operations on float32 operands into float32 (or bool)
+// give the same bits in float32 as in float64 rounded once, so they run in
+// float32: no conversions, fewer registers, more resident blocks.
+constexpr bool exact_in_f32(int op) {
+  return op != PB_EW_POWER && !(op >= PB_EW_EXP && op <= PB_EW_TANH);
+}
+
+__device__ __forceinline__ float apply_f32(int op, float a, float b, float c) {
+  switch (op) {
+    case PB_EW_ADD: return a + b;
+    case PB_EW_SUBTRACT: return a - b;
+    case PB_EW_MULTIPLY: return a * b;
+    case PB_EW_DIVIDE: return a / b;
+    case PB_EW_NEGATIVE: return -a;
+    case PB_EW_POSITIVE: return a;
+    case PB_EW_ABSOLUTE: return fabsf(a);
+    case PB_EW_SQRT: return sqrtf(a);
+    case PB_EW_EQUAL: return a == b;
+    case PB_EW_NOT_EQUAL: return a != b;
+    case PB_EW_LESS: return a < b;
+    case PB_EW_LESS_EQUAL: return a <= b;
+    case PB_EW_GREATER: return a > b;
+    case PB_EW_GREATER_EQUAL: return a >= b;
+    case PB_EW_ISFINITE: return isfinite(a);
+    case PB_EW_CAST: return a;
+    default: return a != 0.0f ? b : c;  // PB_EW_WHERE
+  }
+}
+
+// Every operand and the output float32 (bool output for comparisons),
+// operation exact in float32: float4 in, float4 (or uchar4) out.
+template <int OP>
+__global__ void __launch_bounds__(kThreads) elementwise_f32_kernel(const EwParams p) {
+  constexpr int NA = operands(OP);
+  const int64_t groups = p.count / 4;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  auto load4f = [&](int j, int64_t i) {
+    if (p.kind[j] == 2) {
+      const float v = __ldg(static_cast<const float*>(p.arg[j]));
+      return make_float4(v, v, v, v);
+    }
+    return __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p.arg[j]) + i));
+  };
+  auto group = [&](int64_t g) {
+    float4 v[3] = {};
+#pragma unroll
+    for (int j = 0; j < NA; ++j) v[j] = load4f(j, 4 * g);
+    const float4 r = make_float4(apply_f32(OP, v[0].x, v[1].x, v[2].x), apply_f32(OP, v[0].y, v[1].y, v[2].y),
+                                 apply_f32(OP, v[0].z, v[1].z, v[2].z), apply_f32(OP, v[0].w, v[1].w, v[2].w));
+    if (p.out_dtype == PB_F32)
+      *reinterpret_cast<float4*>(static_cast<float*>(p.out) + 4 * g) = r;
+    else
+      *reinterpret_cast<uchar4*>(static_cast<unsigned char*>(p.out) + 4 * g) =
+          make_uchar4(r.x != 0.0f, r.y != 0.0f, r.z != 0.0f, r.w != 0.0f);
+  };
+  int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; g + step < groups; g += 2 * step) {
+    group(g);
+    group(g + step);
+  }
+  if (g < groups) group(g);
+  const int64_t tail = groups * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (tail < p.count) {
+    float v[3] = {0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < NA; ++j) v[j] = __ldg(static_cast<const float*>(p.arg[j]) + (p.kind[j] == 2 ? 0 : tail));
+    const float r = apply_f32(OP, v[0], v[1], v[2]);
+    if (p.out_dtype == PB_F32)
+      static_cast<float*>(p.out)[tail] = r;
+    else
+      static_cast<unsigned char*>(p.out)[tail] = r != 0.0f;
+  }
+}
+
 using DenseKernel = void (*)(const EwParams);
 template <int... OPS>
 constexpr auto dense_table(std::integer_sequence<int, OPS...>) {
   return std::array<DenseKernel, sizeof...(OPS)>{&elementwise_dense_kernel<OPS>...};
 }
+template <int... OPS>
+constexpr auto f32_table(std::integer_sequence<int, OPS...>) {
+  return std::array<DenseKernel, sizeof...(OPS)>{
+      (exact_in_f32(OPS) ? &elementwise_f32_kernel<exact_in_f32(OPS) ? OPS : 0> : nullptr)...};
+}
 constexpr auto kDense = dense_table(std::make_integer_sequence<int, PB_EW_WHERE + 1>{});
+constexpr auto kDenseF32 = f32_table(std::make_integer_sequence<int, PB_EW_WHERE + 1>{});
 
 struct GatherParams {
   const unsigned char* src;
@@ -399,9 +479,13 @@ int pb_elementwise(pb_ctx* ctx, int dev, int op, int nargs, const void* const* a
   bool dense = ((uintptr_t)out & 15) == 0;
   for (int j = 0; j < nargs; ++j) dense &= p.kind[j] != 0 && ((uintptr_t)p.arg[j] & 15) == 0;
   if (dense) {
+    bool f32 = kDenseF32[op] != nullptr && (out_dtype == PB_F32 || out_dtype == PB_BOOL);
+    for (int j = 0; j < nargs; ++j) f32 &= p.dtype[j] == PB_F32;
+    if (op == PB_EW_WHERE) f32 = false;  // a bool condition operand
+    const DenseKernel kernel = f32 ? kDenseF32[op] : kDense[op];
     int64_t blocks = ceil_div(p.count / 4 + 1, (int64_t)kThreads);
-    const int64_t cap = wave(d, kDense[op]);
-    kDense[op]<<<(unsigned)(blocks < cap ? blocks : cap), kThreads, 0, d->stream>>>(p);
+    const int64_t cap = wave(d, kernel);
+    kernel<<<(unsigned)(blocks < cap ? blocks : cap), kThreads, 0, d->stream>>>(p);
   } else {
     elementwise_kernel<<<(unsigned)grid_for(d, p.count), kThreads, 0, d->stream>>>(p);
   }

@@ -215,11 +215,7 @@ int gemm_dmma_f64(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
   if (gx > INT32_MAX || gy > 65535) PB_FAIL(PB_ERR_UNSUPPORTED, "GEMM grid too large");
   const unsigned gz = (unsigned)(batch < 65535 ? batch : 65535);
   const int smem = NSTAGE * STAGE_DOUBLES * (int)sizeof(double);
-  static bool configured = false;
-  if (!configured) {
-    PB_CUDA(cudaFuncSetAttribute(dmma_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured = true;
-  }
+  PB_CHECK(allow_smem(d, (const void*)dmma_gemm_kernel, smem));
   dmma_gemm_kernel<<<dim3((unsigned)gx, (unsigned)gy, gz), NT, smem, d->stream>>>(p);
   PB_LAUNCHED(d);
   return PB_OK;

@@ -163,12 +163,7 @@ int launch_simt(Device* d, const BatchMap& map, int64_t batch, int64_t M, int64_
   if (gx > INT32_MAX || gy > 65535) PB_FAIL(PB_ERR_UNSUPPORTED, "GEMM grid too large");
   const unsigned gz = (unsigned)(batch < 65535 ? batch : 65535);
   const size_t smem = 2 * BK * (BM + BN) * sizeof(T);
-  static bool configured[2] = {false, false};
-  if (!configured[sizeof(T) == 8]) {
-    PB_CUDA(cudaFuncSetAttribute(simt_gemm_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem));
-    configured[sizeof(T) == 8] = true;
-  }
+  PB_CHECK(allow_smem(d, (const void*)simt_gemm_kernel<T>, smem));
   simt_gemm_kernel<T><<<dim3((unsigned)gx, (unsigned)gy, gz), NT, smem, d->stream>>>(p);
   PB_LAUNCHED(d);
   return PB_OK;
@@ -183,12 +178,7 @@ int gemm_nonfinite_repair_f32(Device* d, const BatchMap& map, int64_t batch, int
   const int64_t tiles = batch * ceil_div(M, (int64_t)BM) * ceil_div(N, (int64_t)BN);
   const unsigned grid = (unsigned)(tiles < d->sm_count ? tiles : d->sm_count);
   const size_t smem = 2 * BK * (BM + BN) * sizeof(float);
-  static bool configured = false;
-  if (!configured) {
-    PB_CUDA(cudaFuncSetAttribute(simt_gemm_kernel<float>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    configured = true;
-  }
+  PB_CHECK(allow_smem(d, (const void*)simt_gemm_kernel<float>, smem));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(NT);

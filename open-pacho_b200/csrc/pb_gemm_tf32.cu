@@ -1167,12 +1167,7 @@ int encode_kmajor(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols
 template <int BN>
 int launch_tf32(Device* d, const CUtensorMap& ma, const CUtensorMap& mb, const Tf32Params& p) {
   const int smem = Smem<BN>::TOTAL;
-  static bool configured = false;
-  if (!configured) {
-    PB_CUDA(cudaFuncSetAttribute(tf32x3_gemm_kernel<BN>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured = true;
-  }
+  PB_CHECK(allow_smem(d, (const void*)tf32x3_gemm_kernel<BN>, smem));
   // Persistent: one CTA per SM (shared memory allows no more), work items strided.
   const int64_t items = p.tiles * p.ksplit;
   const int64_t grid = items < d->sm_count ? items : d->sm_count;
@@ -1216,12 +1211,7 @@ template <int FBN>
 int launch_tmem(Device* d, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
                 const Tf32Params& p, int64_t Kp) {
   const int smem = TSmem<FBN>::TOTAL;
-  static bool configured = false;
-  if (!configured) {
-    PB_CUDA(cudaFuncSetAttribute(tf32x3_tmem_kernel<FBN>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured = true;
-  }
+  PB_CHECK(allow_smem(d, (const void*)tf32x3_tmem_kernel<FBN>, smem));
   const int64_t items = p.tiles * p.ksplit;
   const int64_t grid = items < d->sm_count ? items : d->sm_count;
   return launch_dependent(d, tf32x3_tmem_kernel<FBN>, dim3((unsigned)grid), dim3(T_THREADS),

@@ -7,6 +7,8 @@
 #include <stdio.h>
 #include <atomic>
 #include <mutex>
+#include <set>
+#include <utility>
 #include <string>
 
 #include "../../include/pacho_b200.h"
@@ -105,6 +107,19 @@ int enter(pb_ctx* ctx, int dev, Device** out);
 int scratch(Device* d, size_t bytes, void** out);
 // Ensure at least `n` zeroed counters; returns the pointer.
 int counters(Device* d, size_t n, unsigned int** out);
+// Raise `kernel`'s dynamic shared-memory limit to `bytes` on d's device, once
+// per (kernel, device): the attribute is per device, so a context over
+// several devices sets it on each.  The device must be current (enter()).
+inline int allow_smem(Device* d, const void* kernel, size_t bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  std::lock_guard<std::mutex> g(mu);
+  const auto key = std::make_pair(kernel, d->ordinal);
+  if (done.count(key)) return PB_OK;
+  PB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  done.insert(key);
+  return PB_OK;
+}
 // Fill `count` elements of dtype PB_F32 / PB_F64 / PB_BOOL with `value`.
 int fill_device(Device* d, int dtype, void* dst, size_t count, double value);
 // Ensure at least `n` operand tag words; returns them and a fresh generation.

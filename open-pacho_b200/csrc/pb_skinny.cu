@@ -168,12 +168,8 @@ template <typename T, int MR>
 int launch_rows(Device* d, SkinnyParams<T>& p, bool aligned) {
   constexpr int V = Vec16<T>::n;
   const size_t smem = ((size_t)kThreads * V + kStageK) * MR * sizeof(T);
-  static bool configured[2] = {false, false};
   auto kernel = aligned ? skinny_kernel<T, MR, true> : skinny_kernel<T, MR, false>;
-  if (!configured[aligned]) {
-    PB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    configured[aligned] = true;
-  }
+  PB_CHECK(allow_smem(d, (const void*)kernel, smem));
   const unsigned gz = (unsigned)(p.batch < 65535 ? p.batch : 65535);
   kernel<<<dim3((unsigned)p.strips, (unsigned)p.ksplit, gz), kThreads, smem, d->stream>>>(p);
   PB_LAUNCHED(d);
