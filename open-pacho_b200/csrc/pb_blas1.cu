@@ -252,9 +252,9 @@ struct GemvPlan {
   int64_t blocks;
 };
 
-GemvPlan plan_gemv(int64_t rows, int64_t K, int64_t elem, int sm_count) {
+// `resident`: blocks of the split kernel that fit at once (one wave).
+GemvPlan plan_gemv(int64_t rows, int64_t K, int64_t elem, int64_t resident) {
   GemvPlan p;
-  const int64_t resident = (int64_t)sm_count * (2048 / kThreads);
   if (rows >= 2 * resident || K * elem <= 16384) {
     // Whole rows per block: one warp per row up to 32 KiB rows (warp-only
     // reduction), more warps per row beyond that.
@@ -278,15 +278,17 @@ GemvPlan plan_gemv(int64_t rows, int64_t K, int64_t elem, int sm_count) {
   return p;
 }
 
-// Grid of the whole-row kernel: persistent (capped at PB_GEMV_PERSIST waves).
-int64_t rows_grid(const GemvPlan& p, int sm_count) {
-  const int64_t cap = (int64_t)PB_GEMV_PERSIST * sm_count * (2048 / kThreads);
+// Grid of the whole-row kernel: persistent (capped at PB_GEMV_PERSIST waves
+// of its resident blocks).
+int64_t rows_grid(const GemvPlan& p, int64_t resident) {
+  const int64_t cap = (int64_t)PB_GEMV_PERSIST * resident;
   return p.blocks < cap ? p.blocks : cap;
 }
 
 template <typename T, bool STREAM_X>
 int launch_gemv(Device* d, const T* A, const T* x, T* y, int64_t rows, int64_t K, int64_t lda) {
-  GemvPlan p = plan_gemv(rows, K, sizeof(T), d->sm_count);
+  GemvPlan p = plan_gemv(rows, K, sizeof(T),
+                         resident_blocks(d, (const void*)gemv_kernel<T, true, STREAM_X>, kThreads));
   if (p.blocks > INT32_MAX) PB_FAIL(PB_ERR_UNSUPPORTED, "GEMV grid too large");
   T* partial = nullptr;
   unsigned int* cnt = nullptr;
@@ -300,7 +302,8 @@ int launch_gemv(Device* d, const T* A, const T* x, T* y, int64_t rows, int64_t K
   bool aligned = ((uintptr_t)A % 16 == 0) && ((uintptr_t)x % 16 == 0) &&
                  (rows == 1 || lda % VN == 0) && (p.chunk % VN == 0);
   if (p.nchunks == 1 && !STREAM_X && lda == K && K < INT32_MAX) {
-    const unsigned grid = (unsigned)rows_grid(p, d->sm_count);
+    const unsigned grid =
+        (unsigned)rows_grid(p, resident_blocks(d, (const void*)gemv_rows_kernel<T, true>, kThreads));
     if (aligned)
       gemv_rows_kernel<T, true><<<grid, kThreads, 0, d->stream>>>(A, x, y, rows, (int)K,
                                                                    p.rows_per_block);
@@ -355,7 +358,8 @@ int dot_scratch_address(Device* d, void** out) {
 
 template <typename T>
 int launch_dot_static(Device* d, const T* x, const T* y, T* out, int64_t n) {
-  GemvPlan p = plan_gemv(1, n, sizeof(T), d->sm_count);
+  GemvPlan p = plan_gemv(1, n, sizeof(T),
+                         resident_blocks(d, (const void*)gemv_kernel<T, true, true>, kThreads));
   if (p.nchunks > kStaticDotPartials)
     PB_FAIL(PB_ERR_UNSUPPORTED,
             "pb_dot_noalloc: this DOT needs %d partial sums but the static scratch holds %d",

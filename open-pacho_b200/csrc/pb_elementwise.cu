@@ -417,11 +417,7 @@ int64_t grid_for(Device* d, int64_t count) {
 // grid-stride kernel: more would leave a second, partial wave.
 template <typename K>
 int64_t wave(Device* d, K kernel) {
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0) != cudaSuccess ||
-      per_sm < 1)
-    per_sm = 1;
-  return (int64_t)per_sm * d->sm_count;
+  return resident_blocks(d, (const void*)kernel, kThreads);
 }
 
 bool valid_dtype(int t) { return t == PB_F32 || t == PB_F64 || t == PB_BOOL; }

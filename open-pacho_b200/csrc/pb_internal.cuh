@@ -6,6 +6,7 @@
 #include <stdint.h>
 #include <stdio.h>
 #include <atomic>
+#include <map>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -119,6 +120,24 @@ inline int allow_smem(Device* d, const void* kernel, size_t bytes) {
   PB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
   done.insert(key);
   return PB_OK;
+}
+// Blocks of `threads` threads of `kernel` resident on d's device at once (one
+// wave), from the occupancy API, cached per (kernel, device).  Grids sized to
+// it avoid a partial second wave.
+inline int64_t resident_blocks(Device* d, const void* kernel, int threads) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int64_t> known;
+  std::lock_guard<std::mutex> g(mu);
+  const auto key = std::make_pair(kernel, d->ordinal);
+  auto it = known.find(key);
+  if (it != known.end()) return it->second;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const int64_t n = (int64_t)per_sm * d->sm_count;
+  known[key] = n;
+  return n;
 }
 // Fill `count` elements of dtype PB_F32 / PB_F64 / PB_BOOL with `value`.
 int fill_device(Device* d, int dtype, void* dst, size_t count, double value);

@@ -432,9 +432,9 @@ struct Plan {
   int64_t blocks;
 };
 
-Plan plan_rows(int64_t rows, int64_t K, int64_t elem, int sm_count) {
+// `resident`: blocks of the row kernel that fit at once (one wave).
+Plan plan_rows(int64_t rows, int64_t K, int64_t elem, int64_t resident) {
   Plan p;
-  const int64_t resident = (int64_t)sm_count * (2048 / kThreads);
   if (rows >= 2 * resident || K * elem <= 16384) {
     // Whole rows per block: a warp per row up to 32 KiB rows (warp-only
     // reduction), more warps per row beyond that.
@@ -458,7 +458,8 @@ Plan plan_rows(int64_t rows, int64_t K, int64_t elem, int sm_count) {
 
 template <typename T, bool PAIR_OUT>
 int launch_rows(Device* d, const T* x, T* out, NormPair* pair_out, int64_t rows, int64_t K) {
-  Plan p = plan_rows(rows, K, sizeof(T), d->sm_count);
+  Plan p = plan_rows(rows, K, sizeof(T),
+                     resident_blocks(d, (const void*)norm_rows_kernel<T, true, PAIR_OUT>, kThreads));
   if (p.blocks > INT32_MAX) PB_FAIL(PB_ERR_UNSUPPORTED, "norm grid too large");
   NormPair* partial = nullptr;
   unsigned int* cnt = nullptr;
