@@ -265,12 +265,30 @@ int pb_broadcast(pb_ctx* ctx, int dev, void* buf, size_t bytes, int root);
 /* Full-array norm of a tensor sliced contiguously across ranks: each rank
  * passes its own slice (n local elements, possibly 0); every rank receives
  * the global norm in `out` (device, 1 element).  Each rank's local
- * (scale exponent, ssq, NaN/Inf class) triple is all-gathered (16 bytes per
- * rank, one NCCL call) and merged on the device in rank order, so every rank
- * computes the identical result.  No counterpart in the
- * reference, which is single-device (src/openpacho/_cuda.py:138-199). */
+ * (scale exponent, ssq, NaN/Inf class) triple is exchanged -- pushed over
+ * NVLink into every peer's mailbox by the reduction kernel itself when peer
+ * mailboxes are mapped (pb_peer_import), else one NCCL all-gather of 16 bytes
+ * per rank -- and merged on the device in rank order, so every rank computes
+ * the identical result.  No counterpart in the reference, which is
+ * single-device (src/openpacho/_cuda.py:138-199). */
 int pb_norm_sharded(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, void* out);
 /* Sum all-reduce of `count` elements in place (used for sharded DOT). */
+/* Peer mailboxes for the sharded norm and DOT: after them, pb_norm_sharded and
+ * pb_dot_sharded exchange each rank's partial with NVLink stores into every
+ * peer's memory (the norm from inside its reduction kernel), merged in rank
+ * order with waits bounded at 10 s (PB_ERR_DEVICE on timeout) -- no NCCL call.
+ * pb_peer_export allocates this rank's mailbox and returns its 64-byte CUDA
+ * IPC handle; once every rank's handle is known, pb_peer_import maps them
+ * (handles: nranks x 64 bytes in rank order).  PB_ERR_UNAVAILABLE when CUDA
+ * IPC is not available: keep using the NCCL path.  2 <= nranks <= 8. */
+int pb_peer_export(pb_ctx* ctx, int dev, int nranks, int rank, unsigned char handle[64]);
+int pb_peer_import(pb_ctx* ctx, int dev, int nranks, const unsigned char* handles);
+int pb_peer_close(pb_ctx* ctx, int dev);
+/* *out = sum over ranks of the DOT of each rank's (x, y) slice (peer
+ * mailboxes required), the same value on every rank. */
+int pb_dot_sharded(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, const void* y,
+                   void* out);
+
 int pb_allreduce_sum(pb_ctx* ctx, int dev, int dtype, void* buf, size_t count);
 
 #if defined(__GNUC__)

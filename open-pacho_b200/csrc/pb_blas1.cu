@@ -401,6 +401,15 @@ int launch_fill(Device* d, T* out, size_t n, T value) {
 
 }  // namespace
 
+// DOT into device memory (the local partial of the sharded DOT).
+int dot_device(Device* d, int dtype, int64_t n, const void* x, const void* y, void* out) {
+  if (!n) return fill_device(d, dtype, out, 1, 0.0);
+  if (!x || !y) PB_FAIL(PB_ERR_INVALID, "null input");
+  if (dtype == PB_F32)
+    return launch_gemv<float, true>(d, (const float*)x, (const float*)y, (float*)out, 1, n, n);
+  return launch_gemv<double, true>(d, (const double*)x, (const double*)y, (double*)out, 1, n, n);
+}
+
 int fill_device(Device* d, int dtype, void* dst, size_t count, double value) {
   if (dtype == PB_F32) return launch_fill<float>(d, (float*)dst, count, (float)value);
   if (dtype == PB_F64) return launch_fill<double>(d, (double*)dst, count, value);

@@ -22,6 +22,7 @@ namespace pb {
 
 int norm_pairs_finalize(Device* d, int dtype, const void* pairs, int n, void* out);
 int norm_pair_zero(Device* d, int dtype, void* pair);
+int norm_sharded_p2p(Device* d, int dtype, int64_t n, const void* x, void* out);
 
 namespace {
 
@@ -239,6 +240,9 @@ int pb_norm_sharded(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, v
   std::lock_guard<std::recursive_mutex> g(ctx->mu);
   Device* d;
   PB_CHECK(enter(ctx, dev, &d));
+  if (n > 0 && !x) PB_FAIL(PB_ERR_INVALID, "null input");
+  // With peer mailboxes mapped: push over NVLink from the norm kernel itself.
+  if (d->box_ranks > 1) return norm_sharded_p2p(d, dtype, n, x, out);
   PB_CHECK(need_comm(d));
   // pairs[r] = rank r's (scale exponent, ssq, class); one all-gather, then
   // every rank merges them in rank order (identical result everywhere).

@@ -90,6 +90,12 @@ struct Device {
   // NCCL communicator (ncclComm_t) when joined.
   void* comm = nullptr;
   int nranks = 1, rank = 0;
+  // Peer mailboxes (pb_peer_export/import): every rank's slot array mapped
+  // into this device's address space (own first allocated here), the call
+  // sequence number of the next exchange.
+  struct MailSlot* box[8] = {};
+  int box_ranks = 0, box_rank = 0;
+  unsigned long long box_seq = 0;
 };
 
 }  // namespace pb
@@ -147,9 +153,71 @@ int operand_tags(Device* d, size_t n, unsigned int** out, unsigned int* gen);
 int tensor_map_encoder(void** fn);
 
 // Entry points implemented per translation unit, all on an entered device.
-int norm_pair_global(Device* d, int dtype, int64_t n, const void* x, void* pair_out);
+// push: write the pair into every rank's mailbox instead of pair_out.
+int norm_pair_global(Device* d, int dtype, int64_t n, const void* x, void* pair_out,
+                     const struct PushArgs* push = nullptr);
+// Unmap the peers' mailboxes and free this one (pb_peer.cu).
+int peer_close(Device* d);
 // Stream wait bounded in time that also watches the NCCL communicator.
 int comm_stream_wait(Device* d);
+
+// ---- peer mailboxes: NVLink exchange of one small result per rank --------
+//
+// Rank r's mailbox holds two 32-byte slots per writer rank (one per parity of
+// the call sequence number): slot [w * 2 + seq % 2] is written only by rank w,
+// over NVLink, with the payload first and the sequence number last (release,
+// system scope); the owner reads the sequence number with acquire loads.  Two
+// parities suffice: rank w can start call s+2 only after its own call s+1,
+// whose merge needed every rank's value of s+1, which each rank pushes only
+// after its merge of call s (stream order).
+constexpr int kMaxRanks = 8;
+struct MailSlot {
+  double a;                // norm: ssq; DOT: partial sum
+  int e, cls;              // norm: scale exponent and class
+  double unused;
+  unsigned long long seq;  // call sequence number, stored last
+};
+static_assert(sizeof(MailSlot) == 32, "mailbox slot size");
+
+struct PushArgs {
+  MailSlot* box[kMaxRanks];  // every rank's mailbox, own included
+  int nranks, rank, parity;
+  unsigned long long seq;
+};
+
+// Wait (one thread) until `slot` carries sequence number `seq`; false, with
+// the kernel error flag set, after kMailboxWaitNs.  The acquire load orders
+// the payload reads after it.
+constexpr unsigned long long kMailboxWaitNs = 10ull * 1000 * 1000 * 1000;
+__device__ __forceinline__ bool mailbox_wait(const MailSlot* slot, unsigned long long seq, int* err) {
+  unsigned long long t0, t, v;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (;;) {
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(&slot->seq) : "memory");
+    if (v == seq) return true;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > kMailboxWaitNs) {
+      atomicExch(err, KERR_WAIT_TIMEOUT);
+      return false;
+    }
+    __nanosleep(256);
+  }
+}
+
+// Push this rank's value into every mailbox (one thread).
+__device__ __forceinline__ void push_slot(const PushArgs& a, double value, int e, int cls) {
+  for (int r = 0; r < a.nranks; ++r) {
+    MailSlot* s = a.box[r] + (a.rank * 2 + a.parity);
+    s->a = value;
+    s->e = e;
+    s->cls = cls;
+  }
+  __threadfence_system();
+  for (int r = 0; r < a.nranks; ++r) {
+    unsigned long long* q = &(a.box[r] + (a.rank * 2 + a.parity))->seq;
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(q), "l"(a.seq) : "memory");
+  }
+}
 
 // Batch-offset table (up to 8 broadcast dims), passed by value to kernels.
 struct BatchMap {

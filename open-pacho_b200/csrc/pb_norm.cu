@@ -244,12 +244,15 @@ __device__ __forceinline__ void store_warp_pair(NormPair* red, NormPair p) {
 
 // Rows of length K (inner == 1).  Same decomposition as the GEMV kernel.
 // PAIR_OUT: write the merged pair of the single row instead of the norm
-// (used by the multi-GPU combine).
+// (used by the multi-GPU combine): to pair_out, or, when push.nranks > 0,
+// straight into every rank's mailbox over NVLink (the compute and the
+// exchange of the sharded norm in one kernel).
 template <typename T, bool ALIGNED, bool PAIR_OUT>
 __global__ void __launch_bounds__(kThreads)
     norm_rows_kernel(const T* __restrict__ x, T* __restrict__ out, NormPair* __restrict__ pair_out,
                      int64_t rows, int64_t K, int rows_per_block, int64_t chunk, int nchunks,
-                     NormPair* __restrict__ partial, unsigned int* __restrict__ counters) {
+                     NormPair* __restrict__ partial, unsigned int* __restrict__ counters,
+                     const PushArgs push) {
   __shared__ NormPair red[kWarps];
   __shared__ bool last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -274,7 +277,8 @@ __global__ void __launch_bounds__(kThreads)
       if (r < rows) {
         NormPair s = red[threadIdx.x * G];
         for (int w = 1; w < G; ++w) merge(s, red[threadIdx.x * G + w]);
-        if (PAIR_OUT) pair_out[r] = s;
+        if (PAIR_OUT && push.nranks) push_slot(push, s.ssq, s.e, s.cls);
+        else if (PAIR_OUT) pair_out[r] = s;
         else out[r] = finalize<T>(s);
       }
     }
@@ -308,7 +312,8 @@ __global__ void __launch_bounds__(kThreads)
   if (threadIdx.x == 0) {
     NormPair t = red[0];
     for (int w = 1; w < kWarps; ++w) merge(t, red[w]);
-    if (PAIR_OUT) pair_out[row] = t;
+    if (PAIR_OUT && push.nranks) push_slot(push, t.ssq, t.e, t.cls);
+    else if (PAIR_OUT) pair_out[row] = t;
     else out[row] = finalize<T>(t);
     counters[row] = 0u;
   }
@@ -457,7 +462,8 @@ Plan plan_rows(int64_t rows, int64_t K, int64_t elem, int64_t resident) {
 }
 
 template <typename T, bool PAIR_OUT>
-int launch_rows(Device* d, const T* x, T* out, NormPair* pair_out, int64_t rows, int64_t K) {
+int launch_rows(Device* d, const T* x, T* out, NormPair* pair_out, int64_t rows, int64_t K,
+                const PushArgs& push = PushArgs{}) {
   Plan p = plan_rows(rows, K, sizeof(T),
                      resident_blocks(d, (const void*)norm_rows_kernel<T, true, PAIR_OUT>, kThreads));
   if (p.blocks > INT32_MAX) PB_FAIL(PB_ERR_UNSUPPORTED, "norm grid too large");
@@ -473,10 +479,10 @@ int launch_rows(Device* d, const T* x, T* out, NormPair* pair_out, int64_t rows,
   bool aligned = ((uintptr_t)x % 16 == 0) && (rows == 1 || K % VN == 0) && (p.chunk % VN == 0);
   if (aligned)
     norm_rows_kernel<T, true, PAIR_OUT><<<(unsigned)p.blocks, kThreads, 0, d->stream>>>(
-        x, out, pair_out, rows, K, p.rows_per_block, p.chunk, p.nchunks, partial, cnt);
+        x, out, pair_out, rows, K, p.rows_per_block, p.chunk, p.nchunks, partial, cnt, push);
   else
     norm_rows_kernel<T, false, PAIR_OUT><<<(unsigned)p.blocks, kThreads, 0, d->stream>>>(
-        x, out, pair_out, rows, K, p.rows_per_block, p.chunk, p.nchunks, partial, cnt);
+        x, out, pair_out, rows, K, p.rows_per_block, p.chunk, p.nchunks, partial, cnt, push);
   PB_LAUNCHED(d);
   return PB_OK;
 }
@@ -512,12 +518,58 @@ int launch_cols(Device* d, const T* x, T* out, int64_t outer, int64_t R, int64_t
 
 }  // namespace
 
-int norm_pair_global(Device* d, int dtype, int64_t n, const void* x, void* pair_out) {
+int norm_pair_global(Device* d, int dtype, int64_t n, const void* x, void* pair_out,
+                     const PushArgs* push) {
+  const PushArgs none{};
+  const PushArgs& p = push ? *push : none;
   if (dtype == PB_F32)
-    return launch_rows<float, true>(d, (const float*)x, nullptr, (NormPair*)pair_out, 1, n);
+    return launch_rows<float, true>(d, (const float*)x, nullptr, (NormPair*)pair_out, 1, n, p);
   if (dtype == PB_F64)
-    return launch_rows<double, true>(d, (const double*)x, nullptr, (NormPair*)pair_out, 1, n);
+    return launch_rows<double, true>(d, (const double*)x, nullptr, (NormPair*)pair_out, 1, n, p);
   PB_FAIL(PB_ERR_INVALID, "unknown dtype %d", dtype);
+}
+
+// Merge the pairs of every rank from this rank's mailbox, in rank order, and
+// write the norm: one thread, each wait bounded (kMailboxWaitNs) with the
+// kernel error flag set when it runs out.
+template <typename T>
+__global__ void mailbox_norm_kernel(const MailSlot* box, int nranks, int parity,
+                                    unsigned long long seq, T* out, int* err) {
+  if (threadIdx.x != 0) return;
+  NormPair s;
+  for (int r = 0; r < nranks; ++r) {
+    const MailSlot* slot = box + r * 2 + parity;
+    if (!mailbox_wait(slot, seq, err)) return;
+    NormPair q;
+    q.ssq = *(volatile const double*)&slot->a;
+    q.e = *(volatile const int*)&slot->e;
+    q.cls = *(volatile const int*)&slot->cls;
+    if (r == 0) s = q;
+    else merge(s, q);
+  }
+  *out = finalize<T>(s);
+}
+
+__global__ void push_empty_kernel(const PushArgs a, int e0) {
+  if (threadIdx.x == 0) push_slot(a, 0.0, e0, 0);
+}
+
+// The neutral pair of an empty slice, pushed to every rank.
+int norm_push_empty(Device* d, int dtype, const PushArgs& a) {
+  push_empty_kernel<<<1, 32, 0, d->stream>>>(a, dtype == PB_F64 ? kEmin : 0);
+  PB_LAUNCHED(d);
+  return PB_OK;
+}
+
+int mailbox_norm(Device* d, int dtype, int parity, unsigned long long seq, void* out) {
+  if (dtype == PB_F32)
+    mailbox_norm_kernel<float><<<1, 32, 0, d->stream>>>(d->box[d->box_rank], d->box_ranks, parity,
+                                                        seq, (float*)out, d->err_dev);
+  else
+    mailbox_norm_kernel<double><<<1, 32, 0, d->stream>>>(d->box[d->box_rank], d->box_ranks, parity,
+                                                         seq, (double*)out, d->err_dev);
+  PB_LAUNCHED(d);
+  return PB_OK;
 }
 
 int norm_pairs_finalize(Device* d, int dtype, const void* pairs, int n, void* out) {

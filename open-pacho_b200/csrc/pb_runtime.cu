@@ -99,6 +99,7 @@ static void release_device(Device* d) {
   if (d->ordinal < 0) return;
   cudaSetDevice(d->ordinal);
   if (d->stream) cudaStreamSynchronize(d->stream);
+  peer_close(d);
   if (d->scratch) cudaFreeAsync(d->scratch, d->stream);
   if (d->counters) cudaFreeAsync(d->counters, d->stream);
   if (d->tags) cudaFreeAsync(d->tags, d->stream);

@@ -89,6 +89,10 @@ PROTOTYPES = {
     "pb_reduce": [_ctx, _i, _i, _i, _p, _i, _pi64, C.c_uint32, _i, _p],
     "pb_dot": [_ctx, _i, _i, _i64, _p, _p, _p],
     "pb_dot_noalloc": [_ctx, _i, _i, _i64, _p, _p, _p],
+    "pb_peer_export": [_ctx, _i, _i, _i, C.c_char_p],
+    "pb_peer_import": [_ctx, _i, _i, C.c_char_p],
+    "pb_peer_close": [_ctx, _i],
+    "pb_dot_sharded": [_ctx, _i, _i, _i64, _p, _p, _p],
     "pb_norm": [_ctx, _i, _i, _i64, _i64, _i64, _p, _p],
     "pb_norm_strided": [_ctx, _i, _i, _i, _pi64, _pi64, _i, _pi64, _pi64, _p, _p],
     "pb_comm_unique_id": [C.c_char_p],

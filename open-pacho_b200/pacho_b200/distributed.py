@@ -9,18 +9,23 @@ the sharded forms of its hot path that split naturally:
   ``torch.distributed.TCPStore``); a per-step heartbeat lets ranks detect a
   departed peer on the host *before* launching a collective;
 * :func:`sharded_norm` -- global Euclidean norm of a vector sliced across ranks
-  (local (scale, ssq) pairs all-gathered and merged in rank order);
+  (local (scale, ssq) pairs exchanged and merged in rank order);
 * :func:`sharded_dot` -- global DOT of sliced vectors (local DOT + sum);
 * :func:`rowblock_matmul` -- row blocks of A per rank, B broadcast from a root;
 * :func:`batch_matmul` -- the leading batch dimension split across ranks.
 
 No data-path collective is used where the work is independent (row blocks,
-batch split); the broadcast of B happens once per operand.
+batch split); the broadcast of B happens once per operand.  The norm and DOT
+partials travel through peer mailboxes (CUDA IPC mappings of each rank's
+small slot array, set up when the group forms): NVLink stores from the
+kernels and a bounded wait, with NCCL as the fallback where IPC is not
+available (``Group.p2p`` says which; ``PB_P2P=0`` forces NCCL).
 """
 
 from __future__ import annotations
 
 import ctypes as C
+import os
 import time
 
 import numpy as np
@@ -71,6 +76,7 @@ class Group:
         self.store, self.prefix, self.timeout = store, prefix, timeout
         self._step = 0
         self._joined = False
+        self.p2p = False
         lib = backend._lib
         if world == 1:
             return
@@ -86,6 +92,29 @@ class Group:
         with backend._lock:
             _lib.check(lib.pb_comm_init(backend._ctx, 0, world, rank, raw), "pb_comm_init")
         self._joined = True
+        if os.environ.get("PB_P2P", "1") != "0" and world <= 8:
+            self.p2p = self._map_mailboxes()
+
+    def _map_mailboxes(self) -> bool:
+        """Export this rank's mailbox, map every peer's; every rank agrees
+        on the outcome through the store, so all use the same path."""
+        lib, b, key = self.backend._lib, self.backend, f"{self.prefix}/box"
+        handle = C.create_string_buffer(64)
+        with b._lock:
+            ok = lib.pb_peer_export(b._ctx, 0, self.world, self.rank, handle) == _lib.PB_OK
+        self.store.set(f"{key}/{self.rank}", handle.raw if ok else b"")
+        handles = [_store_get(self.store, f"{key}/{r}", self.timeout) for r in range(self.world)]
+        ok = ok and all(len(h) == 64 for h in handles)
+        if ok:
+            with b._lock:
+                ok = lib.pb_peer_import(b._ctx, 0, self.world, b"".join(handles)) == _lib.PB_OK
+        self.store.set(f"{key}/ok/{self.rank}", b"1" if ok else b"0")
+        agreed = all(_store_get(self.store, f"{key}/ok/{r}", self.timeout) == b"1"
+                     for r in range(self.world))
+        if not agreed:
+            with b._lock:
+                lib.pb_peer_close(b._ctx, 0)
+        return agreed
 
     def heartbeat(self):
         """Announce this rank at the next step and wait (bounded) for every
@@ -102,6 +131,7 @@ class Group:
     def close(self):
         if self._joined:
             with self.backend._lock:
+                self.backend._lib.pb_peer_close(self.backend._ctx, 0)
                 self.backend._lib.pb_comm_destroy(self.backend._ctx, 0)
             self._joined = False
 
@@ -109,6 +139,7 @@ class Group:
         """Drop the communicator without waiting for peers (after RankFailure)."""
         if self._joined:
             with self.backend._lock:
+                self.backend._lib.pb_peer_close(self.backend._ctx, 0)
                 self.backend._lib.pb_comm_abort(self.backend._ctx, 0)
             self._joined = False
 
@@ -158,6 +189,12 @@ def sharded_dot(group: Group, u_local: ndarray, v_local: ndarray) -> ndarray:
     dtype = b.validate_dtype(np.result_type(u_local.dtype, v_local.dtype))
     out = b.empty((1,), dtype)
     code = _lib.dtype_code(dtype)
+    if group.p2p:
+        group.heartbeat()
+        with b._lock:
+            _lib.check(b._lib.pb_dot_sharded(b._ctx, 0, code, u_local.size, _buf(u_local),
+                                             _buf(v_local), C.c_void_p(out.ptr)), "pb_dot_sharded")
+        return ndarray._wrap(out, (), dtype, b)
     with b._lock:
         _lib.check(b._lib.pb_dot(b._ctx, 0, code, u_local.size, _buf(u_local), _buf(v_local),
                                  C.c_void_p(out.ptr)), "pb_dot")

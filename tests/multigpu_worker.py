@@ -1,8 +1,10 @@
 """Worker for tests/test_gpu_multi.py: one process per GPU under torchrun.
 
 Checks each sharded path against the oracle on the full (unsharded) input:
-the sharded norm (float32 and float64, including a rank with an empty slice),
-the sharded DOT, row-block GEMM with B broadcast from rank 0, and the batch
+the sharded norm (float32 and float64, including a rank with an empty slice)
+and the sharded DOT -- both exchanging their partials through the NVLink peer
+mailboxes, repeated so both mailbox parities are used -- row-block GEMM with
+B broadcast from rank 0, and the batch
 split of a broadcast-batched GEMM.  With PB_TEST_FAILURE=1 it then has rank 1
 leave between steps (nothing in flight) and checks that rank 0 detects it on
 the host before launching its next collective and aborts its communicator.
@@ -42,6 +44,8 @@ def main() -> int:
     be = pb.B200Backend(local)
     group = D.Group(be, rank, world, store, timeout=60)
     res: dict = {"rank": rank}
+    # The norm and DOT partials travel through NVLink peer mailboxes.
+    res["p2p_unavailable"] = 0 if group.p2p else 1
 
     for dtype, span in ((np.float32, 35), (np.float64, 300)):
         for n in ((1 << 22) + 5, 1):
@@ -58,8 +62,14 @@ def main() -> int:
     u = rng.uniform(-1, 1, n).astype(np.float32)
     v = rng.uniform(-1, 1, n).astype(np.float32)
     s, e = D.shard_range(n, rank, world)
-    d = D.sharded_dot(group, pb.asarray(u[s:e], backend=be), pb.asarray(v[s:e], backend=be)).item()
-    res["dot"] = tolerance.gemm_violations(np.asarray(d, np.float32), numpy_backend.dot(u, v), u, v)
+    du, dv = pb.asarray(u[s:e], backend=be), pb.asarray(v[s:e], backend=be)
+    for call in range(3):  # three calls: both slot parities, one reused
+        d = D.sharded_dot(group, du, dv).item()
+        res[f"dot_{call}"] = tolerance.gemm_violations(np.asarray(d, np.float32),
+                                                       numpy_backend.dot(u, v), u, v)
+    u64, v64 = u.astype(np.float64), v.astype(np.float64)
+    d = D.sharded_dot(group, pb.asarray(u64[s:e], backend=be), pb.asarray(v64[s:e], backend=be)).item()
+    res["dot_f64"] = tolerance.gemm_violations(np.asarray(d), numpy_backend.dot(u64, v64), u64, v64)
 
     for dtype in (np.float32, np.float64):
         A = rng.standard_normal((1000, 300)).astype(dtype)

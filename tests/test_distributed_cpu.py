@@ -50,6 +50,23 @@ class FakeCommLib:
         self.calls.append(("abort",))
         return 0
 
+    def pb_peer_export(self, ctx, dev, world, rank, handle):
+        # Rank 0 can export, rank 1 cannot (no CUDA IPC): every rank must then
+        # agree on the NCCL path and rank 0 must unmap what it set up.
+        self.calls.append(("export", rank))
+        if rank == 0:
+            C.memmove(handle, bytes(64), 64)
+            return 0
+        return 7  # PB_ERR_UNAVAILABLE
+
+    def pb_peer_import(self, ctx, dev, world, handles):
+        self.calls.append(("import",))
+        return 0
+
+    def pb_peer_close(self, ctx, dev):
+        self.calls.append(("peer_close",))
+        return 0
+
 
 class FakeBackend:
     def __init__(self):
@@ -77,6 +94,7 @@ def _worker(rank, world, port, scenario, queue):
         elif scenario == "rendezvous":
             backend = FakeBackend()
             group = Group(backend, rank, world, store, prefix="t1", timeout=10)
+            backend._lib.calls.append(("p2p", group.p2p))
             group.heartbeat()
             group.heartbeat()
             group.close()
@@ -146,6 +164,10 @@ def test_nccl_id_rendezvous_through_the_store():
     assert id0 == id1 == bytes(range(128))
     assert ("uid",) in results[0] and ("uid",) not in results[1]
     assert all(calls[-1] == ("destroy",) for calls in results.values())
+    # Rank 1 could not export a mailbox: both ranks agree on the NCCL path,
+    # and rank 0 unmaps what it had set up before the group is used.
+    assert all(("p2p", False) in calls for calls in results.values())
+    assert results[0].index(("peer_close",)) < results[0].index(("p2p", False))
 
 
 def test_departed_rank_is_detected_before_any_collective():
