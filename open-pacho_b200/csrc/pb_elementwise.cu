@@ -332,6 +332,35 @@ __device__ __forceinline__ int64_t offset_of(const int64_t* shape, const int64_t
 
 // Block per (output, chunk): 256 threads stride over the chunk's reduced
 // indices, then a fixed shuffle + shared-memory tree.
+// Aligned float32 body [r, body) of one block's chunk: four accumulator lanes
+// (one per float4 component), eight 16-byte loads in flight per thread.
+template <int OP>
+__device__ __forceinline__ double trailing_f32(const float* __restrict__ x, int64_t r,
+                                               int64_t body) {
+  double lane[4] = {identity(OP), identity(OP), identity(OP), identity(OP)};
+  int64_t q = r + 4 * (int64_t)threadIdx.x;
+  for (; q + 28 * kThreads < body; q += 32 * kThreads) {
+    float4 u[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) u[i] = __ldg(reinterpret_cast<const float4*>(x + q + 4 * kThreads * i));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      lane[0] = combine(OP, lane[0], (double)u[i].x);
+      lane[1] = combine(OP, lane[1], (double)u[i].y);
+      lane[2] = combine(OP, lane[2], (double)u[i].z);
+      lane[3] = combine(OP, lane[3], (double)u[i].w);
+    }
+  }
+  for (; q < body; q += 4 * kThreads) {
+    const float4 u = __ldg(reinterpret_cast<const float4*>(x + q));
+    lane[0] = combine(OP, lane[0], (double)u.x);
+    lane[1] = combine(OP, lane[1], (double)u.y);
+    lane[2] = combine(OP, lane[2], (double)u.z);
+    lane[3] = combine(OP, lane[3], (double)u.w);
+  }
+  return combine(OP, combine(OP, lane[0], lane[1]), combine(OP, lane[2], lane[3]));
+}
+
 __global__ void __launch_bounds__(kThreads) reduce_blocks_kernel(const ReduceParams p) {
   __shared__ double warp_part[kThreads / 32];
   const int64_t o = blockIdx.x / p.chunks;
@@ -348,25 +377,10 @@ __global__ void __launch_bounds__(kThreads) reduce_blocks_kernel(const ReducePar
     if (r + threadIdx.x < head) acc = combine(p.op, acc, (double)__ldg(x + r + threadIdx.x));
     r = head;
     const int64_t body = r + (r1 - r) / 4 * 4;
-    // Four accumulator lanes (one per float4 component), two loads in flight.
-    double lane[4] = {identity(p.op), identity(p.op), identity(p.op), identity(p.op)};
-    int64_t q = r + 4 * (int64_t)threadIdx.x;
-    for (; q + 4 * kThreads < body; q += 8 * kThreads) {
-      const float4 u = __ldg(reinterpret_cast<const float4*>(x + q));
-      const float4 v = __ldg(reinterpret_cast<const float4*>(x + q + 4 * kThreads));
-      lane[0] = combine(p.op, combine(p.op, lane[0], (double)u.x), (double)v.x);
-      lane[1] = combine(p.op, combine(p.op, lane[1], (double)u.y), (double)v.y);
-      lane[2] = combine(p.op, combine(p.op, lane[2], (double)u.z), (double)v.z);
-      lane[3] = combine(p.op, combine(p.op, lane[3], (double)u.w), (double)v.w);
-    }
-    if (q < body) {
-      const float4 u = __ldg(reinterpret_cast<const float4*>(x + q));
-      lane[0] = combine(p.op, lane[0], (double)u.x);
-      lane[1] = combine(p.op, lane[1], (double)u.y);
-      lane[2] = combine(p.op, lane[2], (double)u.z);
-      lane[3] = combine(p.op, lane[3], (double)u.w);
-    }
-    acc = combine(p.op, acc, combine(p.op, combine(p.op, lane[0], lane[1]), combine(p.op, lane[2], lane[3])));
+    const double lanes = p.op == PB_REDUCE_SUM ? trailing_f32<PB_REDUCE_SUM>(x, r, body)
+                         : p.op == PB_REDUCE_MIN ? trailing_f32<PB_REDUCE_MIN>(x, r, body)
+                                                 : trailing_f32<PB_REDUCE_MAX>(x, r, body);
+    acc = combine(p.op, acc, lanes);
     if (body + threadIdx.x < r1) acc = combine(p.op, acc, (double)__ldg(x + body + threadIdx.x));
   } else if (p.trailing) {
     for (int64_t r = r0 + threadIdx.x; r < r1; r += kThreads)

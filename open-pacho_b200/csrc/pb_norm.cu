@@ -178,14 +178,26 @@ __device__ NormPair row_pair(const float* __restrict__ x, int64_t k0, int64_t k1
     const int nv = len / 4;
     const float4* xv = reinterpret_cast<const float4*>(x) + tid;
     int v = tid;
+    // Eight 16-byte loads in flight per thread (four left this kernel near
+    // 0.91 of the copy bandwidth at four resident blocks per SM); element
+    // 4*nthr*j + 4*tid + c still lands in lane j % 4, as in the four-load step.
 #pragma unroll 1
-    for (; v + 3 * nthr < nv; v += 4 * nthr, xv += 4 * nthr) {
+    for (; v + 7 * nthr < nv; v += 8 * nthr, xv += 8 * nthr) {
+      float4 r[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) r[i] = ld_stream(xv + i * nthr);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc.add4(r[i], i & 3);
+    }
+    if (v + 3 * nthr < nv) {
       const float4 r0 = ld_stream(xv), r1 = ld_stream(xv + nthr), r2 = ld_stream(xv + 2 * nthr),
                    r3 = ld_stream(xv + 3 * nthr);
       acc.add4(r0, 0);
       acc.add4(r1, 1);
       acc.add4(r2, 2);
       acc.add4(r3, 3);
+      v += 4 * nthr;
+      xv += 4 * nthr;
     }
 #pragma unroll 1
     for (; v < nv; v += nthr, xv += nthr) acc.add4(ld_stream(xv), 0);
