@@ -30,6 +30,7 @@ static int build_map(int batch_ndim, const int64_t* shape, const int64_t* as, co
     map->shape[i] = shape[i];
     map->a_stride[i] = as[i];
     map->b_stride[i] = bs[i];
+    map->div[i] = make_fastdiv(shape[i]);
     b *= shape[i];
   }
   *batch = b;

@@ -349,12 +349,24 @@ struct Tf32Params {
   unsigned int* coltag;      // per kTagCols columns of each B matrix
   int64_t cgroups;           // ceil(N / kTagCols)
   unsigned int gen;          // this launch's generation
+  int64_t batch;             // matrices in the product
+  // Launch-constant divisors of the tile schedule: the K split, tiles per
+  // matrix, tiles per group of GM M-tiles, and the last group's height.
+  FastDiv fd_ksplit, fd_tiles, fd_group, fd_gm_last;
 };
+
+constexpr int GM = 16;  // M-tiles per raster group (a power of two)
+
+// Work item w -> (tile, K split).
+__device__ __forceinline__ void item_of(const Tf32Params& p, int64_t w, int64_t& tile, int& split) {
+  tile = fdiv(w, p.fd_ksplit);
+  split = (int)(w - tile * p.ksplit);
+}
 
 // K-slice range [kb0, kb1) of split `s`.
 __device__ __forceinline__ void split_range(const Tf32Params& p, int s, int& kb0, int& kb1) {
-  kb0 = (int)((int64_t)s * p.kblocks / p.ksplit);
-  kb1 = (int)((int64_t)(s + 1) * p.kblocks / p.ksplit);
+  kb0 = (int)fdiv((int64_t)s * p.kblocks, p.fd_ksplit);
+  kb1 = (int)fdiv((int64_t)(s + 1) * p.kblocks, p.fd_ksplit);
 }
 
 template <int BN>
@@ -377,17 +389,19 @@ struct TileCoord {
 // Tile t -> (batch, m, n): batches in order; inside a batch a grouped raster
 // of 16 M-tiles so CTAs running together share A and B tiles in L2.
 __device__ __forceinline__ TileCoord tile_coord(const Tf32Params& p, int64_t t) {
-  constexpr int GM = 16;
-  const int64_t per_batch = (int64_t)p.tiles_m * p.tiles_n;
   TileCoord c;
-  c.bz = t / per_batch;
-  const int64_t r = t % per_batch;
-  const int64_t per_group = (int64_t)GM * p.tiles_n;
-  const int64_t first_m = (r / per_group) * GM;
-  const int64_t gm = min((int64_t)GM, (int64_t)p.tiles_m - first_m);
-  const int64_t in_group = r % per_group;
-  c.m_tile = first_m + in_group % gm;
-  c.n_tile = in_group / gm;
+  c.bz = fdiv(t, p.fd_tiles);
+  const int64_t r = t - c.bz * p.fd_tiles.d;
+  const int64_t group = fdiv(r, p.fd_group);
+  const int64_t first_m = group * GM;
+  const int64_t in_group = r - group * p.fd_group.d;
+  if (first_m + GM <= p.tiles_m) {  // a full group of GM M-tiles
+    c.m_tile = first_m + (in_group & (GM - 1));
+    c.n_tile = in_group / GM;
+  } else {  // the last, shorter group: tiles_m % GM M-tiles
+    c.n_tile = fdiv(in_group, p.fd_gm_last);
+    c.m_tile = first_m + (in_group - c.n_tile * p.fd_gm_last.d);
+  }
   return c;
 }
 
@@ -463,7 +477,7 @@ __device__ __forceinline__ void finish_item(const Tf32Params& p, const TileCoord
                                             int64_t row, int64_t col0, const float (&acc)[COLS]) {
   if (row >= p.M) return;
   if (p.ksplit > 1) {
-    const int64_t batch = p.tiles / ((int64_t)p.tiles_m * p.tiles_n);
+    const int64_t batch = p.batch;
     store_row<COLS>(p.partial + split * batch * p.M * p.N + (tc.bz * p.M + row) * p.N + col0, acc,
                     col0, p.N);
     return;
@@ -531,9 +545,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // ------------------------------------------------ TMA producer
       int64_t g = 0;  // k-slices issued by this CTA (ring position)
       for (int64_t w = blockIdx.x; w < items && !*abort_flag; w += gridDim.x) {
-        const TileCoord tc = tile_coord(p, w / p.ksplit);
+        int64_t tile;
+        int split;
+        item_of(p, w, tile, split);
+        const TileCoord tc = tile_coord(p, tile);
         int kb0, kb1;
-        split_range(p, (int)(w % p.ksplit), kb0, kb1);
+        split_range(p, split, kb0, kb1);
         int64_t ao, bo;
         batch_offsets(p.map, tc.bz, &ao, &bo);
         const int32_t a_row = (int32_t)(ao * p.M + tc.m_tile * BM);
@@ -565,8 +582,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       int64_t g = 0, gc = 0;  // k-slices consumed / chunks produced by this CTA
       bool ok = true;
       for (int64_t w = blockIdx.x; w < items && ok; w += gridDim.x) {
+        int64_t tile;
+        int split;
+        item_of(p, w, tile, split);
         int kb0, kb1;
-        split_range(p, (int)(w % p.ksplit), kb0, kb1);
+        split_range(p, split, kb0, kb1);
         const int nchunks = (kb1 - kb0 + CHUNK - 1) / CHUNK;
         for (int c = 0; c < nchunks && ok; ++c, ++gc) {
           const int buf = (int)(gc & 1);
@@ -600,8 +620,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * COLS);
     int64_t gc = 0;
     for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
-      const TileCoord tc = tile_coord(p, w / p.ksplit);
-      const int split = (int)(w % p.ksplit);
+      int64_t tile;
+      int split;
+      item_of(p, w, tile, split);
+      const TileCoord tc = tile_coord(p, tile);
       int kb0, kb1;
       split_range(p, split, kb0, kb1);
       const int nchunks = (kb1 - kb0 + CHUNK - 1) / CHUNK;
@@ -677,8 +699,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 // Per slice the MMA thread issues lo*hi, hi*lo, hi*hi (small terms first)
 // into the TMEM accumulator, promoted to fp32 registers every FCHUNK slices
 // (36 MMA steps).
-// Warps: 0 TMA producer, 1 MMA issuer, 2..9 split A (warp w owns TMEM lanes
-// 32*(w%4).. and K half (w-2)/4 of each slice), promote and store.
+// Warps: 0 TMA producer, 1 MMA issuer, 2..5 split A (warp w owns the 32 rows
+// at TMEM lanes 32*(w%4).. of every slice), 6..13 promote and store (warp w
+// owns the same lanes and column half (w-6)/4 of the accumulator).  With
+// the epilogue on warps of its own, the split never waits for a tile's
+// stores, so the tensor pipe keeps a full queue across tile boundaries.
 // TMEM columns: accumulators [0, 2*FBN), then for stage s A hi at
 // 2*FBN + 64*s and A lo 32 columns further.  A stage's A columns are free
 // once its full barrier fires: the TMA for slice g is only issued after the
@@ -688,7 +713,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #define PB_TF32_FCHUNK 3
 #endif
 constexpr int FCHUNK = PB_TF32_FCHUNK;
-constexpr int T_THREADS = 32 * (2 + 8);
+constexpr int T_SPLIT_WARPS = 4, T_ACC_WARPS = 8;
+constexpr int T_ACC_WARP0 = 2 + T_SPLIT_WARPS;
+constexpr int T_THREADS = 32 * (2 + T_SPLIT_WARPS + T_ACC_WARPS);
 
 template <int FBN>
 struct TSmem {
@@ -698,7 +725,7 @@ struct TSmem {
   static constexpr int STAGE = A_BYTES + 2 * B_BYTES;
   static constexpr int STAGES = FBN == 128 ? 4 : 6;
   // Epilogue staging: a 32 x 32 fp32 box (4 KiB, 128-byte swizzle) per warp.
-  static constexpr int OUT = STAGES * STAGE, OUT_BYTES = 8 * 4096;
+  static constexpr int OUT = STAGES * STAGE, OUT_BYTES = T_ACC_WARPS * 4096;
   static constexpr int TOTAL = OUT + OUT_BYTES + 1024 + 256;
   static constexpr uint32_t ACOL = 2 * FBN;     // first A column in TMEM
   static constexpr uint32_t TMEM_COLS = 512;
@@ -751,7 +778,7 @@ __device__ __forceinline__ void store_tma(const Tf32Params& p, const CUtensorMap
                                           uint32_t stage_u32) {
   const int lane = threadIdx.x & 31;
   const int64_t row = tc.m_tile * BM + quad * 32 + lane;
-  const int64_t batch = p.tiles / ((int64_t)p.tiles_m * p.tiles_n);
+  const int64_t batch = p.batch;
   const int32_t z = (int32_t)(p.ksplit > 1 ? split * batch + tc.bz : tc.bz);
   bool bad = false;
   if (p.ksplit == 1 && row < p.M) {
@@ -806,12 +833,12 @@ __global__ void __launch_bounds__(T_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full0 + 8 * s, 1);
-      mbar_init(ready0 + 8 * s, 8);
+      mbar_init(ready0 + 8 * s, T_SPLIT_WARPS);
       mbar_init(empty0 + 8 * s, 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(accf0 + 8 * b, 1);
-      mbar_init(acce0 + 8 * b, 8);
+      mbar_init(acce0 + 8 * b, T_ACC_WARPS);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -840,9 +867,12 @@ __global__ void __launch_bounds__(T_THREADS, 1)
       // ------------------------------------------------ TMA producer
       int64_t g = 0;
       for (int64_t w = blockIdx.x; w < items && !*abort_flag; w += gridDim.x) {
-        const TileCoord tc = tile_coord(p, w / p.ksplit);
+        int64_t tile;
+        int split;
+        item_of(p, w, tile, split);
+        const TileCoord tc = tile_coord(p, tile);
         int kb0, kb1;
-        split_range(p, (int)(w % p.ksplit), kb0, kb1);
+        split_range(p, split, kb0, kb1);
         int64_t ao, bo;
         batch_offsets(p.map, tc.bz, &ao, &bo);
         const int32_t a_row = (int32_t)(ao * p.M + tc.m_tile * BM);
@@ -873,8 +903,11 @@ __global__ void __launch_bounds__(T_THREADS, 1)
       int64_t g = 0, gc = 0;
       bool ok = true;
       for (int64_t w = blockIdx.x; w < items && ok; w += gridDim.x) {
+        int64_t tile;
+        int split;
+        item_of(p, w, tile, split);
         int kb0, kb1;
-        split_range(p, (int)(w % p.ksplit), kb0, kb1);
+        split_range(p, split, kb0, kb1);
         const int nchunks = (kb1 - kb0 + FCHUNK - 1) / FCHUNK;
         for (int c = 0; c < nchunks && ok; ++c, ++gc) {
           const int buf = (int)(gc & 1);
@@ -906,83 +939,26 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         }
       }
     }
-  } else {
-    // ------------------------------------ split A + accumulators (warps 2..9)
-    // Each warp splits its lanes' K half of every landed A slice into TMEM;
-    // after splitting the last slice of chunk c it promotes chunk c-1 (the
-    // tensor pipe is then busy with chunk c), and it promotes the final
-    // chunk at the end of the tile and stores it.
-    constexpr int COLS = FBN / 2;
+  } else if (warp < T_ACC_WARP0) {
+    // ------------------------------------------------ split A (warps 2..5)
+    // Each lane splits its row of every landed A slice (32 values) into the
+    // stage's hi and lo columns of its TMEM lane.
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
     const int row = quad * 32 + lane;  // row of the tile (TMEM lane)
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t acc_base = tmem + lane_off + (uint32_t)(half * COLS);
-    int64_t g = 0, gc = 0;
+    int64_t g = 0;
     bool ok = true;
-    float acc[COLS];
-
-    auto promote = [&]() {
-      const int buf = (int)(gc & 1);
-      const bool got = mbar_wait(accf0 + 8 * buf, (uint32_t)((gc >> 1) & 1), abort_flag, p.err);
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      if (!__all_sync(0xffffffffu, got)) {
-        ok = false;
-        return;
-      }
-      if constexpr (COLS == 32) {
-        uint32_t r[32];
-        tmem_ld32(acc_base + (uint32_t)(buf * FBN), r);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] += __uint_as_float(r[i]);
-      } else {
-#pragma unroll
-        for (int piece = 0; piece < COLS / 32; piece += 2) {
-          uint32_t r0[32], r1[32];
-          tmem_ld32x2(acc_base + (uint32_t)(buf * FBN + piece * 32),
-                      acc_base + (uint32_t)(buf * FBN + piece * 32 + 32), r0, r1);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            acc[piece * 32 + i] += __uint_as_float(r0[i]);
-            acc[piece * 32 + 32 + i] += __uint_as_float(r1[i]);
-          }
-        }
-      }
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acce0 + 8 * buf);
-      ++gc;
-    };
-
-    // The epilogue of a tile (its last promote and the store) is deferred
-    // until the first chunk of the next tile has been split, so the tensor
-    // pipe works on that chunk (the other TMEM buffer) meanwhile.  Promotes
-    // stay in chunk order.
-    int64_t pending = -1;  // work item whose epilogue is deferred
-    auto epilogue = [&]() {
-      promote();  // the pending tile's last chunk
-      if (!ok || *abort_flag) return;
-      const TileCoord ptc = tile_coord(p, pending / p.ksplit);
-      const int psplit = (int)(pending % p.ksplit);
-      const int64_t col0 = ptc.n_tile * FBN + half * COLS;
-      if (p.tma_store)
-        store_tma<COLS>(p, &map_c, ptc, psplit, quad, col0, acc,
-                        reinterpret_cast<float4*>(gbase + L::OUT + (warp - 2) * 4096),
-                        base + L::OUT + (warp - 2) * 4096);
-      else
-        finish_item<COLS>(p, ptc, psplit, ptc.m_tile * BM + row, col0, acc);
-    };
-#pragma unroll
-    for (int i = 0; i < COLS; ++i) acc[i] = 0.0f;
     for (int64_t w = blockIdx.x; w < items && ok; w += gridDim.x) {
-      const TileCoord tc = tile_coord(p, w / p.ksplit);
-      const int split = (int)(w % p.ksplit);
+      int64_t tile;
+      int split;
+      item_of(p, w, tile, split);
+      const TileCoord tc = tile_coord(p, tile);
       int kb0, kb1;
       split_range(p, split, kb0, kb1);
       int64_t ao, bo;
       batch_offsets(p.map, tc.bz, &ao, &bo);
       const int64_t arow = ao * p.M + tc.m_tile * BM + row;  // row of A over all matrices
-      for (int kb = kb0; kb < kb1 && ok; ++kb, ++g) {
+      for (int kb = kb0; kb < kb1; ++kb, ++g) {
         const int s = (int)(g % S);
         const bool got = mbar_wait(full0 + 8 * s, (uint32_t)((g / S) & 1), abort_flag, p.err);
         if (!__all_sync(0xffffffffu, got)) {
@@ -992,23 +968,31 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         // This lane's row is 128 bytes; the 128-byte swizzle stores its 16-byte
         // chunk j at position j ^ (row % 8).
         const float4* src = reinterpret_cast<const float4*>(gbase + s * L::STAGE + L::A + row * 128);
-        uint32_t hi[16], lo[16], emin = 0xffffffffu;
+        const uint32_t acol = tmem + lane_off + L::ACOL + 64u * s;
+        uint32_t emin = 0xffffffffu;
+        __syncwarp();  // converged for the .aligned TMEM stores
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const float4 v = src[(4 * half + t) ^ (row & 7)];
-          split_bits(v.x, hi[4 * t], lo[4 * t]);
-          split_bits(v.y, hi[4 * t + 1], lo[4 * t + 1]);
-          split_bits(v.z, hi[4 * t + 2], lo[4 * t + 2]);
-          split_bits(v.w, hi[4 * t + 3], lo[4 * t + 3]);
-          emin = min(emin, min(min(__float_as_uint(v.x) & 0x7f800000u, __float_as_uint(v.y) & 0x7f800000u),
-                               min(__float_as_uint(v.z) & 0x7f800000u, __float_as_uint(v.w) & 0x7f800000u)));
+        for (int h = 0; h < 2; ++h) {
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const float4 v = src[(4 * h + t) ^ (row & 7)];
+            split_bits(v.x, hi[4 * t], lo[4 * t]);
+            split_bits(v.y, hi[4 * t + 1], lo[4 * t + 1]);
+            split_bits(v.z, hi[4 * t + 2], lo[4 * t + 2]);
+            split_bits(v.w, hi[4 * t + 3], lo[4 * t + 3]);
+            emin = min(emin, min(min(__float_as_uint(v.x) & 0x7f800000u, __float_as_uint(v.y) & 0x7f800000u),
+                                 min(__float_as_uint(v.z) & 0x7f800000u, __float_as_uint(v.w) & 0x7f800000u)));
+          }
+          tmem_st16(acol + 16u * h, hi);
+          tmem_st16(acol + 32u + 16u * h, lo);
         }
         if (emin < (kTinyExp << 23)) {
-          // A zero or tiny value: tag the row if one of the sixteen is tiny.
+          // A zero or tiny value: tag the row if one of the 32 is tiny.
           bool t = false;
 #pragma unroll
-          for (int t4 = 0; t4 < 4; ++t4) {
-            const float4 v = src[(4 * half + t4) ^ (row & 7)];
+          for (int t8 = 0; t8 < 8; ++t8) {
+            const float4 v = src[t8 ^ (row & 7)];
             t |= tiny(v.x) | tiny(v.y) | tiny(v.z) | tiny(v.w);
           }
           if (t) {
@@ -1017,32 +1001,70 @@ __global__ void __launch_bounds__(T_THREADS, 1)
             __threadfence();
           }
         }
-        const uint32_t acol = tmem + lane_off + L::ACOL + 64u * s + 16u * half;
-        __syncwarp();  // converged for the .aligned TMEM stores
-        tmem_st16(acol, hi);
-        tmem_st16(acol + 32u, lo);
+        __syncwarp();
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(ready0 + 8 * s);
-        const int c = (kb - kb0) / FCHUNK;
-        const bool chunk_end = (kb - kb0) % FCHUNK == FCHUNK - 1 || kb == kb1 - 1;
-        if (chunk_end) {
-          if (c >= 1) {
-            promote();  // chunk c-1 of this tile
-          } else if (pending >= 0) {
-            epilogue();  // the previous tile, now that this tile's first chunk is split
-            pending = -1;
-            if (!ok || *abort_flag) break;
-#pragma unroll
-            for (int i = 0; i < COLS; ++i) acc[i] = 0.0f;
-          }
-        }
       }
-      if (!ok || *abort_flag) break;
-      pending = w;
     }
-    if (pending >= 0 && ok && !*abort_flag) epilogue();
+  } else {
+    // ------------------------------- promote and store (warps 6..13)
+    // Every FCHUNK slices the MMA thread commits a chunk of the tile into one
+    // of the two TMEM accumulators; these warps add it into fp32 registers,
+    // free the accumulator, and at the end of the work item store the tile.
+    constexpr int COLS = FBN / 2;
+    const int quad = warp & 3;
+    const int half = (warp - T_ACC_WARP0) >> 2;
+    const int row = quad * 32 + lane;  // row of the tile (TMEM lane)
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t acc_base = tmem + lane_off + (uint32_t)(half * COLS);
+    int64_t gc = 0;
+    bool ok = true;
+    float acc[COLS];
+
+    auto promote = [&](bool first) {
+      const int buf = (int)(gc & 1);
+      const bool got = mbar_wait(accf0 + 8 * buf, (uint32_t)((gc >> 1) & 1), abort_flag, p.err);
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      if (!__all_sync(0xffffffffu, got)) {
+        ok = false;
+        return;
+      }
+      // One 32-column piece at a time (these warps are off the critical path;
+      // two pieces in flight would not fit the 128-register cap of 14 warps).
+#pragma unroll
+      for (int piece = 0; piece < COLS / 32; ++piece) {
+        uint32_t r[32];
+        tmem_ld32(acc_base + (uint32_t)(buf * FBN + piece * 32), r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          acc[piece * 32 + i] = first ? __uint_as_float(r[i]) : acc[piece * 32 + i] + __uint_as_float(r[i]);
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce0 + 8 * buf);
+      ++gc;
+    };
+
+    for (int64_t w = blockIdx.x; w < items && ok; w += gridDim.x) {
+      int64_t tile;
+      int split;
+      item_of(p, w, tile, split);
+      int kb0, kb1;
+      split_range(p, split, kb0, kb1);
+      const int nchunks = (kb1 - kb0 + FCHUNK - 1) / FCHUNK;
+      for (int c = 0; c < nchunks && ok; ++c) promote(c == 0);
+      if (!ok || *abort_flag) break;
+      const TileCoord tc = tile_coord(p, tile);
+      const int64_t col0 = tc.n_tile * FBN + half * COLS;
+      if (p.tma_store)
+        store_tma<COLS>(p, &map_c, tc, split, quad, col0, acc,
+                        reinterpret_cast<float4*>(gbase + L::OUT + (warp - T_ACC_WARP0) * 4096),
+                        base + L::OUT + (warp - T_ACC_WARP0) * 4096);
+      else
+        finish_item<COLS>(p, tc, split, tc.m_tile * BM + row, col0, acc);
+    }
     if (lane == 0) bulk_wait_all();  // staging buffers are read before the CTA exits
   }
 
@@ -1182,6 +1204,11 @@ int finish_setup(Device* d, Tf32Params& p, int64_t batch, int64_t M, int64_t N, 
   p.A = A;
   p.B = B;
   p.K = K;
+  p.batch = batch;
+  p.fd_ksplit = make_fastdiv(p.ksplit);
+  p.fd_tiles = make_fastdiv((int64_t)p.tiles_m * p.tiles_n);
+  p.fd_group = make_fastdiv((int64_t)GM * p.tiles_n);
+  p.fd_gm_last = make_fastdiv(p.tiles_m % GM ? p.tiles_m % GM : GM);
   p.repair_inline = K <= (p.ksplit > 1 ? kReduceRepairMaxK : kInlineRepairMaxK);
   p.nf_tm = ceil_div(M, (int64_t)kNonFiniteTile);
   p.nf_tn = ceil_div(N, (int64_t)kNonFiniteTile);

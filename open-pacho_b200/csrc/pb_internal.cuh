@@ -220,19 +220,59 @@ __device__ __forceinline__ void push_slot(const PushArgs& a, double value, int e
 }
 
 // Batch-offset table (up to 8 broadcast dims), passed by value to kernels.
+// ---------------------------------------- division by launch constants --
+//
+// Quotients by a divisor fixed for a launch (batch extents, tile counts, the
+// K split) as a multiply-high and a shift instead of a 64-bit division
+// routine, which costs a single-thread pipeline stage (the TMA producer
+// between two tiles) about a microsecond per tile.  Granlund and Montgomery,
+// "Division by invariant integers using multiplication" (PLDI 1994), section
+// 4: with l = ceil(log2 d) and m = floor(2^32 (2^l - d) / d) + 1,
+// floor(n / d) = (mulhi(m, n) + n) >> l for every 32-bit n for which the sum
+// does not overflow, so for all n < 2^31 when 1 <= d <= 2^31.  Other operands
+// take the plain division.
+struct FastDiv {
+  int64_t d;
+  uint32_t m, s;
+  uint32_t lim;  // operands below lim take the multiply (0: none do)
+};
+
+inline FastDiv make_fastdiv(int64_t d) {
+  FastDiv f{d, 0u, 0u, 0u};
+  if (d < 1 || d > (int64_t(1) << 31)) return f;
+  uint32_t l = 0;
+  while ((int64_t(1) << l) < d) ++l;
+  f.m = (uint32_t)((((uint64_t(1) << l) - (uint64_t)d) << 32) / (uint64_t)d + 1);
+  f.s = l;
+  f.lim = 0x80000000u;
+  return f;
+}
+
+__host__ __device__ __forceinline__ int64_t fdiv(int64_t n, const FastDiv& f) {
+#ifdef __CUDA_ARCH__
+  if ((uint64_t)n < f.lim) {
+    const uint32_t x = (uint32_t)n;
+    return (int64_t)((__umulhi(x, f.m) + x) >> f.s);
+  }
+#endif
+  return n / f.d;
+}
+
 struct BatchMap {
   int ndim;
   int64_t shape[8];
   int64_t a_stride[8];
   int64_t b_stride[8];
+  FastDiv div[8];  // make_fastdiv(shape[i])
 };
 
 __host__ __device__ inline void batch_offsets(const BatchMap& m, int64_t b, int64_t* ao,
                                               int64_t* bo) {
   int64_t a = 0, c = 0;
   for (int i = m.ndim - 1; i >= 0; --i) {
-    int64_t idx = b % m.shape[i];
-    b /= m.shape[i];
+    const int64_t q = fdiv(b, m.div[i]);
+    const int64_t idx = b - q * m.shape[i];
+    b = q;
     a += idx * m.a_stride[i];
     c += idx * m.b_stride[i];
   }
