@@ -248,13 +248,19 @@ inline FastDiv make_fastdiv(int64_t d) {
   return f;
 }
 
-__host__ __device__ __forceinline__ int64_t fdiv(int64_t n, const FastDiv& f) {
+__host__ __device__ __forceinline__ uint32_t mulhi32(uint32_t a, uint32_t b) {
 #ifdef __CUDA_ARCH__
+  return __umulhi(a, b);
+#else
+  return (uint32_t)(((uint64_t)a * b) >> 32);
+#endif
+}
+
+__host__ __device__ __forceinline__ int64_t fdiv(int64_t n, const FastDiv& f) {
   if ((uint64_t)n < f.lim) {
     const uint32_t x = (uint32_t)n;
-    return (int64_t)((__umulhi(x, f.m) + x) >> f.s);
+    return (int64_t)((mulhi32(x, f.m) + x) >> f.s);
   }
-#endif
   return n / f.d;
 }
 

@@ -127,7 +127,7 @@ def _gemm_shapes():
     rng = np.random.default_rng(11)
     for m, n, k in ((128, 128, 32), (129, 255, 33), (300, 520, 97), (1, 300, 64), (257, 1, 40),
                     (64, 64, 1), (200, 136, 1000), (1, 4099, 3000), (3, 1001, 20000),
-                    (8, 64, 5), (5, 2, 70000)):
+                    (8, 64, 5), (5, 2, 70000), (2181, 200, 96)):
         yield (f"rand{m}x{n}x{k}", rng.standard_normal((m, k)).astype(np.float32),
                rng.standard_normal((k, n)).astype(np.float32))
 
