@@ -127,7 +127,7 @@ def _gemm_shapes():
     rng = np.random.default_rng(11)
     for m, n, k in ((128, 128, 32), (129, 255, 33), (300, 520, 97), (1, 300, 64), (257, 1, 40),
                     (64, 64, 1), (200, 136, 1000), (1, 4099, 3000), (3, 1001, 20000),
-                    (8, 64, 5), (5, 2, 70000), (2181, 200, 96)):
+                    (8, 64, 5), (5, 2, 70000), (2181, 200, 96), (900, 1100, 500)):
         yield (f"rand{m}x{n}x{k}", rng.standard_normal((m, k)).astype(np.float32),
                rng.standard_normal((k, n)).astype(np.float32))
 
@@ -195,7 +195,8 @@ def test_tf32x3_error_does_not_grow_with_k(b200, algo):
 
 @pytest.mark.parametrize("algo", [_lib.PB_GEMM_TF32X3_PRESPLIT, _lib.PB_GEMM_TF32X3_FUSED],
                          ids=["presplit", "fused"])
-@pytest.mark.parametrize("shape", [(2048, 2048, 256), (2048, 1024, 256), (2, 600, 300, 1024)],
+@pytest.mark.parametrize("shape", [(2048, 2048, 256), (2048, 1024, 256), (2, 600, 300, 1024),
+                                   (1024, 1024, 1024)],
                          ids=lambda s: "x".join(map(str, s)))
 def test_tf32x3_special_values_match_ieee(b200, algo, shape):
     """Inf/NaN operands give the IEEE classes of the reference's float32 GEMM.
@@ -203,7 +204,9 @@ def test_tf32x3_special_values_match_ieee(b200, algo, shape):
     The 3xTF32 split turns some +-Inf results into NaN (0 * Inf cross terms);
     those tiles are recomputed.  The first two shapes fill every SM without
     splitting K, so the marks come from the tcgen05 epilogues; the batched
-    shape splits K, so they come from the split reduction."""
+    shape splits K four ways, so they come from the split reduction; 1024^3
+    splits K two ways, which the TMEM kernel sums in CTA pairs before its
+    epilogue checks."""
     *batch, m, n, k = shape
     rng = np.random.default_rng(21)
     a = rng.standard_normal((*batch, m, k)).astype(np.float32)
@@ -233,7 +236,8 @@ def test_tf32x3_special_values_match_ieee(b200, algo, shape):
 
 @pytest.mark.parametrize("algo", [_lib.PB_GEMM_TF32X3_PRESPLIT, _lib.PB_GEMM_TF32X3_FUSED],
                          ids=["presplit", "fused"])
-@pytest.mark.parametrize("shape", [(2048, 2048, 256), (2048, 1024, 256), (2, 600, 300, 1024)],
+@pytest.mark.parametrize("shape", [(2048, 2048, 256), (2048, 1024, 256), (2, 600, 300, 1024),
+                                   (1024, 1024, 1024)],
                          ids=lambda s: "x".join(map(str, s)))
 def test_tf32x3_tiny_operands_keep_float32_accuracy(b200, algo, shape):
     """Operands below 2^-57 (products that would be subnormal on the tensor
