@@ -1,4 +1,5 @@
-"""Sharded paths on 2 GPUs (child processes under torchrun; skipped on 1 GPU).
+"""Sharded paths on 2 and 4 GPUs (child processes under torchrun; skipped
+without enough GPUs).
 
 NVLS is off (NCCL_NVLS_ENABLE=0) and the library's communicator waits are
 bounded (PB_COMM_TIMEOUT_S); the whole launch runs in its own process group
@@ -36,11 +37,11 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _launch(failure: bool, tmp_path):
+def _launch(failure: bool, tmp_path, nproc: int = 2):
     env = {**os.environ, "NCCL_NVLS_ENABLE": "0", "PB_COMM_TIMEOUT_S": "60",
            "PB_STORE_PORT": str(_free_port()), "PB_TEST_FAILURE": "1" if failure else "0",
            "PB_RESULT_DIR": str(tmp_path)}
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={nproc}",
            "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            str(ROOT / "tests" / "multigpu_worker.py")]
     proc = subprocess.Popen(cmd, env=env, cwd=ROOT, stdout=subprocess.PIPE,
@@ -50,10 +51,10 @@ def _launch(failure: bool, tmp_path):
     except subprocess.TimeoutExpired:
         os.killpg(proc.pid, signal.SIGKILL)
         out, _ = proc.communicate()
-        pytest.fail("2-GPU worker timed out:\n" + out[-4000:])
+        pytest.fail(f"{nproc}-GPU worker timed out:\n" + out[-4000:])
     assert proc.returncode == 0, out[-4000:]
     files = sorted(tmp_path.glob("rank*.json"))
-    assert len(files) == 2, out[-4000:]
+    assert len(files) == nproc, out[-4000:]
     results = [json.loads(f.read_text()) for f in files]
     return {r["rank"]: r for r in results}
 
@@ -62,6 +63,17 @@ def test_sharded_norm_dot_rowblock_and_batch_split_on_two_gpus(tmp_path):
     if _gpu_count() < 2:
         pytest.skip("needs 2 GPUs")
     results = _launch(failure=False, tmp_path=tmp_path)
+    for r in results.values():
+        checks = {k: v for k, v in r.items() if k != "rank"}
+        assert checks and all(v == 0 for v in checks.values()), r
+
+
+def test_sharded_paths_on_four_gpus(tmp_path):
+    """Four ranks: peer mailboxes of four slots, uneven shards."""
+    if _gpu_count() < 4:
+        pytest.skip("needs 4 GPUs")
+    results = _launch(failure=False, tmp_path=tmp_path, nproc=4)
+    assert sorted(results) == [0, 1, 2, 3]
     for r in results.values():
         checks = {k: v for k, v in r.items() if k != "rank"}
         assert checks and all(v == 0 for v in checks.values()), r
