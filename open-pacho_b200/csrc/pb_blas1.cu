@@ -31,7 +31,6 @@ namespace {
 #endif
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kUnroll = 4;
 
 template <typename T> struct V16;
 template <> struct V16<float> { using type = float4; static constexpr int n = 4; };

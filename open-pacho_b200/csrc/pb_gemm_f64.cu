@@ -66,6 +66,7 @@ __device__ __forceinline__ void dmma(double (&c)[4], double a0, double a1, doubl
       : "d"(a0), "d"(a1), "d"(b0));
 }
 
+#if PB_DMMA_K == 8
 // m16n8k8: a = (g, t), (g+8, t), (g, t+4), (g+8, t+4); b = (t, g), (t+4, g).
 __device__ __forceinline__ void dmma8(double (&c)[4], const double (&a)[4], const double (&b)[2]) {
   asm volatile(
@@ -74,6 +75,7 @@ __device__ __forceinline__ void dmma8(double (&c)[4], const double (&a)[4], cons
       : "+d"(c[0]), "+d"(c[1]), "+d"(c[2]), "+d"(c[3])
       : "d"(a[0]), "d"(a[1]), "d"(a[2]), "d"(a[3]), "d"(b[0]), "d"(b[1]));
 }
+#endif
 
 __global__ void __launch_bounds__(NT, 1) dmma_gemm_kernel(DmmaParams p) {
   extern __shared__ __align__(16) double smem[];
