@@ -8,10 +8,12 @@
 // This kernel: 128x128 output tile per 256-thread CTA; 8 warps in a 2 (M) x 4
 // (N) grid, each owning 64x32 = 4x4 tiles of m16n8, i.e. 16 DMMA per K-step of
 // 4 with 64 float64 accumulators per thread.  K advances in slices of 16 through
-// a 4-stage cp.async ring.  A is stored K-contiguous, B transposed to
-// K-contiguous, both with a 160-byte row pitch so a warp's fragment load of 32
-// doubles takes the minimum two shared-memory wavefronts.  Tails in M, N, K are
-// zero-filled by the copies (src-size 0) and masked at the store.
+// a 4-stage cp.async ring.  Both operands keep their global layout in shared
+// memory, so every copy reads consecutive addresses (16-byte copies when K and
+// N are even and the bases aligned, else 8-byte): A as [m][k] with a 160-byte
+// row pitch, B as [k][n] with a 1056-byte pitch; with those pitches a
+// half-warp's fragment load of 16 doubles covers all 32 banks once.  Tails in
+// M, N, K are zero-filled by the copies (src-size 0) and masked at the store.
 #include "pb_internal.cuh"
 
 namespace pb {
@@ -29,8 +31,10 @@ namespace {
 #define PB_DMMA_STAGES 4
 #endif
 constexpr int TM = 128, TN = 128, TK = PB_DMMA_TK, PITCH = TK + 4, NSTAGE = PB_DMMA_STAGES, NT = 256;
-static_assert(TK % PB_DMMA_K == 0 && (TM * TK) % NT == 0, "stage shape");
-constexpr int STAGE_DOUBLES = (TM + TN) * PITCH;
+constexpr int PITCHB = TN + 4;  // B rows [k][n]
+static_assert(TK % PB_DMMA_K == 0 && (TM * TK) % (2 * NT) == 0 && (TN * TK) % (2 * NT) == 0,
+              "stage shape");
+constexpr int STAGE_DOUBLES = TM * PITCH + TK * PITCHB;
 
 struct DmmaParams {
   const double* A;
@@ -48,6 +52,11 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 // 8-byte asynchronous copy; `bytes` = 0 writes zeros.
 __device__ __forceinline__ void cp_async8(uint32_t dst, const void* src, int bytes) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(bytes)
+               : "memory");
+}
+// 16-byte asynchronous copy (L2 only); `bytes` = 0 writes zeros.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes)
                : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() {
@@ -77,6 +86,7 @@ __device__ __forceinline__ void dmma8(double (&c)[4], const double (&a)[4], cons
 }
 #endif
 
+template <bool VEC>
 __global__ void __launch_bounds__(NT, 1) dmma_gemm_kernel(DmmaParams p) {
   extern __shared__ __align__(16) double smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -93,31 +103,47 @@ __global__ void __launch_bounds__(NT, 1) dmma_gemm_kernel(DmmaParams p) {
     const double* B = p.B + bo * K * N;
     double* C = p.C + bz * M * N;
 
-    // Stage loader.  Each warp instruction copies two smem rows of 16 doubles
-    // (lanes 0-15 one row, 16-31 the next), so its 32 eight-byte writes land in
-    // two wavefronts (160-byte pitch: the second row is shifted by 8 banks).
-    // A: rows are K-contiguous in global memory too (two 128-byte reads).
-    // B: stored transposed [n][k]; half-warp lanes read one column down 16
-    //    rows of B (sectors shared by neighbouring columns stay in L1).
+    // Stage loader: A rows of TK doubles (K-contiguous), B rows of TN doubles
+    // (N-contiguous); consecutive threads copy consecutive addresses.  With
+    // VEC, K and N are even, so a pair never straddles the K or N edge.
     auto load = [&](int64_t kt, int stage) {
       double* sa = smem + stage * STAGE_DOUBLES;
       double* sb = sa + TM * PITCH;
       const int64_t k0 = kt * TK;
+      if constexpr (VEC) {
 #pragma unroll
-      for (int i = 0; i < TM * TK / NT; ++i) {
-        const int idx = i * NT + tid, r = idx / TK, kk = idx % TK;
-        const int64_t gr = m0 + r, gk = k0 + kk;
-        const bool ok = gr < M && gk < K;
-        cp_async8(smem_u32(sa + r * PITCH + kk), ok ? (const void*)(A + gr * K + gk) : (const void*)A,
-                  ok ? 8 : 0);
-      }
+        for (int i = 0; i < TM * TK / (2 * NT); ++i) {
+          const int idx = i * NT + tid, r = idx / (TK / 2), kk = 2 * (idx % (TK / 2));
+          const int64_t gr = m0 + r, gk = k0 + kk;
+          const bool ok = gr < M && gk < K;
+          cp_async16(smem_u32(sa + r * PITCH + kk), ok ? (const void*)(A + gr * K + gk) : (const void*)A,
+                     ok ? 16 : 0);
+        }
 #pragma unroll
-      for (int i = 0; i < TN * TK / NT; ++i) {
-        const int idx = i * NT + tid, n = idx / TK, kk = idx % TK;
-        const int64_t gn = n0 + n, gk = k0 + kk;
-        const bool ok = gk < K && gn < N;
-        cp_async8(smem_u32(sb + n * PITCH + kk), ok ? (const void*)(B + gk * N + gn) : (const void*)B,
-                  ok ? 8 : 0);
+        for (int i = 0; i < TN * TK / (2 * NT); ++i) {
+          const int idx = i * NT + tid, kk = idx / (TN / 2), nn = 2 * (idx % (TN / 2));
+          const int64_t gk = k0 + kk, gn = n0 + nn;
+          const bool ok = gk < K && gn < N;
+          cp_async16(smem_u32(sb + kk * PITCHB + nn), ok ? (const void*)(B + gk * N + gn) : (const void*)B,
+                     ok ? 16 : 0);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < TM * TK / NT; ++i) {
+          const int idx = i * NT + tid, r = idx / TK, kk = idx % TK;
+          const int64_t gr = m0 + r, gk = k0 + kk;
+          const bool ok = gr < M && gk < K;
+          cp_async8(smem_u32(sa + r * PITCH + kk), ok ? (const void*)(A + gr * K + gk) : (const void*)A,
+                    ok ? 8 : 0);
+        }
+#pragma unroll
+        for (int i = 0; i < TN * TK / NT; ++i) {
+          const int idx = i * NT + tid, kk = idx / TN, nn = idx % TN;
+          const int64_t gk = k0 + kk, gn = n0 + nn;
+          const bool ok = gk < K && gn < N;
+          cp_async8(smem_u32(sb + kk * PITCHB + nn), ok ? (const void*)(B + gk * N + gn) : (const void*)B,
+                    ok ? 8 : 0);
+        }
       }
     };
 
@@ -141,7 +167,7 @@ __global__ void __launch_bounds__(NT, 1) dmma_gemm_kernel(DmmaParams p) {
       if (next < ktiles) load(next, (int)(next % NSTAGE));
       cp_async_commit();
       const double* sa = smem + (kt % NSTAGE) * STAGE_DOUBLES + (wm * 64) * PITCH;
-      const double* sb = smem + (kt % NSTAGE) * STAGE_DOUBLES + TM * PITCH + (wn * 32) * PITCH;
+      const double* sb = smem + (kt % NSTAGE) * STAGE_DOUBLES + TM * PITCH + wn * 32;
 #if PB_DMMA_K == 8
 #pragma unroll
       for (int k8 = 0; k8 < TK; k8 += 8) {
@@ -155,8 +181,8 @@ __global__ void __launch_bounds__(NT, 1) dmma_gemm_kernel(DmmaParams p) {
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          b[j][0] = sb[(j * 8 + g) * PITCH + k8 + t];
-          b[j][1] = sb[(j * 8 + g) * PITCH + k8 + t + 4];
+          b[j][0] = sb[(k8 + t) * PITCHB + j * 8 + g];
+          b[j][1] = sb[(k8 + t + 4) * PITCHB + j * 8 + g];
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i)
@@ -173,7 +199,7 @@ __global__ void __launch_bounds__(NT, 1) dmma_gemm_kernel(DmmaParams p) {
           a[i][1] = sa[(i * 16 + g + 8) * PITCH + k4 + t];
         }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) b[j] = sb[(j * 8 + g) * PITCH + k4 + t];
+        for (int j = 0; j < 4; ++j) b[j] = sb[(k4 + t) * PITCHB + j * 8 + g];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -217,8 +243,11 @@ int gemm_dmma_f64(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
   if (gx > INT32_MAX || gy > 65535) PB_FAIL(PB_ERR_UNSUPPORTED, "GEMM grid too large");
   const unsigned gz = (unsigned)(batch < 65535 ? batch : 65535);
   const int smem = NSTAGE * STAGE_DOUBLES * (int)sizeof(double);
-  PB_CHECK(allow_smem(d, (const void*)dmma_gemm_kernel, smem));
-  dmma_gemm_kernel<<<dim3((unsigned)gx, (unsigned)gy, gz), NT, smem, d->stream>>>(p);
+  // 16-byte copies need even K and N (rows of 16-byte multiples) and aligned bases.
+  const bool vec = K % 2 == 0 && N % 2 == 0 && ((uintptr_t)A & 15) == 0 && ((uintptr_t)B & 15) == 0;
+  auto kernel = vec ? dmma_gemm_kernel<true> : dmma_gemm_kernel<false>;
+  PB_CHECK(allow_smem(d, (const void*)kernel, smem));
+  kernel<<<dim3((unsigned)gx, (unsigned)gy, gz), NT, smem, d->stream>>>(p);
   PB_LAUNCHED(d);
   return PB_OK;
 }
