@@ -19,8 +19,9 @@
 namespace pb {
 namespace {
 
-// Measured on B200 (8192^3, TFLOP/s): m16n8k4, TK 16, 4 stages 28.5; m16n8k8
-// 27.9; TK 32 with 3 stages 22.2 (k4) / 22.8 (k8).  The defaults are the best.
+// Measured on B200 (8192^3, TFLOP/s, one run each): m16n8k4, TK 16, 4 stages
+// 31.9; 5 or 6 stages 31.6; TK 32 with 3 stages 32.4; m16n8k8 31.3 (with B
+// transposed in shared memory, before 16-byte copies: 28.5 / 27.9 / 22.2).
 #ifndef PB_DMMA_K
 #define PB_DMMA_K 4  // DMMA shape m16n8k4 or m16n8k8
 #endif
