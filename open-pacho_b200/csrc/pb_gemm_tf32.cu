@@ -54,6 +54,7 @@ __device__ __forceinline__ float tf32_rn(float x) {
 // are tagged by the split passes, and the epilogue recomputes the outputs
 // they touch with float32 FMA.
 constexpr uint32_t kTinyExp = 127 - 57;  // biased exponent of 2^-57
+constexpr float kTinyMag = 0x1p-57f;     // 2^-57: below it (zero included) the exact check runs
 constexpr int kTagCols = 64;
 
 __device__ __forceinline__ bool tiny(float x) {
@@ -969,7 +970,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         // chunk j at position j ^ (row % 8).
         const float4* src = reinterpret_cast<const float4*>(gbase + s * L::STAGE + L::A + row * 128);
         const uint32_t acol = tmem + lane_off + L::ACOL + 64u * s;
-        uint32_t emin = 0xffffffffu;
+        float amin = FLT_MAX;  // smallest magnitude of the row's 32 values (NaN ignored)
         __syncwarp();  // converged for the .aligned TMEM stores
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -981,13 +982,12 @@ __global__ void __launch_bounds__(T_THREADS, 1)
             split_bits(v.y, hi[4 * t + 1], lo[4 * t + 1]);
             split_bits(v.z, hi[4 * t + 2], lo[4 * t + 2]);
             split_bits(v.w, hi[4 * t + 3], lo[4 * t + 3]);
-            emin = min(emin, min(min(__float_as_uint(v.x) & 0x7f800000u, __float_as_uint(v.y) & 0x7f800000u),
-                                 min(__float_as_uint(v.z) & 0x7f800000u, __float_as_uint(v.w) & 0x7f800000u)));
+            amin = fminf(amin, fminf(fminf(fabsf(v.x), fabsf(v.y)), fminf(fabsf(v.z), fabsf(v.w))));
           }
           tmem_st16(acol + 16u * h, hi);
           tmem_st16(acol + 32u + 16u * h, lo);
         }
-        if (emin < (kTinyExp << 23)) {
+        if (amin < kTinyMag) {
           // A zero or tiny value: tag the row if one of the 32 is tiny.
           bool t = false;
 #pragma unroll
