@@ -1,4 +1,4 @@
-"""Host-side logic of the multi-GPU layer, as two gloo ranks on CPU.
+"""Host-side logic of the multi-GPU layer, as two or four gloo ranks on CPU.
 
 Covers the partitioning, the NCCL-id rendezvous through a TCP store and the
 heartbeat that detects a departed rank before any collective is launched.
@@ -30,8 +30,9 @@ def _free_port() -> int:
 
 
 class FakeCommLib:
-    def __init__(self):
+    def __init__(self, all_export=False):
         self.calls = []
+        self.all_export = all_export
 
     def pb_comm_unique_id(self, buf):
         C.memmove(buf, bytes(range(128)), 128)
@@ -53,14 +54,15 @@ class FakeCommLib:
     def pb_peer_export(self, ctx, dev, world, rank, handle):
         # Rank 0 can export, rank 1 cannot (no CUDA IPC): every rank must then
         # agree on the NCCL path and rank 0 must unmap what it set up.
+        # With all_export every rank exports a handle of 64 bytes of its rank.
         self.calls.append(("export", rank))
-        if rank == 0:
-            C.memmove(handle, bytes(64), 64)
+        if rank == 0 or self.all_export:
+            C.memmove(handle, bytes([rank]) * 64, 64)
             return 0
         return 7  # PB_ERR_UNAVAILABLE
 
     def pb_peer_import(self, ctx, dev, world, handles):
-        self.calls.append(("import",))
+        self.calls.append(("import", world, bytes(handles)))
         return 0
 
     def pb_peer_close(self, ctx, dev):
@@ -69,8 +71,8 @@ class FakeCommLib:
 
 
 class FakeBackend:
-    def __init__(self):
-        self._lib = FakeCommLib()
+    def __init__(self, all_export=False):
+        self._lib = FakeCommLib(all_export)
         self._ctx = C.c_void_p(1)
         self._lock = threading.RLock()
 
@@ -91,8 +93,8 @@ def _worker(rank, world, port, scenario, queue):
             gathered = [None] * world
             dist.all_gather_object(gathered, got)
             queue.put((rank, gathered))
-        elif scenario == "rendezvous":
-            backend = FakeBackend()
+        elif scenario in ("rendezvous", "mailboxes"):
+            backend = FakeBackend(all_export=scenario == "mailboxes")
             group = Group(backend, rank, world, store, prefix="t1", timeout=10)
             backend._lib.calls.append(("p2p", group.p2p))
             group.heartbeat()
@@ -168,6 +170,33 @@ def test_nccl_id_rendezvous_through_the_store():
     # and rank 0 unmaps what it had set up before the group is used.
     assert all(("p2p", False) in calls for calls in results.values())
     assert results[0].index(("peer_close",)) < results[0].index(("p2p", False))
+
+
+def test_four_ranks_partition_and_fall_back_together():
+    """Four ranks: contiguous shards, one shared NCCL id, and rank 1's failed
+    mailbox export sends every rank to the NCCL path."""
+    parts = _run("partition", world=4)
+    for gathered in parts.values():
+        for n in gathered[0]:
+            spans = [g[n] for g in gathered]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+    results = _run("rendezvous", world=4)
+    inits = {r: [c for c in calls if c[0] == "init"] for r, calls in results.items()}
+    assert sorted((c[0][1], c[0][2]) for c in inits.values()) == [(4, r) for r in range(4)]
+    assert len({c[0][3] for c in inits.values()}) == 1
+    assert all(("p2p", False) in calls for calls in results.values())
+
+
+def test_four_ranks_map_every_mailbox_in_rank_order():
+    """Every rank exports: each imports the four handles concatenated in rank
+    order and the group uses the peer mailboxes."""
+    results = _run("mailboxes", world=4)
+    want = b"".join(bytes([r]) * 64 for r in range(4))
+    for calls in results.values():
+        imports = [c for c in calls if c[0] == "import"]
+        assert imports == [("import", 4, want)]
+        assert ("p2p", True) in calls
 
 
 def test_departed_rank_is_detected_before_any_collective():
