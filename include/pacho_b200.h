@@ -63,6 +63,8 @@ int pb_abi_version(void);
 /* Replaces cuda_devices() (src/openpacho/_cuda.py, used by backends.devices
  * at src/openpacho/backends.py:55-60). */
 int pb_device_count(int* count);
+/* Name, memory, SM count and compute capability of one CUDA ordinal: the
+ * fields of the reference's DeviceInfo records (src/openpacho/_cuda.py:68-94). */
 int pb_device_info(int ordinal, char* name, size_t name_len, size_t* total_bytes,
                    int* sm_count, int* cc_major, int* cc_minor);
 /* CUDA driver version (e.g. 13000), the `driver` field of the reference's
@@ -75,34 +77,45 @@ int pb_driver_version(int* version);
 /* Create a context over `ndev` CUDA ordinals; one stream and one stream-ordered
  * memory pool per device. */
 int pb_init(int ndev, const int* ordinals, pb_ctx** out);
-/* Synchronise and release every resource of the context. */
+/* Synchronise and release every resource of the context (CUDABackend.close,
+ * src/openpacho/_cuda.py:644-673). */
 int pb_destroy(pb_ctx* ctx);
-/* Stream-ordered device allocation (never returns NULL for bytes > 0). */
+/* Stream-ordered device allocation (never returns NULL for bytes > 0);
+ * replaces CUDABackend.empty's cuMemAlloc or pool reuse (src/openpacho/_cuda.py:241-256). */
 int pb_alloc(pb_ctx* ctx, int dev, size_t bytes, void** ptr);
+/* Stream-ordered release back to the device pool; replaces the release of an
+ * _Allocation into the backend's pool (src/openpacho/_cuda.py:113-125, 258-289). */
 int pb_free(pb_ctx* ctx, int dev, void* ptr);
 /* Host -> device copy on the context stream.  blocking != 0 waits for the copy
  * (snapshot semantics of CUDABackend.upload, _cuda.py:293-303). */
 int pb_h2d(pb_ctx* ctx, int dev, void* dst, const void* src, size_t bytes, int blocking);
 /* Device -> host copy; synchronises the stream first (download, _cuda.py:305-311). */
 int pb_d2h(pb_ctx* ctx, int dev, void* dst, const void* src, size_t bytes);
-/* Asynchronous device -> host copy into pinned memory (no synchronisation). */
+/* Asynchronous device -> host copy into pinned memory (no synchronisation).
+ * No counterpart in the reference, whose download always synchronises. */
 int pb_d2h_async(pb_ctx* ctx, int dev, void* dst, const void* src, size_t bytes);
+/* Device -> device copy on the context stream.  No counterpart in the
+ * reference's backend protocol (its copies go through host memory). */
 int pb_d2d(pb_ctx* ctx, int dev, void* dst, const void* src, size_t bytes);
 /* Fill `count` elements with `value` (CUDABackend.full, _cuda.py:404-414);
  * PB_BOOL stores value != 0. */
 int pb_fill(pb_ctx* ctx, int dev, int dtype, void* dst, size_t count, double value);
-/* Wait for all submitted work; reports kernel-side error flags. */
+/* Wait for all submitted work; reports kernel-side error flags
+ * (CUDABackend.synchronize, src/openpacho/_cuda.py:237-239). */
 int pb_sync(pb_ctx* ctx, int dev);
-/* Page-lock host memory for asynchronous copies. */
+/* Page-lock host memory for asynchronous copies, and undo it.  No
+ * counterpart in the reference. */
 int pb_host_register(void* ptr, size_t bytes);
 int pb_host_unregister(void* ptr);
 /* Return pooled device memory and scratch to the driver
  * (release_cached_memory, _cuda.py:262-274). */
 int pb_trim(pb_ctx* ctx, int dev);
-/* CUDA-event timer on the device stream (for benchmarks). */
+/* CUDA-event timer on the device stream (for benchmarks): start, then stop and
+ * read the elapsed milliseconds.  No counterpart in the reference. */
 int pb_timer_start(pb_ctx* ctx, int dev);
 int pb_timer_stop(pb_ctx* ctx, int dev, float* ms);
-/* Number of kernels this library launched on `dev` since pb_init. */
+/* Number of kernels this library launched on `dev` since pb_init.  No
+ * counterpart in the reference. */
 int pb_launch_count(pb_ctx* ctx, int dev, uint64_t* count);
 
 /* ---- hot path ---------------------------------------------------------- */
@@ -249,11 +262,14 @@ enum { PB_REDUCE_SUM = 0, PB_REDUCE_MIN = 1, PB_REDUCE_MAX = 2 };
 int pb_reduce(pb_ctx* ctx, int dev, int op, int in_dtype, const void* src, int ndim,
               const int64_t* shape, uint32_t axes_mask, int out_dtype, void* out);
 
-/* ---- multi-GPU (one process per GPU; NCCL loaded on first use) --------- */
+/* ---- multi-GPU (one process per GPU; NCCL loaded on first use) --------- *
+ * None of these has a counterpart in the reference, which is single-device
+ * (src/openpacho/_cuda.py:138-199). */
 
 /* Opaque NCCL unique id (128 bytes) made by rank 0 and shared out of band. */
 int pb_comm_unique_id(unsigned char id[128]);
-/* Join the communicator of `nranks` processes as `rank` for device `dev`. */
+/* Join the communicator of `nranks` processes as `rank` for device `dev`;
+ * leave it (waiting for peers) with pb_comm_destroy. */
 int pb_comm_init(pb_ctx* ctx, int dev, int nranks, int rank, const unsigned char id[128]);
 int pb_comm_destroy(pb_ctx* ctx, int dev);
 /* Abandon the communicator without waiting for peers (after a peer failed);
@@ -272,7 +288,6 @@ int pb_broadcast(pb_ctx* ctx, int dev, void* buf, size_t bytes, int root);
  * the identical result.  No counterpart in the reference, which is
  * single-device (src/openpacho/_cuda.py:138-199). */
 int pb_norm_sharded(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, void* out);
-/* Sum all-reduce of `count` elements in place (used for sharded DOT). */
 /* Peer mailboxes for the sharded norm and DOT: after them, pb_norm_sharded and
  * pb_dot_sharded exchange each rank's partial with NVLink stores into every
  * peer's memory (the norm from inside its reduction kernel), merged in rank
@@ -280,7 +295,8 @@ int pb_norm_sharded(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, v
  * pb_peer_export allocates this rank's mailbox and returns its 64-byte CUDA
  * IPC handle; once every rank's handle is known, pb_peer_import maps them
  * (handles: nranks x 64 bytes in rank order).  PB_ERR_UNAVAILABLE when CUDA
- * IPC is not available: keep using the NCCL path.  2 <= nranks <= 8. */
+ * IPC is not available: keep using the NCCL path.  2 <= nranks <= 8.
+ * pb_peer_close unmaps the peers' mailboxes and frees this rank's. */
 int pb_peer_export(pb_ctx* ctx, int dev, int nranks, int rank, unsigned char handle[64]);
 int pb_peer_import(pb_ctx* ctx, int dev, int nranks, const unsigned char* handles);
 int pb_peer_close(pb_ctx* ctx, int dev);
@@ -289,6 +305,8 @@ int pb_peer_close(pb_ctx* ctx, int dev);
 int pb_dot_sharded(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, const void* y,
                    void* out);
 
+/* NCCL sum all-reduce of `count` elements in place (the sharded DOT's
+ * fallback when peer mailboxes are not mapped). */
 int pb_allreduce_sum(pb_ctx* ctx, int dev, int dtype, void* buf, size_t count);
 
 #if defined(__GNUC__)
