@@ -31,7 +31,6 @@ import subprocess
 import sys
 import threading
 import time
-from math import prod
 from pathlib import Path
 
 import numpy as np
