@@ -209,3 +209,63 @@ def norm_distribution_cases():
         rows = x.reshape(64, 1024)
         yield f"dist_rows_{np.dtype(dtype).name}", rows, 1, False
         yield f"dist_cols_{np.dtype(dtype).name}", rows, 0, False
+
+
+# ------------------------------------------------ around the path --------
+#
+# Elementwise operations, casts, reductions and strided gathers (the rows
+# widened beyond the GEMM/norm path).  Each case is (name, kind, op, inputs,
+# params): kind "ew" calls the public ufunc `op` on the inputs, "cast" is
+# astype(params["dtype"]), "reduce" is sum/min/max over params["axis"],
+# "gather" is transpose(params["axes"]) or diag(k=params["k"]) together with
+# the (shape, offset, strides) view the backend is asked to copy.
+def around_cases():
+    out = []
+    for dtype in DTYPES:
+        tag = np.dtype(dtype).name
+        # tests/test_extrema.py:61-80: zero ties, NaN and infinities across chunks.
+        host = np.zeros((5, 8193), dtype=dtype)
+        host[0, :4096] = -0.0
+        host[1] = -0.0
+        host[3, 4097] = np.nan
+        host[4, 0], host[4, -1] = -np.inf, np.inf
+        out.append((f"extrema_min_{tag}", "reduce", "min", [host], {"axis": (1,)}))
+        out.append((f"extrema_max_{tag}", "reduce", "max", [host], {"axis": (1,)}))
+        # tests/test_where.py:43-56: numeric truth, selected non-finites, zero sign.
+        cond = np.array([0, -0.0, 0.5, np.nan, np.inf, -np.inf], dtype=dtype)
+        left = np.array([np.nan, np.nan, np.nan, -0.0, np.inf, -np.inf], dtype=dtype)
+        right = np.array([0, -0.0, 42, 13, np.nan, np.nan], dtype=dtype)
+        out.append((f"where_{tag}", "ew", "where", [cond, left, right], {}))
+        # Arithmetic, comparisons and transcendentals over special values.
+        rng = np.random.default_rng(31)
+        x = rng.standard_normal((4, 1, 37)).astype(dtype)
+        y = rng.standard_normal((3, 37)).astype(dtype)
+        x.reshape(-1)[:6] = [np.inf, -np.inf, np.nan, -0.0, 0.0, np.finfo(dtype).tiny / 8]
+        y.reshape(-1)[:6] = [0.0, -0.0, 2.0, np.inf, -3.5, 1e-30]
+        for op in ("add", "subtract", "multiply", "true_divide", "power", "equal", "less",
+                   "greater_equal"):
+            out.append((f"ew_{op}_{tag}", "ew", op, [x, y], {}))
+        for op in ("exp", "log", "sqrt", "sin", "tanh", "absolute", "negative", "isfinite"):
+            out.append((f"ew_{op}_{tag}", "ew", op, [x], {}))
+        # Sums over axis sets, all axes included.
+        z = rng.standard_normal((7, 9, 11)).astype(dtype)
+        out.append((f"sum_axes02_{tag}", "reduce", "sum", [z], {"axis": (0, 2)}))
+        out.append((f"sum_all_{tag}", "reduce", "sum", [z], {"axis": (0, 1, 2)}))
+        # Strided gathers: a transpose and two diagonals.
+        g = rng.standard_normal((3, 4, 5)).astype(dtype)
+        out.append((f"transpose_{tag}", "gather", "transpose", [g],
+                    {"axes": (2, 0, 1), "view": ((5, 3, 4), 0, (1, 20, 5))}))
+        d = rng.standard_normal((4, 6)).astype(dtype)
+        out.append((f"diag0_{tag}", "gather", "diag", [d], {"k": 0, "view": ((4,), 0, (7,))}))
+        out.append((f"diag1_{tag}", "gather", "diag", [d], {"k": 1, "view": ((4,), 1, (7,))}))
+    # tests/test_edge_cases.py:81-83: astype(bool) of NaN and signed values;
+    # tests/test_edge_cases.py:124-131: broadcasting across ranks and a 0-d operand.
+    values = np.asarray([0.0, 2.0, -1.0, np.nan], dtype=np.float32)
+    out.append(("cast_bool_float32", "cast", "cast", [values], {"dtype": "bool"}))
+    wide = np.asarray([1e39, -1e39, 3.0, 1e-46, np.nan], dtype=np.float64)
+    out.append(("cast_float32_float64", "cast", "cast", [wide], {"dtype": "float32"}))
+    lh = np.arange(6, dtype=np.float32).reshape(2, 1, 3)
+    rh = np.arange(12, dtype=np.float32).reshape(4, 3)
+    out.append(("broadcast_add_float32", "ew", "add", [lh, rh], {}))
+    out.append(("scalar_multiply_float32", "ew", "multiply", [lh, np.asarray(2.0, np.float32)], {}))
+    return out

@@ -7,7 +7,9 @@ Run once in the build container, where the reference is importable:
 It imports ``openpacho`` (the reference, NumPy backend -- its parity oracle,
 src/openpacho/backends.py:82-150) and evaluates the reference's own hot-path
 test cases from ``cases.py`` through the public API
-(``openpacho.matmul``/``openpacho.linalg.norm``, asarray/asnumpy).  For every
+(``openpacho.matmul``/``openpacho.linalg.norm``, asarray/asnumpy), and the
+elementwise, cast, reduction and gather cases around that path through the
+matching public functions.  For every
 case it stores the SHA-256 of the inputs and the reference's outputs in
 ``golden.npz`` next to this file.  The GPU box never runs this script.
 """
@@ -52,6 +54,21 @@ def main() -> int:
             out[name] = r
             meta[name] = {"kind": "norm", "inputs": cases.digest(x), "axis": axis,
                           "keepdims": keepdims}
+
+    for name, kind, op, inputs, params in cases.around_cases():
+        args = [p.asarray(a) for a in inputs]
+        if kind == "ew":
+            r = getattr(p, op)(*args)
+        elif kind == "cast":
+            r = args[0].astype(np.dtype(params["dtype"]))
+        elif kind == "reduce":
+            r = getattr(p, op)(args[0], axis=params["axis"])
+        elif op == "transpose":
+            r = p.transpose(args[0], params["axes"])
+        else:
+            r = p.diag(args[0], params["k"])
+        out[name] = p.asnumpy(r)
+        meta[name] = {"kind": kind, "op": op, "inputs": cases.digest(*inputs)}
 
     np.savez_compressed(HERE / "golden.npz", **out)
     (HERE / "golden.json").write_text(json.dumps(

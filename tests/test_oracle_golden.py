@@ -1,4 +1,6 @@
-"""The oracle reproduces the reference's own outputs bit for bit (CPU).
+"""The oracle reproduces the reference's own outputs bit for bit (CPU): the
+GEMM and norm hot path, and the elementwise, cast, reduction and gather
+operations around it.
 
 The fixtures were produced by the reference itself (OpenPacho on its NumPy
 backend) from the reference's hot-path test cases; see golden/make_golden.py.
@@ -30,7 +32,8 @@ def _norm_inputs():
 
 def test_fixture_covers_every_case(golden):
     data, meta = golden
-    names = [n for n, *_ in _matmul_inputs()] + [n for n, *_ in _norm_inputs()]
+    names = ([n for n, *_ in _matmul_inputs()] + [n for n, *_ in _norm_inputs()]
+             + [c[0] for c in cases.around_cases()])
     assert sorted(names) == sorted(meta) == sorted(data.files)
 
 
@@ -55,6 +58,29 @@ def test_oracle_norm_matches_reference(golden, case):
     want = data[name]
     assert got.dtype == want.dtype and got.shape == want.shape
     np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("case", cases.around_cases(), ids=lambda c: c[0])
+def test_oracle_around_path_matches_reference(golden, case):
+    """Elementwise, cast, reduction and gather restatements against the
+    reference's own outputs: same dtype and shape, equal values with NaN in the
+    same places and the same zero signs."""
+    data, meta = golden
+    name, kind, op, inputs, params = case
+    assert cases.digest(*inputs) == meta[name]["inputs"], "regenerated inputs drifted"
+    want = data[name]
+    if kind == "ew":
+        got = numpy_backend.elementwise(op, inputs, want.dtype)
+    elif kind == "cast":
+        got = numpy_backend.elementwise("cast", inputs, np.dtype(params["dtype"]))
+    elif kind == "reduce":
+        got = numpy_backend.reduce(inputs[0], params["axis"], False, want.dtype, op)
+    else:
+        got = numpy_backend.gather(inputs[0], *params["view"])
+    assert got.dtype == want.dtype and got.shape == want.shape
+    assert np.array_equal(got, want, equal_nan=want.dtype.kind == "f")
+    if want.dtype.kind == "f":
+        np.testing.assert_array_equal(np.signbit(got), np.signbit(want))
 
 
 def test_oracle_known_answers():
