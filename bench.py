@@ -1,23 +1,33 @@
 """Benchmark of the b200 linear-algebra path (driver contract: one JSON line).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload gemv_dot|gemm1024|batched|norm|norm_rows|gemm_f32|gemm_f64|vecmat
-                                |elementwise|reduce]
+                    [--workload suite|batched|gemm1024|gemv_dot|norm|norm_rows|gemm_f32|gemm_f64
+                                |vecmat|elementwise|reduce|residual] [--dtype f32|f64] [--n SIZE]
 
-Default workload = BASELINE config 2 (the metric's memory-bound BLAS-1/2
-config): one step is y = A @ x with A 16384x16384 float32 plus one DOT of two
-2^26 float32 vectors, inputs uniform[-1,1] from default_rng(1) (A, x, then the
-two DOT vectors from the same stream).  value = algorithmic bytes / time
-(GB/s), whole job over all ranks; inputs (1.6 GB) are far larger than L2.
+Default (``suite``): every BASELINE config in one run, one JSON line.  The
+headline ``value`` is config 3 -- the batched broadcast float32 GEMM
+(8,16,512,256) @ (1,16,256,384), N(0,1) from default_rng(2), split along the
+leading batch dimension across ranks (strong scaling, TFLOP/s over all
+ranks).  ``configs`` carries one sub-record per other config, each with its own
+value, roofline, parity count, end-to-end figure and (N = 1) CPU baseline:
 
-Other workloads are BASELINE configs 1, 3, 4 and 5 (TFLOP/s or GB/s), and
-vecmat: x @ A (vector @ matrix, float32 16384^2, GB/s), and the operations
-around the path on 2^28 float32 values: elementwise (x + y) and reduce (sum).  Sharded
-ones split across ranks (batch dim for config 3, row blocks of A for config 5,
-contiguous slices + NCCL merge for config 4); config 1 and 2 run one replica
-per rank.  Multi-GPU: one process per GPU under torchrun; barriers and the
-max-over-ranks time go through a gloo process group (host side only), data
-collectives through the library's own NCCL communicator.
+  config1_gemm_f32_1024   float32 1024^3, default_rng(0); one replica per rank
+  config2_gemv_dot_f32    y = A @ x (A 16384^2) + DOT of two 2^26 vectors, U[-1,1],
+                          default_rng(1); one replica per rank
+  config4a_norm_f32/_f64  full norm of 2^28 values N(0,1) * 10^U(-35,35)
+                          (f64: 10^U(-300,300)), default_rng(3); contiguous slices,
+                          partial (scale, ssq) pairs merged through NVLink peer mailboxes
+  config4b_rows_f32/_f64  axis=1 norms of the same values as (65536, 4096); row blocks
+  config5_gemm_f32_16384  float32 16384^3, default_rng(4); row blocks of A, B broadcast
+  config5_gemm_f64_8192   float64 8192^3, default_rng(4); row blocks of A, B broadcast
+  vecmat_f32_16384        x @ A (vector @ matrix), A 16384^2 f32, default_rng(5)
+  residual_f32_16384      b - A @ x (the compiled-plan residual, GEMV epilogue), default_rng(7)
+
+Multi-GPU: one process per GPU under torchrun.  Barriers and the
+max-over-ranks time go through a gloo process group (host side only); data
+collectives use the library's own NCCL communicator (B broadcast for configs 3
+and 5) and NVLink peer mailboxes (config 4a partials).  Every record's inputs
+are larger than the 126 MB L2 or state otherwise in ``config.l2``.
 """
 
 from __future__ import annotations
@@ -38,20 +48,18 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "open-pacho_b200"))
 
-PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
-# Tensor-pipe ceilings for the GEMM workloads, measured on this pool's B200 with
-# cuBLAS (8192^3, best of 10): TF32 737.7 TFLOP/s -> 3xTF32 ceiling 245.9 logical;
-# FP64 DGEMM 35.5 TFLOP/s.  MEASURED_PEAKS.json carries bf16 only.
-TENSOR_CEILINGS = {
-    "gemm1024": (737.7 / 3, "measured cuBLAS TF32 / 3"),
-    "gemm_f32": (737.7 / 3, "measured cuBLAS TF32 / 3"),
-    "batched": (737.7 / 3, "measured cuBLAS TF32 / 3"),
-    "gemm_f64": (35.5, "measured cuBLAS DGEMM"),
-}
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# Tensor ceilings besides MEASURED_PEAKS.json (which carries bf16 and HBM only):
+# cuBLAS on this pool's B200 (8192^3, best of 10): TF32 737.7 TFLOP/s, DGEMM
+# 35.5 TFLOP/s; B200 specification FP64 (tensor) 40 TFLOP/s.
+CUBLAS_TF32_TFLOPS = 737.7
+CUBLAS_DGEMM_TFLOPS = 35.5
+SPEC_FP64_TFLOPS = 40.0
 L2_BYTES = 126 * 1024 * 1024
 
 
-# ------------------------------------------------------------- workloads --
+# ------------------------------------------------------------- inputs --
+# Seeds and distributions exactly as BASELINE.json's configs state.
 
 def gen_gemv_dot():
     rng = np.random.default_rng(1)
@@ -64,8 +72,7 @@ def gen_gemv_dot():
 
 def gen_gemm(seed, n, dtype):
     rng = np.random.default_rng(seed)
-    return (rng.standard_normal((n, n), dtype=np.float32 if dtype == np.float32 else np.float64),
-            rng.standard_normal((n, n), dtype=np.float32 if dtype == np.float32 else np.float64))
+    return rng.standard_normal((n, n), dtype=dtype), rng.standard_normal((n, n), dtype=dtype)
 
 
 def gen_batched():
@@ -79,13 +86,32 @@ def gen_norm(n=1 << 28, dtype=np.float32, span=35):
     rng = np.random.default_rng(3)
     out = np.empty(n, dtype)
     step = 1 << 24
-    for i in range(0, n, step):  # bounded host memory
+    for i in range(0, n, step):  # bounded host temporaries
         m = min(step, n - i)
         out[i:i + m] = rng.standard_normal(m) * 10.0 ** rng.uniform(-span, span, m)
     return out
 
 
-# ------------------------------------------------------------- plumbing --
+_NORM_CACHE: dict = {}
+
+
+def norm_input(dtype):
+    """Config 4 values for ``dtype`` (shared by the full and the row norms)."""
+    key = np.dtype(dtype).name
+    if key not in _NORM_CACHE:
+        _NORM_CACHE.clear()
+        _NORM_CACHE[key] = gen_norm(1 << 28, dtype, 300 if key == "float64" else 35)
+    return _NORM_CACHE[key]
+
+
+def shard(n: int, world: int, rank: int) -> tuple[int, int]:
+    """Rank's [lo, hi) of n items, as np.array_split divides them."""
+    q, r = divmod(n, world)
+    lo = rank * q + min(rank, r)
+    return lo, lo + q + (1 if rank < r else 0)
+
+
+# ---------------------------------------------------------- plumbing --
 
 class Dist:
     """Rank info + host-side (gloo) barrier/max for torchrun launches."""
@@ -100,7 +126,7 @@ class Dist:
 
             import torch.distributed as dist
 
-            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=180))
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
             # Bound the library's own collective waits too (default 300 s).
             os.environ.setdefault("PB_COMM_TIMEOUT_S", "60")
             self.dist = dist
@@ -110,14 +136,18 @@ class Dist:
         if self.pg:
             self.dist.barrier()
 
-    def max(self, value: float) -> float:
-        if not self.pg:
-            return value
+    def _reduce(self, value: float, op) -> float:
         import torch
 
         t = torch.tensor([value], dtype=torch.float64)
-        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        self.dist.all_reduce(t, op=op)
         return float(t.item())
+
+    def max(self, value: float) -> float:
+        return self._reduce(value, self.dist.ReduceOp.MAX) if self.pg else value
+
+    def sum(self, value: float) -> float:
+        return self._reduce(value, self.dist.ReduceOp.SUM) if self.pg else value
 
     def broadcast_bytes(self, data: bytes | None, size: int) -> bytes:
         if not self.pg:
@@ -194,25 +224,60 @@ class Clocks:
                 "samples": len(self.samples)}
 
 
-def traffic_per_launch(kernel: str, workload: str):
-    """DRAM bytes (read + write) per launch from the committed ncu summary."""
-    path = ROOT / "profiles" / "traffic.json"
-    if not path.exists():
-        return None
-    entry = json.loads(path.read_text()).get(f"{workload}:{kernel}")
-    return None if entry is None else entry.get("dram_bytes_per_launch")
-
-
 def peaks():
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         data = json.loads(path.read_text())
         return {"hbm_gbs": float(data["hbm_gbs"]), "bf16_tflops": float(data["bf16_tflops"]),
+                "bf16_tflops_sustained": float(data.get("bf16_tflops_sustained", data["bf16_tflops"])),
                 "source": "measured"}
     return {**PEAKS_FALLBACK, "source": "fallback"}
 
 
-# ----------------------------------------------------------- b200 arm --
+def traffic_entry(key: str):
+    """The committed ncu DRAM figure for a (workload, kernel) key, if any."""
+    path = ROOT / "profiles" / "traffic.json"
+    if not path.exists():
+        return None
+    return json.loads(path.read_text()).get(key)
+
+
+def traffic_per_launch(key: str, units: float):
+    """DRAM bytes (read + write) per launch of the main kernel: the ncu figure
+    if it was captured at this launch's size, scaled by the units processed
+    when the kernel's traffic grows in proportion to them (streaming
+    kernels), else None."""
+    entry = traffic_entry(key)
+    if not entry:
+        return None, None
+    captured = float(entry.get("units_per_launch") or 0)
+    bytes_ = float(entry["dram_bytes_per_launch"])
+    if captured and abs(captured - units) <= 1e-9 * captured:
+        return bytes_, "captured at this size"
+    if captured and entry.get("proportional"):
+        return bytes_ * units / captured, f"scaled from the capture at {captured:.4g} units"
+    return None, None
+
+
+def cpu_cores() -> int:
+    return len(os.sched_getaffinity(0))
+
+
+def blas_threads_all():
+    """Let OpenBLAS use every core this process may run on, whatever
+    OMP_NUM_THREADS torchrun set; returns the limiter (keep it alive) and the
+    thread count in effect."""
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+
+        limiter = threadpool_limits(limits=cpu_cores(), user_api="blas")
+        info = [i for i in threadpool_info() if i.get("user_api") == "blas"]
+        return limiter, int(info[0]["num_threads"]) if info else cpu_cores()
+    except Exception:  # noqa: BLE001 - threadpoolctl absent: numpy's own default
+        return None, cpu_cores()
+
+
+# ----------------------------------------------------------- the GPU --
 
 class Gpu:
     def __init__(self, device):
@@ -232,24 +297,28 @@ class Gpu:
     def check(self, status, what):
         self.lib.check(status, what)
 
+    def sync(self):
+        self.check(self.raw.pb_sync(self.ctx, 0), "sync")
+
     def busy(self, fn, dist, seconds=0.5):
         """Untimed steps for about `seconds`, so the clock sampler sees the GPU
         under this workload's load before the timed region.  The step count is
         calibrated per rank and agreed (max) across ranks: steps may contain
         collectives, so every rank must run exactly the same number."""
         t0 = time.perf_counter()
-        for _ in range(8):
+        for _ in range(4):
             fn()
-        self.check(self.raw.pb_sync(self.ctx, 0), "sync")
-        per8 = max(time.perf_counter() - t0, 1e-6)
-        rounds = int(dist.max(float(min(max(1, int(seconds / per8)), 4096))))
+        self.sync()
+        per4 = max(time.perf_counter() - t0, 1e-6)
+        rounds = int(dist.max(float(min(max(1, int(seconds / per4)), 4096))))
         for _ in range(rounds):
-            for _ in range(8):
+            for _ in range(4):
                 fn()
-            self.check(self.raw.pb_sync(self.ctx, 0), "sync")
+            self.sync()
 
     def timer(self, fn, reps):
-        self.check(self.raw.pb_sync(self.ctx, 0), "sync")
+        """Seconds for `reps` calls, by CUDA events on the library's stream."""
+        self.sync()
         self.check(self.raw.pb_timer_start(self.ctx, 0), "timer")
         for _ in range(reps):
             fn()
@@ -257,436 +326,955 @@ class Gpu:
         self.check(self.raw.pb_timer_stop(self.ctx, 0, C.byref(ms)), "timer")
         return ms.value / 1e3
 
+    def kernel_seconds(self, fn, reps):
+        """Average duration of the main kernel of `fn` (CUDA events around each
+        launch on the library's stream) and the launches seen."""
+        self.sync()
+        self.check(self.raw.pb_ktimer_enable(self.ctx, 0, 1), "ktimer")
+        try:
+            for _ in range(reps):
+                fn()
+            total, count = C.c_double(), C.c_uint64()
+            self.check(self.raw.pb_ktimer_read(self.ctx, 0, C.byref(total), C.byref(count)), "ktimer")
+        finally:
+            self.raw.pb_ktimer_enable(self.ctx, 0, 0)
+        return (total.value / 1e3 / count.value if count.value else None), count.value
+
     def launches(self):
         return self.backend.launch_count()
+
+    def pin(self, arrays):
+        for a in arrays:
+            self.check(self.raw.pb_host_register(C.c_void_p(a.ctypes.data), max(a.nbytes, 1)), "pin")
+
+    def unpin(self, arrays):
+        for a in arrays:
+            self.raw.pb_host_unregister(C.c_void_p(a.ctypes.data))
+
+    def h2d(self, dst, host):
+        self.check(self.raw.pb_h2d(self.ctx, 0, p_(dst), C.c_void_p(host.ctypes.data), host.nbytes, 0),
+                   "h2d")
+
+    def d2h_async(self, host, src):
+        self.check(self.raw.pb_d2h_async(self.ctx, 0, C.c_void_p(host.ctypes.data), p_(src),
+                                         host.nbytes), "d2h")
+
+    def d2h(self, host, src):
+        self.check(self.raw.pb_d2h(self.ctx, 0, C.c_void_p(host.ctypes.data), p_(src), host.nbytes),
+                   "d2h")
 
 
 def p_(buf):
     return C.c_void_p(buf.ptr)
 
 
-def run_gemv_dot(gpu: Gpu, args, dist: Dist, result: dict):
-    A, x, u, v = gen_gemv_dot()
-    M, K = A.shape
-    n = u.size
-    bytes_gemv = 4 * (M * K + K + M)
-    bytes_dot = 2 * 4 * n
-    step_bytes = bytes_gemv + bytes_dot
-    dA, dx, du, dv = (gpu.upload(t) for t in (A, x, u, v))
-    dy, dd = gpu.empty((M,), np.float32), gpu.empty((1,), np.float32)
-    raw, ctx, F32 = gpu.raw, gpu.ctx, gpu.lib.PB_F32
+class Comm:
+    """The library's NCCL communicator and NVLink peer mailboxes (N > 1)."""
 
-    def gemv():
-        gpu.check(raw.pb_gemv(ctx, 0, F32, M, K, p_(dA), p_(dx), p_(dy)), "pb_gemv")
+    def __init__(self, gpu: Gpu, dist: Dist):
+        self.gpu, self.dist = gpu, dist
+        self.active = dist.world > 1
+        self.exchange = None
+        if not self.active:
+            return
+        raw, ctx = gpu.raw, gpu.ctx
+        uid = C.create_string_buffer(128)
+        if dist.rank == 0:
+            gpu.check(raw.pb_comm_unique_id(uid), "unique id")
+        data = dist.broadcast_bytes(uid.raw if dist.rank == 0 else None, 128)
+        gpu.check(raw.pb_comm_init(ctx, 0, dist.world, dist.rank, data), "comm init")
+        handle = C.create_string_buffer(64)
+        ok = raw.pb_peer_export(ctx, 0, dist.world, dist.rank, handle) == 0
+        handles = dist.all_gather_bytes(handle.raw if ok else bytes(64), 64)
+        ok = ok and raw.pb_peer_import(ctx, 0, dist.world, b"".join(handles)) == 0
+        p2p = all(v == b"\x01" for v in dist.all_gather_bytes(b"\x01" if ok else b"\x00", 1))
+        if not p2p:
+            raw.pb_peer_close(ctx, 0)
+        self.exchange = "NVLink peer mailboxes" if p2p else "NCCL all-gather"
 
-    def dot():
-        gpu.check(raw.pb_dot(ctx, 0, F32, n, p_(du), p_(dv), p_(dd)), "pb_dot")
+    def broadcast(self, buf, nbytes):
+        self.gpu.check(self.gpu.raw.pb_broadcast(self.gpu.ctx, 0, p_(buf), nbytes, 0), "broadcast")
 
-    def step():
-        gemv()
-        dot()
-
-    for _ in range(args.warmup):
-        step()
-    dist.barrier()
-    with Clocks(gpu.backend.ordinal) as clocks:
-        gpu.busy(step, dist)
-        l0 = gpu.launches()
-        seconds = gpu.timer(step, args.steps)
-    launches = gpu.launches() - l0
-    seconds = dist.max(seconds)
-    # Per-kernel live timing for the roofline (dominant kernel: GEMV, 1.07 GB/launch).
-    t_gemv = gpu.timer(gemv, args.steps) / args.steps
-    t_dot = gpu.timer(dot, args.steps) / args.steps
-
-    # Parity spot check of this run's outputs against the oracle (rank 0).
-    y = np.empty(M, np.float32)
-    d = np.empty(1, np.float32)
-    gpu.check(raw.pb_d2h(ctx, 0, C.c_void_p(y.ctypes.data), p_(dy), y.nbytes), "d2h")
-    gpu.check(raw.pb_d2h(ctx, 0, C.c_void_p(d.ctypes.data), p_(dd), 4), "d2h")
-
-    # End to end through the public API: pinned host inputs copied in every step,
-    # results read back every step.
-    e2e = e2e_gemv_dot(gpu, A, x, u, v, args, dist)
-
-    total = step_bytes * args.steps * dist.world
-    result.update({
-        "metric": "GEMV 16384x16384 + DOT 2^26 float32 HBM throughput",
-        "value": total / seconds / 1e9,
-        "unit": "GB/s",
-        "ms_per_step": seconds / args.steps * 1e3,
-        "scaling": "weak",
-        "dtype": "f32",
-        "config": {"workload": "BASELINE config 2: y = A@x (A 16384x16384 f32) + DOT of two 2^26 f32 "
-                               "vectors, U[-1,1], default_rng(1)",
-                   "step_bytes": step_bytes, "parallelism": f"replicas x{dist.world}",
-                   "l2": "inputs (1.6 GB) larger than the 126 MB L2; no flush needed"},
-        "clocks": clocks.summary(),
-        "gpu_launches": launches,
-        "kernels": {"gemv_ms": t_gemv * 1e3, "gemv_gbs": bytes_gemv / t_gemv / 1e9,
-                    "dot_ms": t_dot * 1e3, "dot_gbs": bytes_dot / t_dot / 1e9},
-        "roofline_kernel": ("gemv", bytes_gemv, t_gemv),
-        "e2e": e2e,
-        "_check": ("gemv_dot", A, x, u, v, y, d),
-    })
+    def close(self):
+        if self.active:
+            self.gpu.raw.pb_peer_close(self.gpu.ctx, 0)
+            self.gpu.raw.pb_comm_destroy(self.gpu.ctx, 0)
 
 
-def e2e_gemv_dot(gpu, A, x, u, v, args, dist):
-    raw, ctx, F32 = gpu.raw, gpu.ctx, gpu.lib.PB_F32
-    host = [np.ascontiguousarray(t) for t in (A, x, u, v)]
-    for t in host:
-        gpu.check(raw.pb_host_register(C.c_void_p(t.ctypes.data), t.nbytes), "pin")
-    y = np.empty(A.shape[0], np.float32)
-    d = np.empty(1, np.float32)
-    for t in (y, d):
-        gpu.check(raw.pb_host_register(C.c_void_p(t.ctypes.data), t.nbytes), "pin")
-    dev = [gpu.empty(t.shape, t.dtype) for t in host]
-    dy, dd = gpu.empty(y.shape, np.float32), gpu.empty((1,), np.float32)
-    M, K = A.shape
+# -------------------------------------------------------- workloads --
+#
+# A workload holds one config's host inputs and device buffers on this rank.
+#   setup()        host inputs (this rank's share) and resident device buffers
+#   step()         one pass over the resident inputs (what `value` times)
+#   kernel_step()  the calls whose main kernel the roofline times
+#   e2e_step()     one pass from pinned host inputs to host results
+#   violations()   parity of this rank's outputs against the oracle
+#   cpu_step()     the reference's CPU path on a bounded sample -> units done
 
-    def step():
-        for h, dbuf in zip(host, dev):
-            gpu.check(raw.pb_h2d(ctx, 0, p_(dbuf), C.c_void_p(h.ctypes.data), h.nbytes, 0), "h2d")
-        gpu.check(raw.pb_gemv(ctx, 0, F32, M, K, p_(dev[0]), p_(dev[1]), p_(dy)), "gemv")
-        gpu.check(raw.pb_dot(ctx, 0, F32, u.size, p_(dev[2]), p_(dev[3]), p_(dd)), "dot")
-        gpu.check(raw.pb_d2h_async(ctx, 0, C.c_void_p(y.ctypes.data), p_(dy), y.nbytes), "d2h")
-        gpu.check(raw.pb_d2h_async(ctx, 0, C.c_void_p(d.ctypes.data), p_(dd), 4), "d2h")
+class Workload:
+    name = ""
+    unit = "GB/s"
+    bound = "hbm"
+    scaling = "weak"
+    dtype = "f32"
+    e2e_steps_cap = 20
 
-    step()
-    dist.barrier()
-    seconds = dist.max(gpu.timer(step, args.steps))
-    for t in (*host, y, d):
-        raw.pb_host_unregister(C.c_void_p(t.ctypes.data))
-    step_bytes = 4 * (A.size + x.size + A.shape[0]) + 8 * u.size
-    h2d = sum(t.nbytes for t in host)
-    return {"value": step_bytes * args.steps * dist.world / seconds / 1e9, "unit": "GB/s",
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": y.nbytes + 4,
-            "ms_per_step": seconds / args.steps * 1e3}
+    def __init__(self, args, dist: Dist):
+        self.args, self.dist = args, dist
+        self.world, self.rank = dist.world, dist.rank
 
+    # Units (flops or bytes) this rank processes per step, and per launch of
+    # the main kernel (main_launches launches per kernel_step).
+    units = 0.0
+    kernel_units = 0.0
+    kernel_key = ""
+    main_launches = 1
+    extra: dict = {}
 
-def run_gemm(gpu: Gpu, args, dist: Dist, result: dict, which: str):
-    raw, ctx = gpu.raw, gpu.ctx
-    if which == "gemm1024":
-        A, B = gen_gemm(0, args.n or 1024, np.float32)
-        dtype, shard = np.float32, False
-    elif which == "gemm_f32":
-        A, B = gen_gemm(4, args.n or 16384, np.float32)
-        dtype, shard = np.float32, True
-    else:
-        A, B = gen_gemm(4, args.n or 8192, np.float64)
-        dtype, shard = np.float64, True
-    n = A.shape[0]
-    rows = n // dist.world if shard else n
-    r0 = dist.rank * rows if shard else 0
-    Aloc = np.ascontiguousarray(A[r0:r0 + rows])
-    dA, dB = gpu.upload(Aloc), gpu.upload(B)
-    dC = gpu.empty((rows, n), dtype)
-    code = gpu.lib.dtype_code(dtype)
-    ns = gpu.lib.i64_array([])
+    def scale(self):
+        return 1e12 if self.unit == "TFLOP/s" else 1e9
 
-    def step():
-        gpu.check(raw.pb_gemm(ctx, 0, code, 0, ns, ns, ns, rows, n, n, p_(dA), p_(dB), p_(dC)), "gemm")
+    def kernel_step(self):
+        self.step()
 
-    for _ in range(args.warmup):
-        step()
-    dist.barrier()
-    with Clocks(gpu.backend.ordinal) as clocks:
-        gpu.busy(step, dist)
-        l0 = gpu.launches()
-        seconds = gpu.timer(step, args.steps)
-    launches = gpu.launches() - l0
-    seconds = dist.max(seconds)
-    flops = 2.0 * rows * n * n
-    total = flops * args.steps * dist.world
-    Cl = np.empty((rows, n), dtype)
-    gpu.check(raw.pb_d2h(ctx, 0, C.c_void_p(Cl.ctypes.data), p_(dC), Cl.nbytes), "d2h")
-    result.update({
-        "metric": f"{np.dtype(dtype).name} GEMM {n}^3 TFLOP/s",
-        "value": total / seconds / 1e12, "unit": "TFLOP/s",
-        "ms_per_step": seconds / args.steps * 1e3,
-        "scaling": "strong" if shard else "weak",
-        "dtype": "f32 (3xTF32)" if dtype == np.float32 else "f64",
-        "config": {"workload": f"GEMM {n}^3 {np.dtype(dtype).name}",
-                   "parallelism": f"row blocks x{dist.world}" if shard else f"replicas x{dist.world}"},
-        "clocks": clocks.summary(), "gpu_launches": launches,
-        "roofline_kernel": ("gemm", flops, seconds / args.steps),
-        "_check": ("gemm", Aloc, B, Cl),
-    })
+    def e2e_bytes(self):
+        return 0, 0
 
 
-def run_vecmat(gpu: Gpu, args, dist: Dist, result: dict):
-    """x @ A (vector @ matrix, float32): the skinny kernel, HBM bound."""
-    raw, ctx = gpu.raw, gpu.ctx
-    n = args.n or 16384
-    rng = np.random.default_rng(5)
-    A = rng.uniform(-1, 1, (n, n)).astype(np.float32)
-    x = rng.uniform(-1, 1, n).astype(np.float32)
-    dx, dA = gpu.upload(x), gpu.upload(A)
-    dy = gpu.empty((n,), np.float32)
-    ns = gpu.lib.i64_array([])
-    F32 = gpu.lib.PB_F32
+class Batched(Workload):
+    """BASELINE config 3, split along the leading batch dimension."""
 
-    def step():
-        gpu.check(raw.pb_gemm(ctx, 0, F32, 0, ns, ns, ns, 1, n, n, p_(dx), p_(dA), p_(dy)), "gemm")
+    name, unit, bound, scaling, dtype = "config3_batched_f32", "TFLOP/s", "tensor", "strong", "f32 (3xTF32)"
 
-    for _ in range(args.warmup):
-        step()
-    dist.barrier()
-    with Clocks(gpu.backend.ordinal) as clocks:
-        gpu.busy(step, dist)
-        l0 = gpu.launches()
-        seconds = gpu.timer(step, args.steps)
-    launches = gpu.launches() - l0
-    seconds = dist.max(seconds)
-    step_bytes = 4 * (n * n + 2 * n)
-    y = np.empty(n, np.float32)
-    gpu.check(raw.pb_d2h(ctx, 0, C.c_void_p(y.ctypes.data), p_(dy), y.nbytes), "d2h")
-    result.update({
-        "metric": f"vector @ matrix ({n} @ {n}x{n}) float32 HBM throughput",
-        "value": step_bytes * args.steps * dist.world / seconds / 1e9, "unit": "GB/s",
-        "ms_per_step": seconds / args.steps * 1e3, "scaling": "weak", "dtype": "f32",
-        "config": {"workload": f"x @ A, A {n}x{n} f32, U[-1,1], default_rng(5)",
-                   "step_bytes": step_bytes, "parallelism": f"replicas x{dist.world}",
-                   "l2": "A (1.07 GB) larger than the 126 MB L2; no flush needed"},
-        "clocks": clocks.summary(), "gpu_launches": launches,
-        "roofline_kernel": ("skinny", step_bytes, seconds / args.steps),
-        "_check": ("gemm", x.reshape(1, n), A, y.reshape(1, n)),
-    })
+    def metric(self):
+        return "batched broadcast GEMM (8,16,512,256)@(1,16,256,384) float32 TFLOP/s"
 
+    def config(self):
+        return {"workload": "BASELINE config 3: (8,16,512,256) @ (1,16,256,384) float32, N(0,1), "
+                            "default_rng(2)",
+                "parallelism": f"batch split x{self.world} (B broadcast from rank 0 by NCCL)",
+                "l2": "per step 176 MB of operands and output (1 GPU) > 126 MB L2; at N > 1 the "
+                      "shards are smaller than L2 and no flush is made (strong scaling)"}
 
-def run_around(gpu: Gpu, args, dist: Dist, result: dict, which: str):
-    """Operations around the path on 2^28 float32 values (HBM bound):
-    elementwise add of two arrays (pb_elementwise) or their full sum (pb_reduce)."""
-    raw, ctx = gpu.raw, gpu.ctx
-    n = args.n or (1 << 28)
-    rng = np.random.default_rng(6)
-    x = rng.standard_normal(n, dtype=np.float32)
-    dx = gpu.upload(x)
-    F32 = gpu.lib.PB_F32
-    y = None
-    if which == "elementwise":
-        y = rng.standard_normal(n, dtype=np.float32)
-        dy, dz = gpu.upload(y), gpu.empty((n,), np.float32)
-        ptrs = (C.c_void_p * 2)(dx.ptr, dy.ptr)
-        codes = (C.c_int * 2)(F32, F32)
-        strides, shape = gpu.lib.i64_array([1, 1]), gpu.lib.i64_array([n])
-        add = gpu.lib.EW_OPS["add"]
+    def host(self):
+        self.A, self.B = gen_batched()
+        lo, hi = shard(8, self.world, self.rank)
+        self.Aloc = np.ascontiguousarray(self.A[lo:hi])
+        self.per = hi - lo
 
-        def step():
-            gpu.check(raw.pb_elementwise(ctx, 0, add, 2, ptrs, codes, strides, 1, shape, F32,
-                                         p_(dz)), "elementwise")
-        step_bytes = 12 * n
-    else:
-        dz = gpu.empty((1,), np.float32)
-        shape = gpu.lib.i64_array([n])
-
-        def step():
-            gpu.check(raw.pb_reduce(ctx, 0, gpu.lib.PB_REDUCE_SUM, F32, p_(dx), 1, shape, 1, F32,
-                                    p_(dz)), "reduce")
-        step_bytes = 4 * n + 4
-
-    for _ in range(args.warmup):
-        step()
-    dist.barrier()
-    with Clocks(gpu.backend.ordinal) as clocks:
-        gpu.busy(step, dist)
-        l0 = gpu.launches()
-        seconds = gpu.timer(step, args.steps)
-    launches = gpu.launches() - l0
-    seconds = dist.max(seconds)
-    z = np.empty(n if which == "elementwise" else 1, np.float32)
-    gpu.check(raw.pb_d2h(ctx, 0, C.c_void_p(z.ctypes.data), p_(dz), z.nbytes), "d2h")
-    what = "elementwise add of two float32 arrays" if which == "elementwise" else "sum of float32 values"
-    result.update({
-        "metric": f"{what} (n = {n}) HBM throughput",
-        "value": step_bytes * args.steps * dist.world / seconds / 1e9, "unit": "GB/s",
-        "ms_per_step": seconds / args.steps * 1e3, "scaling": "weak", "dtype": "f32",
-        "config": {"workload": f"{which}, n = {n} float32, N(0,1), default_rng(6)",
-                   "step_bytes": step_bytes, "parallelism": f"replicas x{dist.world}",
-                   "l2": "operands (1 GB each) larger than the 126 MB L2; no flush needed"},
-        "clocks": clocks.summary(), "gpu_launches": launches,
-        "roofline_kernel": (which, step_bytes, seconds / args.steps),
-        "_check": (which, x, y, z),
-    })
-
-
-def run_batched(gpu: Gpu, args, dist: Dist, result: dict):
-    raw, ctx = gpu.raw, gpu.ctx
-    A, B = gen_batched()
-    per = A.shape[0] // dist.world
-    Aloc = np.ascontiguousarray(A[dist.rank * per:(dist.rank + 1) * per])
-    dA, dB = gpu.upload(Aloc), gpu.upload(B)
-    batch = (per, 16)
-    dC = gpu.empty(batch + (512, 384), np.float32)
-    L = gpu.lib
-
-    def step():
-        gpu.check(raw.pb_gemm(ctx, 0, L.PB_F32, 2, L.i64_array(batch), L.i64_array([16, 1]),
-                              L.i64_array([0, 1]), 512, 384, 256, p_(dA), p_(dB), p_(dC)), "gemm")
-
-    for _ in range(args.warmup):
-        step()
-    dist.barrier()
-    with Clocks(gpu.backend.ordinal) as clocks:
-        gpu.busy(step, dist)
-        l0 = gpu.launches()
-        seconds = gpu.timer(step, args.steps)
-    launches = gpu.launches() - l0
-    seconds = dist.max(seconds)
-    flops = 2.0 * per * 16 * 512 * 384 * 256
-    Cl = np.empty(batch + (512, 384), np.float32)
-    gpu.check(raw.pb_d2h(ctx, 0, C.c_void_p(Cl.ctypes.data), p_(dC), Cl.nbytes), "d2h")
-    result.update({
-        "metric": "batched broadcast GEMM (8,16,512,256)@(1,16,256,384) f32 TFLOP/s",
-        "value": flops * args.steps * dist.world / seconds / 1e12, "unit": "TFLOP/s",
-        "ms_per_step": seconds / args.steps * 1e3, "scaling": "strong", "dtype": "f32 (3xTF32)",
-        "config": {"workload": "BASELINE config 3", "parallelism": f"batch split x{dist.world}"},
-        "clocks": clocks.summary(), "gpu_launches": launches,
-        "roofline_kernel": ("gemm", flops, seconds / args.steps),
-        "_check": ("gemm", Aloc, B, Cl),
-    })
-
-
-def run_norm(gpu: Gpu, args, dist: Dist, result: dict, rows: bool):
-    raw, ctx = gpu.raw, gpu.ctx
-    dtype = np.float64 if args.dtype == "f64" else np.float32
-    span = 300 if dtype == np.float64 else 35
-    n = 1 << 28
-    x = gen_norm(n, dtype, span)
-    code = gpu.lib.dtype_code(dtype)
-    if rows:
-        shape = (65536, 4096)
-        nrows = shape[0] // dist.world
-        xl = np.ascontiguousarray(x.reshape(shape)[dist.rank * nrows:(dist.rank + 1) * nrows])
-        dx, dout = gpu.upload(xl), gpu.empty((nrows,), dtype)
-
-        def step():
-            gpu.check(raw.pb_norm(ctx, 0, code, nrows, shape[1], 1, p_(dx), p_(dout)), "norm")
-    else:
-        per = n // dist.world
-        xl = np.ascontiguousarray(x[dist.rank * per:(dist.rank + 1) * per])
-        dx, dout = gpu.upload(xl), gpu.empty((1,), dtype)
-        if dist.world > 1:
-            uid = C.create_string_buffer(128)
-            if dist.rank == 0:
-                gpu.check(raw.pb_comm_unique_id(uid), "unique id")
-            data = dist.broadcast_bytes(uid.raw if dist.rank == 0 else None, 128)
-            gpu.check(raw.pb_comm_init(ctx, 0, dist.world, dist.rank, data), "comm init")
-            # Peer mailboxes: the partial pairs then travel over NVLink from
-            # the norm kernel itself; every rank agrees, else NCCL all-gather.
-            handle = C.create_string_buffer(64)
-            ok = raw.pb_peer_export(ctx, 0, dist.world, dist.rank, handle) == 0
-            handles = dist.all_gather_bytes(handle.raw if ok else bytes(64), 64)
-            ok = ok and raw.pb_peer_import(ctx, 0, dist.world, b"".join(handles)) == 0
-            p2p = all(v == b"\x01" for v in dist.all_gather_bytes(b"\x01" if ok else b"\x00", 1))
-            if not p2p:
-                raw.pb_peer_close(ctx, 0)
-            exchange = "NVLink peer mailboxes" if p2p else "NCCL all-gather"
-
-            def step():
-                gpu.check(raw.pb_norm_sharded(ctx, 0, code, per, p_(dx), p_(dout)), "norm")
+    def setup(self, gpu, comm):
+        self.gpu, self.comm = gpu, comm
+        self.host()
+        L = gpu.lib
+        self.dA = gpu.upload(self.Aloc)
+        if comm.active:
+            self.dB = gpu.upload(self.B) if self.rank == 0 else gpu.empty(self.B.shape, np.float32)
+            t0 = time.perf_counter()
+            comm.broadcast(self.dB, self.B.nbytes)
+            gpu.sync()
+            self.extra = {"b_broadcast_ms_once": (time.perf_counter() - t0) * 1e3}
         else:
-            def step():
-                gpu.check(raw.pb_norm(ctx, 0, code, 1, per, 1, p_(dx), p_(dout)), "norm")
+            self.dB = gpu.upload(self.B)
+        self.dC = gpu.empty((self.per, 16, 512, 384), np.float32)
+        self.args_gemm = (L.PB_F32, 2, L.i64_array((self.per, 16)), L.i64_array([16, 1]),
+                          L.i64_array([0, 1]), 512, 384, 256)
+        self.units = self.kernel_units = 2.0 * self.per * 16 * 512 * 384 * 256
+        self.kernel_key = "batched:gemm"
 
+    def _gemm(self, dA, dB, dC):
+        g = self.gpu
+        g.check(g.raw.pb_gemm(g.ctx, 0, *self.args_gemm, p_(dA), p_(dB), p_(dC)), "gemm")
+
+    def step(self):
+        self._gemm(self.dA, self.dB, self.dC)
+
+    def e2e_setup(self):
+        self.hA = np.ascontiguousarray(self.Aloc)
+        self.hB = np.ascontiguousarray(self.B)
+        self.hC = np.empty((self.per, 16, 512, 384), np.float32)
+        self.pinned = [self.hA, self.hB, self.hC]
+        self.gpu.pin(self.pinned)
+
+    def e2e_step(self):
+        g = self.gpu
+        g.h2d(self.dA, self.hA)
+        if self.comm.active:
+            if self.rank == 0:
+                g.h2d(self.dB, self.hB)
+            self.comm.broadcast(self.dB, self.hB.nbytes)
+        else:
+            g.h2d(self.dB, self.hB)
+        self.step()
+        g.d2h_async(self.hC, self.dC)
+
+    def e2e_bytes(self):
+        h2d = self.hA.nbytes + (self.hB.nbytes if self.rank == 0 else 0)
+        return h2d, self.hC.nbytes
+
+    def violations(self):
+        C_ = np.empty((self.per, 16, 512, 384), np.float32)
+        self.gpu.d2h(C_, self.dC)
+        rows = np.random.default_rng(0).choice(512, size=64, replace=False)
+        from oracle import numpy_backend, tolerance
+
+        a = self.Aloc[..., rows, :]
+        return tolerance.gemm_violations(C_[..., rows, :], numpy_backend.matmul(a, self.B), a, self.B)
+
+    def cpu_prepare(self):
+        if not hasattr(self, "A"):
+            self.A, self.B = gen_batched()
+
+    def cpu_step(self):
+        from oracle import numpy_backend
+
+        numpy_backend.matmul(self.A, self.B)
+        return 2.0 * 8 * 16 * 512 * 384 * 256, "the full config-3 product (NumPy @ -> OpenBLAS sgemm per batch)"
+
+
+class Gemm(Workload):
+    """Config 1 (1024^3 f32, replicas) and config 5 (row blocks of A, B broadcast)."""
+
+    unit, bound = "TFLOP/s", "tensor"
+
+    def __init__(self, args, dist, which):
+        super().__init__(args, dist)
+        self.which = which
+        if which == "gemm1024":
+            self.seed, self.n, self.np_dtype, self.sharded = 0, args.n or 1024, np.float32, False
+            self.name = "config1_gemm_f32_1024"
+        elif which == "gemm_f32":
+            self.seed, self.n, self.np_dtype, self.sharded = 4, args.n or 16384, np.float32, True
+            self.name = "config5_gemm_f32_16384"
+        else:
+            self.seed, self.n, self.np_dtype, self.sharded = 4, args.n or 8192, np.float64, True
+            self.name = "config5_gemm_f64_8192"
+        self.scaling = "strong" if self.sharded else "weak"
+        self.dtype = "f32 (3xTF32)" if self.np_dtype == np.float32 else "f64 (DMMA)"
+        self.e2e_steps_cap = 5 if self.n >= 8192 else 20
+
+    def metric(self):
+        return f"{np.dtype(self.np_dtype).name} GEMM {self.n}^3 TFLOP/s"
+
+    def config(self):
+        cfg = {"workload": (f"BASELINE config {'1' if self.which == 'gemm1024' else '5'}: "
+                            f"{np.dtype(self.np_dtype).name} {self.n}^3, N(0,1), default_rng({self.seed})"),
+               "parallelism": (f"row blocks of A x{self.world} (B broadcast from rank 0 by NCCL)"
+                               if self.sharded else f"replicas x{self.world}")}
+        op_bytes = 3 * self.n * self.n * np.dtype(self.np_dtype).itemsize
+        cfg["l2"] = (f"operands and output {op_bytes / 1e6:.0f} MB > 126 MB L2" if op_bytes > L2_BYTES
+                     else f"operands and output {op_bytes / 1e6:.1f} MB fit the 126 MB L2; the step "
+                          "is a single small product by definition (no flush)")
+        return cfg
+
+    def setup(self, gpu, comm):
+        self.gpu, self.comm = gpu, comm
+        A, self.B = gen_gemm(self.seed, self.n, self.np_dtype)
+        n = self.n
+        lo, hi = shard(n, self.world, self.rank) if self.sharded else (0, n)
+        self.rows = hi - lo
+        self.Aloc = np.ascontiguousarray(A[lo:hi])
+        del A
+        self.dA = gpu.upload(self.Aloc)
+        if self.sharded and comm.active:
+            self.dB = gpu.upload(self.B) if self.rank == 0 else gpu.empty(self.B.shape, self.np_dtype)
+            t0 = time.perf_counter()
+            comm.broadcast(self.dB, self.B.nbytes)
+            gpu.sync()
+            self.extra = {"b_broadcast_ms_once": (time.perf_counter() - t0) * 1e3}
+        else:
+            self.dB = gpu.upload(self.B)
+        self.dC = gpu.empty((self.rows, n), self.np_dtype)
+        self.code = gpu.lib.dtype_code(self.np_dtype)
+        self.ns = gpu.lib.i64_array([])
+        self.units = self.kernel_units = 2.0 * self.rows * n * n
+        self.kernel_key = f"{self.which}:gemm"
+
+    def step(self):
+        g, n = self.gpu, self.n
+        g.check(g.raw.pb_gemm(g.ctx, 0, self.code, 0, self.ns, self.ns, self.ns, self.rows, n, n,
+                              p_(self.dA), p_(self.dB), p_(self.dC)), "gemm")
+
+    def e2e_setup(self):
+        self.hC = np.empty((self.rows, self.n), self.np_dtype)
+        self.pinned = [self.Aloc, self.B, self.hC]
+        self.gpu.pin(self.pinned)
+
+    def e2e_step(self):
+        g = self.gpu
+        g.h2d(self.dA, self.Aloc)
+        if self.sharded and self.comm.active:
+            if self.rank == 0:
+                g.h2d(self.dB, self.B)
+            self.comm.broadcast(self.dB, self.B.nbytes)
+        else:
+            g.h2d(self.dB, self.B)
+        self.step()
+        g.d2h_async(self.hC, self.dC)
+
+    def e2e_bytes(self):
+        own_b = (not (self.sharded and self.comm.active)) or self.rank == 0
+        return self.Aloc.nbytes + (self.B.nbytes if own_b else 0), self.hC.nbytes
+
+    def violations(self):
+        from oracle import numpy_backend, tolerance
+
+        Cl = np.empty((self.rows, self.n), self.np_dtype)
+        self.gpu.d2h(Cl, self.dC)
+        if self.n <= 2048:
+            return tolerance.gemm_violations(Cl, numpy_backend.matmul(self.Aloc, self.B), self.Aloc, self.B)
+        rows = np.random.default_rng(0).choice(self.rows, size=min(64, self.rows), replace=False)
+        a = self.Aloc[rows]
+        return tolerance.gemm_violations(Cl[rows], numpy_backend.matmul(a, self.B), a, self.B)
+
+    def cpu_prepare(self):
+        # Config 1 whole; config 5 a block of rows (OpenBLAS runs such a block
+        # at its full rate; the whole product takes seconds to minutes on CPU).
+        self.sample_rows = self.n if self.n <= 2048 else 256
+        if getattr(self, "Aloc", None) is not None and self.Aloc.shape[0] >= self.sample_rows:
+            A = self.Aloc
+        else:
+            A, self.B = gen_gemm(self.seed, self.n, self.np_dtype)
+        self.Asample = np.ascontiguousarray(A[: self.sample_rows])
+
+    def cpu_step(self):
+        from oracle import numpy_backend
+
+        numpy_backend.matmul(self.Asample, self.B)
+        what = ("the full product" if self.sample_rows == self.n
+                else f"{self.sample_rows} rows of A times the full B")
+        return 2.0 * self.sample_rows * self.n * self.n, f"{what} (NumPy @ -> OpenBLAS)"
+
+
+class GemvDot(Workload):
+    """GEMV 16384^2 + DOT 2^26, one replica per rank."""
+
+    name = "config2_gemv_dot_f32"
+
+    def metric(self):
+        return "GEMV 16384x16384 + DOT 2^26 float32 HBM throughput"
+
+    def config(self):
+        return {"workload": "BASELINE config 2: y = A@x (A 16384x16384 f32) + DOT of two 2^26 f32 "
+                            "vectors, U[-1,1], default_rng(1)",
+                "parallelism": f"replicas x{self.world}",
+                "l2": "inputs (1.6 GB) larger than the 126 MB L2; no flush needed"}
+
+    def setup(self, gpu, comm):
+        self.gpu = gpu
+        self.A, self.x, self.u, self.v = gen_gemv_dot()
+        self.M, self.K = self.A.shape
+        self.n = self.u.size
+        self.bytes_gemv = 4 * (self.M * self.K + self.K + self.M)
+        self.bytes_dot = 2 * 4 * self.n
+        self.dA, self.dx, self.du, self.dv = (gpu.upload(t) for t in (self.A, self.x, self.u, self.v))
+        self.dy, self.dd = gpu.empty((self.M,), np.float32), gpu.empty((1,), np.float32)
+        self.units = self.bytes_gemv + self.bytes_dot
+        self.kernel_units = self.bytes_gemv
+        self.kernel_key = "gemv_dot:gemv"
+
+    def gemv(self):
+        g = self.gpu
+        g.check(g.raw.pb_gemv(g.ctx, 0, g.lib.PB_F32, self.M, self.K, p_(self.dA), p_(self.dx),
+                              p_(self.dy)), "gemv")
+
+    def dot(self):
+        g = self.gpu
+        g.check(g.raw.pb_dot(g.ctx, 0, g.lib.PB_F32, self.n, p_(self.du), p_(self.dv), p_(self.dd)),
+                "dot")
+
+    def step(self):
+        self.gemv()
+        self.dot()
+
+    def kernel_step(self):
+        self.gemv()
+
+    def more_kernels(self):
+        t, _ = self.gpu.kernel_seconds(self.dot, self.args.steps)
+        return {"gemv_gbs": None, "dot_ms": t * 1e3, "dot_gbs": self.bytes_dot / t / 1e9}
+
+    def e2e_setup(self):
+        self.hy = np.empty(self.M, np.float32)
+        self.hd = np.empty(1, np.float32)
+        self.pinned = [self.A, self.x, self.u, self.v, self.hy, self.hd]
+        self.gpu.pin(self.pinned)
+
+    def e2e_step(self):
+        g = self.gpu
+        for h, dbuf in ((self.A, self.dA), (self.x, self.dx), (self.u, self.du), (self.v, self.dv)):
+            g.h2d(dbuf, h)
+        self.step()
+        g.d2h_async(self.hy, self.dy)
+        g.d2h_async(self.hd, self.dd)
+
+    def e2e_bytes(self):
+        return sum(t.nbytes for t in (self.A, self.x, self.u, self.v)), self.hy.nbytes + 4
+
+    def violations(self):
+        from oracle import numpy_backend, tolerance
+
+        y = np.empty(self.M, np.float32)
+        d = np.empty(1, np.float32)
+        self.gpu.d2h(y, self.dy)
+        self.gpu.d2h(d, self.dd)
+        bad = tolerance.gemm_violations(y, numpy_backend.matmul(self.A, self.x), self.A, self.x)
+        bad += tolerance.gemm_violations(d.reshape(()), numpy_backend.dot(self.u, self.v), self.u, self.v)
+        return bad
+
+    def cpu_prepare(self):
+        if not hasattr(self, "A"):
+            self.A, self.x, self.u, self.v = gen_gemv_dot()
+
+    def cpu_step(self):
+        from oracle import numpy_backend
+
+        numpy_backend.matmul(self.A, self.x)
+        numpy_backend.dot(self.u, self.v)
+        return (4.0 * (self.A.size + self.x.size + self.A.shape[0]) + 8.0 * self.u.size,
+                "the full step (NumPy @ -> OpenBLAS sgemv + sdot)")
+
+
+class Norm(Workload):
+    """BASELINE config 4a (full norm, slices + peer-mailbox merge) and 4b
+    (axis=1 row norms, row blocks)."""
+
+    scaling = "strong"
+
+    def __init__(self, args, dist, rows: bool, np_dtype):
+        super().__init__(args, dist)
+        self.rows_mode, self.np_dtype = rows, np.dtype(np_dtype)
+        tag = "f64" if self.np_dtype == np.float64 else "f32"
+        self.dtype = tag
+        self.name = f"config4b_rows_{tag}" if rows else f"config4a_norm_{tag}"
+
+    def metric(self):
+        what = "rows (65536,4096)" if self.rows_mode else "full 2^28"
+        return f"scaled norm {what} {self.np_dtype.name} GB/s"
+
+    def config(self):
+        span = 300 if self.np_dtype == np.float64 else 35
+        cfg = {"workload": (f"BASELINE config 4{'b' if self.rows_mode else 'a'}: "
+                            f"{'axis=1 norms of (65536,4096)' if self.rows_mode else 'norm of 2^28 values'} "
+                            f"{self.np_dtype.name}, N(0,1)*10^U(-{span},{span}), default_rng(3)"),
+               "l2": f"input {2 ** 28 * self.np_dtype.itemsize / 1e9:.2f} GB > 126 MB L2"}
+        if self.rows_mode:
+            cfg["parallelism"] = f"row blocks x{self.world}"
+        else:
+            cfg["parallelism"] = f"slices x{self.world}" + (
+                f", (scale, ssq) pairs merged through {self.exchange}" if self.world > 1 else "")
+        return cfg
+
+    exchange = None
+
+    def setup(self, gpu, comm):
+        self.gpu, self.comm = gpu, comm
+        self.x = norm_input(self.np_dtype)
+        self.code = gpu.lib.dtype_code(self.np_dtype)
+        if self.rows_mode:
+            shape = (65536, 4096)
+            lo, hi = shard(shape[0], self.world, self.rank)
+            self.nrows = hi - lo
+            self.xl = np.ascontiguousarray(self.x.reshape(shape)[lo:hi])
+            self.out = gpu.empty((self.nrows,), self.np_dtype)
+            self.kernel_key = f"norm_rows_{self.dtype}:norm"
+        else:
+            lo, hi = shard(self.x.size, self.world, self.rank)
+            self.xl = self.x[lo:hi]
+            self.out = gpu.empty((1,), self.np_dtype)
+            self.exchange = comm.exchange
+            self.kernel_key = f"norm_{self.dtype}:norm"
+        self.dx = gpu.upload(self.xl)
+        self.units = self.kernel_units = float(self.xl.nbytes)
+
+    def step(self):
+        g = self.gpu
+        if self.rows_mode:
+            g.check(g.raw.pb_norm(g.ctx, 0, self.code, self.nrows, 4096, 1, p_(self.dx), p_(self.out)),
+                    "norm")
+        elif self.comm.active:
+            g.check(g.raw.pb_norm_sharded(g.ctx, 0, self.code, self.xl.size, p_(self.dx), p_(self.out)),
+                    "norm")
+        else:
+            g.check(g.raw.pb_norm(g.ctx, 0, self.code, 1, self.xl.size, 1, p_(self.dx), p_(self.out)),
+                    "norm")
+
+    def e2e_setup(self):
+        self.hx = np.ascontiguousarray(self.xl)
+        self.hout = np.empty(self.nrows if self.rows_mode else 1, self.np_dtype)
+        self.pinned = [self.hx, self.hout]
+        self.gpu.pin(self.pinned)
+
+    def e2e_step(self):
+        self.gpu.h2d(self.dx, self.hx)
+        self.step()
+        self.gpu.d2h_async(self.hout, self.out)
+
+    def e2e_bytes(self):
+        return self.hx.nbytes, self.hout.nbytes
+
+    def violations(self):
+        from oracle import numpy_backend, tolerance
+
+        out = np.empty(self.nrows if self.rows_mode else 1, self.np_dtype)
+        self.gpu.d2h(out, self.out)
+        if self.rows_mode:
+            sel = np.arange(0, self.xl.shape[0], max(1, self.xl.shape[0] // 256))
+            return tolerance.norm_violations(out[sel], numpy_backend.norm(self.xl[sel], axis=1))
+        if self.rank != 0:
+            return 0  # the merged norm is the same on every rank; rank 0 checks it
+        return tolerance.norm_violations(out.reshape(()), numpy_backend.norm(self.x),
+                                         exact=exact_norm(self.x))
+
+    def cpu_prepare(self):
+        self.x = norm_input(self.np_dtype)
+
+    def cpu_step(self):
+        from oracle import numpy_backend
+
+        if self.rows_mode:
+            sample = self.x.reshape(65536, 4096)[:4096]
+            numpy_backend.norm(sample, axis=1)
+            return float(sample.nbytes), "4096 of the 65536 rows through the NumPy-backend norm"
+        sample = self.x[: 1 << 24]
+        numpy_backend.norm(sample)
+        return float(sample.nbytes), "2^24 of the 2^28 values through the NumPy-backend norm"
+
+
+class Vecmat(Workload):
+    """x @ A (vector @ matrix), float32 16384^2: the skinny kernel, replicas."""
+
+    name = "vecmat_f32_16384"
+
+    def metric(self):
+        return f"vector @ matrix ({self.n} @ {self.n}x{self.n}) float32 HBM throughput"
+
+    def config(self):
+        return {"workload": f"x @ A, A {self.n}x{self.n} f32, U[-1,1], default_rng(5) (around the "
+                            "path: the survey's vector edge shapes)",
+                "parallelism": f"replicas x{self.world}",
+                "l2": "A (1.07 GB) larger than the 126 MB L2; no flush needed"}
+
+    def __init__(self, args, dist):
+        super().__init__(args, dist)
+        self.n = args.n or 16384
+
+    def setup(self, gpu, comm):
+        self.gpu = gpu
+        rng = np.random.default_rng(5)
+        n = self.n
+        self.A = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+        self.x = rng.uniform(-1, 1, n).astype(np.float32)
+        self.dx, self.dA = gpu.upload(self.x), gpu.upload(self.A)
+        self.dy = gpu.empty((n,), np.float32)
+        self.ns = gpu.lib.i64_array([])
+        self.units = self.kernel_units = 4.0 * (n * n + 2 * n)
+        self.kernel_key = "vecmat:skinny"
+
+    def step(self):
+        g, n = self.gpu, self.n
+        g.check(g.raw.pb_gemm(g.ctx, 0, g.lib.PB_F32, 0, self.ns, self.ns, self.ns, 1, n, n,
+                              p_(self.dx), p_(self.dA), p_(self.dy)), "gemm")
+
+    def e2e_setup(self):
+        self.hy = np.empty(self.n, np.float32)
+        self.pinned = [self.A, self.x, self.hy]
+        self.gpu.pin(self.pinned)
+
+    def e2e_step(self):
+        self.gpu.h2d(self.dx, self.x)
+        self.gpu.h2d(self.dA, self.A)
+        self.step()
+        self.gpu.d2h_async(self.hy, self.dy)
+
+    def e2e_bytes(self):
+        return self.A.nbytes + self.x.nbytes, self.hy.nbytes
+
+    def violations(self):
+        from oracle import numpy_backend, tolerance
+
+        y = np.empty(self.n, np.float32)
+        self.gpu.d2h(y, self.dy)
+        x2 = self.x.reshape(1, -1)
+        return tolerance.gemm_violations(y.reshape(1, -1), numpy_backend.matmul(x2, self.A), x2, self.A)
+
+    def cpu_prepare(self):
+        if not hasattr(self, "A"):
+            rng = np.random.default_rng(5)
+            self.A = rng.uniform(-1, 1, (self.n, self.n)).astype(np.float32)
+            self.x = rng.uniform(-1, 1, self.n).astype(np.float32)
+
+    def cpu_step(self):
+        from oracle import numpy_backend
+
+        numpy_backend.matmul(self.x, self.A)
+        return 4.0 * (self.n * self.n + 2 * self.n), "the full product (NumPy @ -> OpenBLAS sgemv)"
+
+
+class Around(Workload):
+    """Operations around the path on 2^28 float32 values: elementwise add of
+    two arrays (pb_elementwise) or their sum (pb_reduce)."""
+
+    def __init__(self, args, dist, which):
+        super().__init__(args, dist)
+        self.which = which
+        self.n = args.n or (1 << 28)
+        self.name = f"{which}_f32_2p28"
+
+    def metric(self):
+        what = "elementwise add of two float32 arrays" if self.which == "elementwise" else "sum of float32 values"
+        return f"{what} (n = {self.n}) HBM throughput"
+
+    def config(self):
+        return {"workload": f"{self.which}, n = {self.n} float32, N(0,1), default_rng(6)",
+                "parallelism": f"replicas x{self.world}",
+                "l2": "operands (1 GB each) larger than the 126 MB L2; no flush needed"}
+
+    def _inputs(self):
+        rng = np.random.default_rng(6)
+        self.x = rng.standard_normal(self.n, dtype=np.float32)
+        self.y = rng.standard_normal(self.n, dtype=np.float32) if self.which == "elementwise" else None
+
+    def setup(self, gpu, comm):
+        self.gpu = gpu
+        self._inputs()
+        L = gpu.lib
+        self.dx = gpu.upload(self.x)
+        if self.which == "elementwise":
+            self.dy, self.dz = gpu.upload(self.y), gpu.empty((self.n,), np.float32)
+            self.ptrs = (C.c_void_p * 2)(self.dx.ptr, self.dy.ptr)
+            self.codes = (C.c_int * 2)(L.PB_F32, L.PB_F32)
+            self.strides, self.shape = L.i64_array([1, 1]), L.i64_array([self.n])
+            self.units = self.kernel_units = 12.0 * self.n
+        else:
+            self.dz = gpu.empty((1,), np.float32)
+            self.shape = L.i64_array([self.n])
+            self.units = self.kernel_units = 4.0 * self.n + 4
+        self.kernel_key = f"{self.which}:{self.which}"
+
+    def step(self):
+        g, L = self.gpu, self.gpu.lib
+        if self.which == "elementwise":
+            g.check(g.raw.pb_elementwise(g.ctx, 0, L.EW_OPS["add"], 2, self.ptrs, self.codes, self.strides,
+                                         1, self.shape, L.PB_F32, p_(self.dz)), "elementwise")
+        else:
+            g.check(g.raw.pb_reduce(g.ctx, 0, L.PB_REDUCE_SUM, L.PB_F32, p_(self.dx), 1, self.shape, 1,
+                                    L.PB_F32, p_(self.dz)), "reduce")
+
+    def e2e_setup(self):
+        self.hz = np.empty(self.n if self.which == "elementwise" else 1, np.float32)
+        self.pinned = [self.x, self.hz] + ([self.y] if self.y is not None else [])
+        self.gpu.pin(self.pinned)
+
+    def e2e_step(self):
+        self.gpu.h2d(self.dx, self.x)
+        if self.y is not None:
+            self.gpu.h2d(self.dy, self.y)
+        self.step()
+        self.gpu.d2h_async(self.hz, self.dz)
+
+    def e2e_bytes(self):
+        return self.x.nbytes + (self.y.nbytes if self.y is not None else 0), self.hz.nbytes
+
+    def violations(self):
+        from oracle import numpy_backend, tolerance
+
+        z = np.empty(self.n if self.which == "elementwise" else 1, np.float32)
+        self.gpu.d2h(z, self.dz)
+        if self.which == "elementwise":
+            want = numpy_backend.elementwise("add", (self.x, self.y), np.float32)
+            return int(np.sum(want.view(np.uint32) != z.view(np.uint32)))
+        want = numpy_backend.reduce(self.x, (0,), False, np.float32)
+        bound = 4 * self.x.size * tolerance.unit_roundoff(np.float32) * float(
+            np.sum(np.abs(self.x), dtype=np.float64))
+        return int(abs(float(z[0]) - float(want)) > bound)
+
+    def cpu_prepare(self):
+        if not hasattr(self, "x"):
+            self._inputs()
+
+    def cpu_step(self):
+        from oracle import numpy_backend
+
+        m = 1 << 25
+        if self.which == "elementwise":
+            numpy_backend.elementwise("add", (self.x[:m], self.y[:m]), np.float32)
+            return 12.0 * m, "2^25 of the 2^28 elements (NumPy add)"
+        numpy_backend.reduce(self.x[:m], (0,), False, np.float32)
+        return 4.0 * m, "2^25 of the 2^28 values (NumPy sum)"
+
+
+# ------------------------------------------------------ measurement --
+
+def measure(w: Workload, gpu: Gpu, comm: Comm, args, dist: Dist, pk: dict) -> dict:
+    """Everything the JSON line reports for one workload on this rank;
+    collective steps (barriers, max) are taken identically on every rank."""
+    w.setup(gpu, comm)
     for _ in range(args.warmup):
-        step()
+        w.step()
+    gpu.sync()
     dist.barrier()
     with Clocks(gpu.backend.ordinal) as clocks:
-        gpu.busy(step, dist)
+        gpu.busy(w.step, dist)
+        dist.barrier()
         l0 = gpu.launches()
-        seconds = gpu.timer(step, args.steps)
-    launches = gpu.launches() - l0
+        seconds = gpu.timer(w.step, args.steps)
+        launches = gpu.launches() - l0
     seconds = dist.max(seconds)
-    nbytes = xl.nbytes
-    out = np.empty(nrows if rows else 1, dtype)
-    gpu.check(raw.pb_d2h(ctx, 0, C.c_void_p(out.ctypes.data), p_(dout), out.nbytes), "d2h")
-    result.update({
-        "metric": f"scaled norm {'rows (65536,4096)' if rows else 'full 2^28'} {np.dtype(dtype).name} GB/s",
-        "value": nbytes * args.steps * dist.world / seconds / 1e9, "unit": "GB/s",
-        "ms_per_step": seconds / args.steps * 1e3, "scaling": "strong",
-        "dtype": "f64" if dtype == np.float64 else "f32",
-        "config": {"workload": "BASELINE config 4" + ("b" if rows else "a"),
-                   "parallelism": f"slices x{dist.world}"
-                   + (f", pairs merged through {exchange}" if not rows and dist.world > 1 else "")},
-        "clocks": clocks.summary(), "gpu_launches": launches,
-        "roofline_kernel": ("norm", nbytes, seconds / args.steps),
-        "_check": ("norm_rows", xl, out) if rows else ("norm", x, out),
-    })
-    if not rows and dist.world > 1:
-        raw.pb_peer_close(ctx, 0)
-        raw.pb_comm_destroy(ctx, 0)
+    total_units = dist.sum(w.units)
 
+    # Main kernel alone (events around each launch), max over ranks.
+    kt, kl = gpu.kernel_seconds(w.kernel_step, args.steps)
+    kt = dist.max(kt or 0.0)
+    more = w.more_kernels() if hasattr(w, "more_kernels") else {}
 
-# ------------------------------------------------------ reference arm --
-
-def cpu_threads():
+    # End to end through the C ABI with pinned host buffers.
+    w.e2e_setup()
     try:
-        from threadpoolctl import threadpool_info
+        w.e2e_step()
+        gpu.sync()
+        dist.barrier()
+        e2e_steps = max(1, min(args.steps, w.e2e_steps_cap))
+        e2e_seconds = dist.max(gpu.timer(w.e2e_step, e2e_steps))
+    finally:
+        gpu.unpin(w.pinned)
+    h2d, d2h = w.e2e_bytes()
+    h2d, d2h = dist.sum(h2d), dist.sum(d2h)
 
-        info = [i for i in threadpool_info() if i.get("user_api") == "blas"]
-        if info:
-            return int(info[0]["num_threads"])
-    except Exception:  # noqa: BLE001
-        pass
-    return len(os.sched_getaffinity(0))
+    bad = int(dist.sum(float(w.violations())))
+
+    scale = w.scale()
+    rec = {
+        "metric": w.metric(), "value": total_units * args.steps / seconds / scale, "unit": w.unit,
+        "ms_per_step": seconds / args.steps * 1e3, "scaling": w.scaling, "dtype": w.dtype,
+        "config": w.config(), "clocks": clocks.summary(), "gpu_launches": launches,
+    }
+    rec["roofline"] = roofline(w, kt, pk)
+    rec["kernel_ms"] = kt * 1e3
+    if more:
+        more["gemv_gbs"] = w.kernel_units / kt / 1e9 if kt else None
+        rec["kernels"] = more
+    rec["e2e"] = {"value": total_units * e2e_steps / e2e_seconds / scale, "unit": w.unit,
+                  "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                  "ms_per_step": e2e_seconds / e2e_steps * 1e3,
+                  "note": "whole job: every rank's pinned host inputs copied in and results read "
+                          "back each step" + (", B broadcast by NCCL from rank 0" if getattr(w, "comm", None)
+                                              and getattr(w.comm, "active", False) and hasattr(w, "dB") else "")}
+    rec["parity_violations"] = bad
+    if w.extra:
+        rec.update(w.extra)
+    return rec
 
 
-def cpu_gemv_dot(budget_s: float):
-    """The reference's NumPy backend on this workload: A @ x and u @ v."""
-    from oracle import numpy_backend
+def roofline(w: Workload, kt: float, pk: dict) -> dict:
+    if not kt:
+        return {"bound": w.bound, "achieved": None, "peak": None, "frac": None, "traffic": None}
+    traffic, how = traffic_per_launch(w.kernel_key, w.kernel_units)
+    if w.bound == "hbm":
+        achieved = w.kernel_units / kt / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / pk["hbm_gbs"], "peak_source": f"{pk['source']} copy bandwidth"}
+    else:
+        achieved = w.kernel_units / kt / 1e12
+        if "f64" in w.dtype:
+            peak, src = SPEC_FP64_TFLOPS, "B200 specification FP64 tensor 40 TFLOP/s (nominal)"
+            alt = {"cublas_dgemm_measured": CUBLAS_DGEMM_TFLOPS,
+                   "frac_of_cublas_dgemm": achieved / CUBLAS_DGEMM_TFLOPS}
+        else:
+            # 3xTF32: three TF32 products per logical product; TF32 runs at
+            # half the bf16 rate.  A step of seconds runs at the sustained
+            # (power-capped) clock, a short one at the burst clock.
+            sustained = w.units >= 1e12
+            bf16 = pk["bf16_tflops_sustained"] if sustained else pk["bf16_tflops"]
+            peak = bf16 / 2 / 3
+            src = (f"{pk['source']} bf16 {'sustained' if sustained else 'burst'} {bf16:.1f} / 2 (TF32) / 3 "
+                   "(3xTF32)")
+            alt = {"cublas_tf32_over_3": CUBLAS_TF32_TFLOPS / 3,
+                   "frac_of_cublas_tf32_over_3": achieved / (CUBLAS_TF32_TFLOPS / 3)}
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "peak_source": src, **alt}
+    roof.update({"traffic": traffic, "traffic_source": how, "kernel": w.kernel_key,
+                 "algorithmic_units_per_launch": w.kernel_units,
+                 "kernel_ms_avg": kt * 1e3})
+    return roof
 
-    A, x, u, v = gen_gemv_dot()
-    numpy_backend.matmul(A, x)
-    numpy_backend.dot(u, v)
-    step_bytes = 4 * (A.size + x.size + A.shape[0]) + 8 * u.size
-    reps, t0 = 0, time.perf_counter()
+
+def cpu_time(w: Workload, budget_s: float, max_steps: int, warmup: int = 1):
+    """The reference's CPU path on w's bounded sample: (units/s, steps, sample)."""
+    w.cpu_prepare()
+    for _ in range(max(1, warmup)):
+        w.cpu_step()
+    done, steps, t0 = 0.0, 0, time.perf_counter()
+    what = ""
     while True:
-        numpy_backend.matmul(A, x)
-        numpy_backend.dot(u, v)
-        reps += 1
-        if time.perf_counter() - t0 > budget_s or reps >= 200:
+        units, what = w.cpu_step()
+        done += units
+        steps += 1
+        if steps >= max_steps or time.perf_counter() - t0 > budget_s:
             break
-    seconds = (time.perf_counter() - t0) / reps
-    return {"value": step_bytes / seconds / 1e9, "unit": "GB/s", "cores": cpu_threads(),
-            "kind": "port", "sample": f"{reps} full steps (GEMV 16384^2 + DOT 2^26) with NumPy/OpenBLAS",
-            "ms_per_step": seconds * 1e3}
+    seconds = time.perf_counter() - t0
+    return done / seconds / w.scale(), steps, what, seconds / steps
 
+
+def make_workloads(args, dist):
+    """Workloads in run order, each built when its turn comes (so only one
+    config's inputs are held at a time)."""
+    wl = args.workload
+    if wl == "suite":
+        yield Batched(args, dist)
+        yield Gemm(args, dist, "gemm1024")
+        yield GemvDot(args, dist)
+        yield Norm(args, dist, False, np.float32)
+        yield Norm(args, dist, True, np.float32)
+        yield Norm(args, dist, False, np.float64)
+        yield Norm(args, dist, True, np.float64)
+        yield Gemm(args, dist, "gemm_f32")
+        yield Gemm(args, dist, "gemm_f64")
+        yield Vecmat(args, dist)
+        yield Residual(args, dist)
+        return
+    dt = np.float64 if args.dtype == "f64" else np.float32
+    yield {"batched": lambda: Batched(args, dist), "gemm1024": lambda: Gemm(args, dist, "gemm1024"),
+           "gemm_f32": lambda: Gemm(args, dist, "gemm_f32"), "gemm_f64": lambda: Gemm(args, dist, "gemm_f64"),
+           "gemv_dot": lambda: GemvDot(args, dist), "norm": lambda: Norm(args, dist, False, dt),
+           "norm_rows": lambda: Norm(args, dist, True, dt), "vecmat": lambda: Vecmat(args, dist),
+           "elementwise": lambda: Around(args, dist, "elementwise"),
+           "reduce": lambda: Around(args, dist, "reduce"),
+           "residual": lambda: Residual(args, dist)}[wl]()
+
+
+class Residual(Workload):
+    """b - A @ x with the subtraction fused into the GEMV epilogue (the
+    compiled-plan residual, src/openpacho/_compiler.py:157-176), float32
+    16384^2, against the unfused GEMV + elementwise subtract pair."""
+
+    name = "residual_f32_16384"
+
+    def metric(self):
+        return "residual b - A @ x (A 16384x16384 float32, fused GEMV epilogue) HBM throughput"
+
+    def config(self):
+        return {"workload": "b - A @ x, A 16384x16384 f32, x and b 16384, U[-1,1], default_rng(7)",
+                "parallelism": f"replicas x{self.world}",
+                "l2": "A (1.07 GB) larger than the 126 MB L2; no flush needed"}
+
+    def _inputs(self):
+        rng = np.random.default_rng(7)
+        self.A = rng.uniform(-1, 1, (16384, 16384)).astype(np.float32)
+        self.x = rng.uniform(-1, 1, 16384).astype(np.float32)
+        self.b = rng.uniform(-1, 1, 16384).astype(np.float32)
+
+    def setup(self, gpu, comm):
+        self.gpu = gpu
+        self._inputs()
+        self.dA, self.dx, self.db = (gpu.upload(t) for t in (self.A, self.x, self.b))
+        self.dr = gpu.empty((16384,), np.float32)
+        self.dy = gpu.empty((16384,), np.float32)
+        self.units = self.kernel_units = 4.0 * (16384 * 16384 + 3 * 16384)
+        self.kernel_key = "residual:gemv"
+
+    def step(self):
+        g = self.gpu
+        g.check(g.raw.pb_gemv_residual(g.ctx, 0, g.lib.PB_F32, 16384, 16384, p_(self.dA), p_(self.dx),
+                                       p_(self.db), p_(self.dr)), "gemv_residual")
+
+    def unfused(self):
+        g, L = self.gpu, self.gpu.lib
+        g.check(g.raw.pb_gemv(g.ctx, 0, L.PB_F32, 16384, 16384, p_(self.dA), p_(self.dx), p_(self.dy)),
+                "gemv")
+        ptrs = (C.c_void_p * 2)(self.db.ptr, self.dy.ptr)
+        codes = (C.c_int * 2)(L.PB_F32, L.PB_F32)
+        g.check(g.raw.pb_elementwise(g.ctx, 0, L.EW_OPS["subtract"], 2, ptrs, codes, L.i64_array([1, 1]), 1,
+                                     L.i64_array([16384]), L.PB_F32, p_(self.dy)), "subtract")
+
+    def more_kernels(self):
+        t = self.gpu.timer(self.unfused, self.args.steps) / self.args.steps
+        return {"unfused_gemv_then_subtract_ms": t * 1e3,
+                "unfused_bytes": 4.0 * (16384 * 16384 + 2 * 16384 + 16384) + 12.0 * 16384,
+                "fused_bytes": self.units}
+
+    def e2e_setup(self):
+        self.hr = np.empty(16384, np.float32)
+        self.pinned = [self.A, self.x, self.b, self.hr]
+        self.gpu.pin(self.pinned)
+
+    def e2e_step(self):
+        for h, dbuf in ((self.A, self.dA), (self.x, self.dx), (self.b, self.db)):
+            self.gpu.h2d(dbuf, h)
+        self.step()
+        self.gpu.d2h_async(self.hr, self.dr)
+
+    def e2e_bytes(self):
+        return self.A.nbytes + self.x.nbytes + self.b.nbytes, self.hr.nbytes
+
+    def violations(self):
+        from oracle import numpy_backend, tolerance
+
+        r = np.empty(16384, np.float32)
+        self.gpu.d2h(r, self.dr)
+        # The product is rounded to float32 before the subtraction
+        # (src/openpacho/_gemv.py:1-6), so the bound is the GEMV's plus the
+        # rounding of the difference.
+        y = numpy_backend.matmul(self.A, self.x)
+        want = numpy_backend.elementwise("subtract", (self.b, y), np.float32)
+        bound = tolerance.gemm_bound(self.A, self.x) + tolerance.unit_roundoff(np.float32) * (
+            np.abs(self.b.astype(np.float64)) + np.abs(y.astype(np.float64)))
+        return int(np.sum(~(np.abs(r.astype(np.float64) - want.astype(np.float64)) <= 2 * bound)))
+
+    def cpu_prepare(self):
+        if not hasattr(self, "A"):
+            self._inputs()
+
+    def cpu_step(self):
+        from oracle import numpy_backend
+
+        y = numpy_backend.matmul(self.A, self.x)
+        numpy_backend.elementwise("subtract", (self.b, y), np.float32)
+        return 4.0 * (16384 * 16384 + 3 * 16384), "the full residual (NumPy @ -> OpenBLAS sgemv, then subtract)"
+
+
+# ----------------------------------------------------- reference arm --
 
 def reference_arm(args, dist: Dist):
+    """The reference's CPU implementation of the path (the NumPy-backend
+    restatement in oracle/, src/openpacho/backends.py:139-142 and
+    src/openpacho/_norm.py:44-52) on the host cores, same workloads, configs
+    and units as the b200 arm.  Under torchrun rank 0 alone runs."""
     if dist.rank != 0:
         return 0
-    if args.workload != "gemv_dot":
-        print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the "
-                          "default workload only"}))
-        return 0
-    from oracle import numpy_backend
-
-    A, x, u, v = gen_gemv_dot()
-    for _ in range(max(1, args.warmup)):
-        numpy_backend.matmul(A, x)
-        numpy_backend.dot(u, v)
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        numpy_backend.matmul(A, x)
-        numpy_backend.dot(u, v)
-        times.append(time.perf_counter() - t0)
-    step_bytes = 4 * (A.size + x.size + A.shape[0]) + 8 * u.size
-    seconds = sum(times)
-    value = step_bytes * args.steps / seconds / 1e9
-    print(json.dumps({
-        "impl": "reference", "metric": "GEMV 16384x16384 + DOT 2^26 float32 HBM throughput",
-        "value": value, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": seconds / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": "BASELINE config 2 (see the b200 arm)"},
-        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cpu_threads(), "kind": "port",
-                         "sample": f"{args.steps} full steps through the NumPy-backend restatement "
-                                   "(NumPy @ -> OpenBLAS sgemv + sdot)"},
-        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }))
+    limiter, threads = blas_threads_all()
+    records = {}
+    headline = None
+    for w in make_workloads(args, dist):
+        budget = 20.0 if headline is None else 4.0
+        value, steps, what, sec = cpu_time(w, budget, max_steps=args.steps, warmup=min(args.warmup, 2))
+        # Configs are built as on the b200 arm for this world size.
+        if isinstance(w, Norm) and not w.rows_mode and dist.world > 1:
+            w.exchange = "NVLink peer mailboxes"
+        rec = {"metric": w.metric(), "value": value, "unit": w.unit, "ms_per_step": sec * 1e3,
+               "steps": steps, "scaling": w.scaling, "dtype": w.dtype, "config": w.config(),
+               "cpu_baseline": {"value": value, "unit": w.unit, "cores": threads, "kind": "port",
+                                "sample": f"{steps} steps of {what}; OpenBLAS threads {threads} of "
+                                          f"{cpu_cores()} host cores"},
+               "e2e": {"value": value, "unit": w.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        if headline is None:
+            headline = rec
+        else:
+            records[w.name] = rec
+    line = {
+        "impl": "reference", "metric": headline["metric"], "value": headline["value"],
+        "unit": headline["unit"], "n_gpus": args.gpus, "steps": headline["steps"], "warmup": args.warmup,
+        "ms_per_step": headline["ms_per_step"], "higher_is_better": True, "scaling": headline["scaling"],
+        "vs_baseline": None, "dtype": headline["dtype"], "data": DATA, "config": headline["config"],
+        "cpu_baseline": headline["cpu_baseline"], "e2e": headline["e2e"],
+    }
+    if records:
+        line["configs"] = records
+    print(json.dumps(line))
+    del limiter
     return 0
+
+
+DATA = "synthetic (seeded numpy default_rng, BASELINE distributions)"
 
 
 # ----------------------------------------------------------------- main --
@@ -719,38 +1307,46 @@ def exact_norm(x: np.ndarray) -> float:
     return float(np.sqrt(total) * np.longdouble(2.0) ** e)
 
 
-def parity_check(check):
-    from oracle import numpy_backend, tolerance
-
-    kind = check[0]
-    if kind == "gemv_dot":
-        _, A, x, u, v, y, d = check
-        bad = tolerance.gemm_violations(y, numpy_backend.matmul(A, x), A, x)
-        bad += tolerance.gemm_violations(d.reshape(()), numpy_backend.dot(u, v), u, v)
-        return bad
-    if kind == "gemm":
-        _, A, B, Cm = check
-        rows = np.random.default_rng(0).choice(A.shape[-2], size=min(64, A.shape[-2]), replace=False)
-        a = A[..., rows, :]
-        return tolerance.gemm_violations(Cm[..., rows, :], numpy_backend.matmul(a, B), a, B)
-    if kind == "elementwise":
-        _, x, y, z = check
-        return int(np.sum(numpy_backend.elementwise("add", (x, y), np.float32).view(np.uint32)
-                          != z.view(np.uint32)))
-    if kind == "reduce":
-        _, x, _, z = check
-        want = numpy_backend.reduce(x, (0,), False, np.float32)
-        bound = 4 * x.size * tolerance.unit_roundoff(np.float32) * float(np.sum(np.abs(x), dtype=np.float64))
-        return int(abs(float(z[0]) - float(want)) > bound)
-    if kind == "norm_rows":
-        _, x, out = check
-        sel = np.arange(0, x.shape[0], max(1, x.shape[0] // 256))
-        return tolerance.norm_violations(out[sel], numpy_backend.norm(x[sel], axis=1))
-    if kind == "norm":  # the full (possibly sharded) norm against the whole input
-        _, x, out = check
-        return tolerance.norm_violations(out.reshape(()), numpy_backend.norm(x),
-                                         exact=exact_norm(x))
-    return None
+def b200_arm(args, dist: Dist) -> int:
+    gpu = Gpu(dist.local)
+    comm = Comm(gpu, dist)
+    pk = peaks()
+    limiter, threads = blas_threads_all() if dist.rank == 0 else (None, 0)
+    records = {}
+    try:
+        for w in make_workloads(args, dist):
+            rec = measure(w, gpu, comm, args, dist, pk)
+            if dist.world == 1 and dist.rank == 0 and not args.no_cpu_baseline:
+                budget = 15.0 if not records else 3.0
+                value, steps, what, _ = cpu_time(w, budget, max_steps=200)
+                rec["cpu_baseline"] = {"value": value, "unit": w.unit, "cores": threads, "kind": "port",
+                                       "sample": f"{steps} steps of {what}; OpenBLAS threads {threads} "
+                                                 f"of {cpu_cores()} host cores"}
+            records[w.name] = rec
+            del w
+            gpu.backend.release_cached_memory()
+    finally:
+        comm.close()
+    if dist.rank != 0:
+        return 0
+    names = list(records)
+    head = records.pop(names[0])
+    line = {
+        "metric": head.pop("metric"), "value": head.pop("value"), "unit": head.pop("unit"),
+        "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": head.pop("ms_per_step"), "higher_is_better": True,
+        "scaling": head.pop("scaling"), "vs_baseline": None, "dtype": head.pop("dtype"),
+        "data": DATA, "config": head.pop("config"),
+    }
+    line.update(head)
+    if records:
+        line["configs"] = records
+        line["parity_violations_all"] = int(line["parity_violations"] + sum(
+            r["parity_violations"] for r in records.values()))
+        line["gpu_launches_all"] = int(line["gpu_launches"] + sum(r["gpu_launches"] for r in records.values()))
+    print(json.dumps(line))
+    del limiter
+    return 0
 
 
 def main(argv=None):
@@ -759,68 +1355,23 @@ def main(argv=None):
     parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    parser.add_argument("--workload", default="gemv_dot",
-                        choices=("gemv_dot", "gemm1024", "batched", "norm", "norm_rows", "gemm_f32",
-                                 "gemm_f64", "vecmat", "elementwise", "reduce"))
+    parser.add_argument("--workload", default="suite",
+                        choices=("suite", "batched", "gemm1024", "gemv_dot", "norm", "norm_rows", "gemm_f32",
+                                 "gemm_f64", "vecmat", "elementwise", "reduce", "residual"))
     parser.add_argument("--dtype", choices=("f32", "f64"), default="f32", help="norm workloads")
     parser.add_argument("--n", type=int, default=0,
-                        help="GEMM size override (profiling captures); 0 = the BASELINE size")
+                        help="GEMM / vecmat / around-path size override (profiling captures); 0 = BASELINE")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args(argv)
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
+    if args.steps < 1:
+        parser.error("--steps must be >= 1")
     dist = Dist()
     try:
         if args.impl == "reference":
             return reference_arm(args, dist)
-        gpu = Gpu(dist.local)
-        result: dict = {}
-        if args.workload == "gemv_dot":
-            run_gemv_dot(gpu, args, dist, result)
-        elif args.workload in ("gemm1024", "gemm_f32", "gemm_f64"):
-            run_gemm(gpu, args, dist, result, args.workload)
-        elif args.workload == "batched":
-            run_batched(gpu, args, dist, result)
-        elif args.workload == "vecmat":
-            run_vecmat(gpu, args, dist, result)
-        elif args.workload in ("elementwise", "reduce"):
-            run_around(gpu, args, dist, result, args.workload)
-        else:
-            run_norm(gpu, args, dist, result, rows=args.workload == "norm_rows")
-        check = result.pop("_check")
-        name, work, sec = result.pop("roofline_kernel")
-        pk = peaks()
-        bad = parity_check(check) if dist.rank == 0 else None
-        if dist.rank != 0:
-            return 0
-        if result["unit"] == "GB/s" or name in ("gemv", "norm", "skinny", "elementwise", "reduce"):
-            achieved = work / sec / 1e9
-            roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                    "frac": achieved / pk["hbm_gbs"], "kernel": name, "peak_source": pk["source"],
-                    "traffic": traffic_per_launch(name, args.workload),
-                    "algorithmic_bytes": work}
-        else:
-            achieved = work / sec / 1e12
-            ceiling = TENSOR_CEILINGS.get(args.workload)
-            roof = {"bound": "tensor", "achieved": achieved,
-                    "peak": ceiling[0] if ceiling else None, "unit": "TFLOP/s",
-                    "frac": achieved / ceiling[0] if ceiling else None, "kernel": name,
-                    "peak_source": ceiling[1] if ceiling else None,
-                    "traffic": traffic_per_launch(name, args.workload)}
-        line = {
-            "metric": result.pop("metric"), "value": result.pop("value"), "unit": result.pop("unit"),
-            "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": result.pop("ms_per_step"), "higher_is_better": True,
-            "scaling": result.pop("scaling"), "vs_baseline": None, "dtype": result.pop("dtype"),
-            "data": "synthetic (seeded numpy default_rng, BASELINE distributions)",
-            "config": result.pop("config"), "roofline": roof,
-        }
-        line.update(result)
-        line["parity_violations"] = bad
-        if args.workload == "gemv_dot" and dist.world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_gemv_dot(10.0)
-        print(json.dumps(line))
-        return 0
+        return b200_arm(args, dist)
     finally:
         dist.close()
 

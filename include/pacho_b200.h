@@ -117,6 +117,24 @@ int pb_timer_stop(pb_ctx* ctx, int dev, float* ms);
 /* Number of kernels this library launched on `dev` since pb_init.  No
  * counterpart in the reference. */
 int pb_launch_count(pb_ctx* ctx, int dev, uint64_t* count);
+/* Per-kernel timer for rooflines: while enabled, every entry point brackets
+ * its main kernel (the GEMM tile kernel, the GEMV/DOT/norm/elementwise/
+ * reduction kernel -- not the operand-split or partial-merge helpers) with
+ * CUDA events on the device stream.  pb_ktimer_read waits for the stream,
+ * returns the summed milliseconds and the number of bracketed launches since
+ * the last enable/read, and starts a new count.  At most 4096 launches are
+ * kept between reads (PB_ERR_UNSUPPORTED beyond).  An event between two
+ * chained launches serialises them, so time the whole step with the timer off.
+ * No counterpart in the reference. */
+int pb_ktimer_enable(pb_ctx* ctx, int dev, int enable);
+int pb_ktimer_read(pb_ctx* ctx, int dev, double* total_ms, uint64_t* launches);
+/* Device memory in use by this context on `dev`: bytes the stream-ordered
+ * pool holds reserved from the driver and in use, the size of the context's
+ * grow-only scratch buffer, and the device's free memory (cudaMemGetInfo).
+ * Memory statistics of the kind the reference's pool keeps in Python
+ * (src/openpacho/_cuda.py:232-274). */
+int pb_memory_stats(pb_ctx* ctx, int dev, size_t* pool_reserved, size_t* pool_used,
+                    size_t* scratch_bytes, size_t* device_free);
 
 /* ---- hot path ---------------------------------------------------------- */
 
@@ -163,6 +181,17 @@ int pb_gemm_ex(pb_ctx* ctx, int dev, int dtype, int batch_ndim, const int64_t* b
 int pb_gemv(pb_ctx* ctx, int dev, int dtype, int64_t rows, int64_t K, const void* A,
             const void* x, void* y);
 
+/* out[r] = b[r] - (A @ x)[r] for r < rows: the GEMV with the compiled plan's
+ * residual subtraction in its epilogue, so the product never goes to HBM.
+ * The product is rounded to the dtype before the subtraction, as in the
+ * eager b - A @ x; results are bit-identical to pb_gemv followed by an
+ * elementwise subtract.  K == 0 copies b.  `out` may alias `b`.  Replaces
+ * residual_matvec_data (src/openpacho/_gemv.py:10-60), which the compiled
+ * plans reach through the lowering hook (src/openpacho/_compiler.py:157-176,
+ * 306-307). */
+int pb_gemv_residual(pb_ctx* ctx, int dev, int dtype, int64_t rows, int64_t K, const void* A,
+                     const void* x, const void* b, void* out);
+
 /* *out = sum_i x[i] * y[i] written to device memory.  Replaces the long-DOT
  * chunked path (src/openpacho/_cuda_gemv.py:67-84) and cuBLAS ?dot in
  * device-pointer mode (src/openpacho/_cuda_blas.py:18-30). */
@@ -178,9 +207,12 @@ int pb_dot(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, const void
  * 33 KiB device array inside the library (room for 4096 partials; a DOT uses
  * at most 16 per SM, 2368 on a B200), which every GPU that loads the library
  * keeps until the process exits; a plan needing more is rejected with
- * PB_ERR_UNSUPPORTED.  The first call on each device looks the array's
- * address up with that device current -- make that first call before any
- * stream capture.  All calls share the one array: calls ordered on one
+ * PB_ERR_UNSUPPORTED.  pb_init looks the array's device address up for each
+ * device of the context, with that device current, and loads the DOT
+ * kernels there, so no pb_dot_noalloc call loads code or data onto the
+ * device (with lazy module loading, that load could allocate).  The call
+ * zeroes the array's arrival counter (a stream-ordered memset of existing
+ * memory) before the kernel.  All calls share the one array: calls ordered on one
  * context's stream are safe, calls that overlap on the GPU (other streams or
  * contexts on the same device) race.  No counterpart in the reference. */
 int pb_dot_noalloc(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, const void* y,
@@ -300,6 +332,13 @@ int pb_norm_sharded(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, v
 int pb_peer_export(pb_ctx* ctx, int dev, int nranks, int rank, unsigned char handle[64]);
 int pb_peer_import(pb_ctx* ctx, int dev, int nranks, const unsigned char* handles);
 int pb_peer_close(pb_ctx* ctx, int dev);
+/* Limit, in nanoseconds, of each wait of the mailbox merge kernels for a
+ * peer's partial (default 10 s; 0 restores it).  A wait that runs out sets the
+ * kernel error word and the kernel returns, so the next pb_sync reports
+ * PB_ERR_DEVICE and the context stays usable; the group's sequence numbers
+ * are then out of step and the mailboxes must be closed and set up again.
+ * No counterpart in the reference (single-device). */
+int pb_peer_set_wait(pb_ctx* ctx, int dev, uint64_t limit_ns);
 /* *out = sum over ranks of the DOT of each rank's (x, y) slice (peer
  * mailboxes required), the same value on every rank. */
 int pb_dot_sharded(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, const void* y,

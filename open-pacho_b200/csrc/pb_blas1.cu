@@ -120,7 +120,8 @@ template <typename T, bool ALIGNED, bool STREAM_X>
 __global__ void __launch_bounds__(kThreads)
     gemv_kernel(const T* __restrict__ A, const T* __restrict__ x, T* __restrict__ y,
                 int64_t rows, int64_t K, int64_t lda, int rows_per_block, int64_t chunk,
-                int nchunks, T* __restrict__ partial, unsigned int* __restrict__ counters) {
+                int nchunks, T* __restrict__ partial, unsigned int* __restrict__ counters,
+                const T* __restrict__ resid) {
   __shared__ T red[kWarps];
   __shared__ bool last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -145,7 +146,7 @@ __global__ void __launch_bounds__(kThreads)
       if (r < rows) {
         T s = T(0);
         for (int w = 0; w < G; ++w) s += red[threadIdx.x * G + w];
-        y[r] = s;
+        y[r] = resid ? resid[r] - s : s;
       }
     }
     return;
@@ -171,7 +172,7 @@ __global__ void __launch_bounds__(kThreads)
   if (threadIdx.x == 0) {
     T t = T(0);
     for (int w = 0; w < kWarps; ++w) t += red[w];
-    y[row] = t;
+    y[row] = resid ? resid[row] - t : t;
     counters[row] = 0u;  // leave the counter ready for the next launch
   }
 }
@@ -183,7 +184,7 @@ __global__ void __launch_bounds__(kThreads)
 template <typename T, bool ALIGNED>
 __global__ void __launch_bounds__(kThreads, 4)
     gemv_rows_kernel(const T* __restrict__ A, const T* __restrict__ x, T* __restrict__ y,
-                     int64_t rows, int K, int rows_per_block) {
+                     int64_t rows, int K, int rows_per_block, const T* __restrict__ resid) {
   using V = typename V16<T>::type;
   constexpr int VN = V16<T>::n;
   __shared__ T red[kWarps];
@@ -230,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 4)
       if (r < rows) {
         T s = T(0);
         for (int w = 0; w < G; ++w) s += red[threadIdx.x * G + w];
-        y[r] = s;
+        y[r] = resid ? resid[r] - s : s;
       }
     }
     __syncthreads();
@@ -284,8 +285,12 @@ int64_t rows_grid(const GemvPlan& p, int64_t resident) {
   return p.blocks < cap ? p.blocks : cap;
 }
 
+// resid: nullptr for y = A x; else the residual epilogue y = resid - A x, with
+// A x rounded to T before the subtraction (one rounding each, as the eager
+// product followed by an elementwise subtract).
 template <typename T, bool STREAM_X>
-int launch_gemv(Device* d, const T* A, const T* x, T* y, int64_t rows, int64_t K, int64_t lda) {
+int launch_gemv(Device* d, const T* A, const T* x, T* y, int64_t rows, int64_t K, int64_t lda,
+                const T* resid = nullptr) {
   GemvPlan p = plan_gemv(rows, K, sizeof(T),
                          resident_blocks(d, (const void*)gemv_kernel<T, true, STREAM_X>, kThreads));
   if (p.blocks > INT32_MAX) PB_FAIL(PB_ERR_UNSUPPORTED, "GEMV grid too large");
@@ -303,23 +308,25 @@ int launch_gemv(Device* d, const T* A, const T* x, T* y, int64_t rows, int64_t K
   if (p.nchunks == 1 && !STREAM_X && lda == K && K < INT32_MAX) {
     const unsigned grid =
         (unsigned)rows_grid(p, resident_blocks(d, (const void*)gemv_rows_kernel<T, true>, kThreads));
+    PB_CHECK(kt_begin(d));
     if (aligned)
       gemv_rows_kernel<T, true><<<grid, kThreads, 0, d->stream>>>(A, x, y, rows, (int)K,
-                                                                   p.rows_per_block);
+                                                                   p.rows_per_block, resid);
     else
       gemv_rows_kernel<T, false><<<grid, kThreads, 0, d->stream>>>(A, x, y, rows, (int)K,
-                                                                    p.rows_per_block);
+                                                                    p.rows_per_block, resid);
     PB_LAUNCHED(d);
-    return PB_OK;
+    return kt_end(d);
   }
+  PB_CHECK(kt_begin(d));
   if (aligned)
     gemv_kernel<T, true, STREAM_X><<<(unsigned)p.blocks, kThreads, 0, d->stream>>>(
-        A, x, y, rows, K, lda, p.rows_per_block, p.chunk, p.nchunks, partial, cnt);
+        A, x, y, rows, K, lda, p.rows_per_block, p.chunk, p.nchunks, partial, cnt, resid);
   else
     gemv_kernel<T, false, STREAM_X><<<(unsigned)p.blocks, kThreads, 0, d->stream>>>(
-        A, x, y, rows, K, lda, p.rows_per_block, p.chunk, p.nchunks, partial, cnt);
+        A, x, y, rows, K, lda, p.rows_per_block, p.chunk, p.nchunks, partial, cnt, resid);
   PB_LAUNCHED(d);
-  return PB_OK;
+  return kt_end(d);
 }
 
 // ---- DOT for callers that cannot allocate ------------------------------
@@ -333,27 +340,20 @@ constexpr size_t kStaticDotCounterOffset = kStaticDotPartials * sizeof(double);
 static __device__ __align__(256) unsigned char g_dot_scratch[kStaticDotCounterOffset + 256];
 
 // In host code `g_dot_scratch` is only a host-side stand-in for the device
-// array; its device address is looked up once per device, with that device
-// current, and cached here by CUDA ordinal.
-constexpr int kMaxOrdinals = 64;
-std::mutex g_dot_scratch_mu;
-void* g_dot_scratch_addr[kMaxOrdinals] = {};
-
-int dot_scratch_address(Device* d, void** out) {
-  if (d->ordinal < 0 || d->ordinal >= kMaxOrdinals)
-    PB_FAIL(PB_ERR_UNSUPPORTED, "pb_dot_noalloc supports CUDA ordinals below %d", kMaxOrdinals);
-  std::lock_guard<std::mutex> g(g_dot_scratch_mu);
-  if (!g_dot_scratch_addr[d->ordinal]) {
-    void* ptr = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&ptr, g_dot_scratch);
-    if (e != cudaSuccess || !ptr)
-      PB_FAIL(PB_ERR_CUDA, "cudaGetSymbolAddress(static DOT scratch) failed: %s",
-              cudaGetErrorString(e));
-    g_dot_scratch_addr[d->ordinal] = ptr;
-  }
-  *out = g_dot_scratch_addr[d->ordinal];
+// array.  pb_init calls dot_static_prepare with each device current: it looks
+// the array's device address up for that device (kept in the context) and
+// loads the DOT kernels and their occupancy figures, so that with lazy module
+// loading no pb_dot_noalloc call is the one that loads code or data onto the
+// device.
+template <typename T>
+static int prepare_dot_kernels(Device* d) {
+  cudaFuncAttributes attr;
+  PB_CUDA(cudaFuncGetAttributes(&attr, gemv_kernel<T, true, true>));
+  PB_CUDA(cudaFuncGetAttributes(&attr, gemv_kernel<T, false, true>));
+  resident_blocks(d, (const void*)gemv_kernel<T, true, true>, kThreads);
   return PB_OK;
 }
+
 
 template <typename T>
 int launch_dot_static(Device* d, const T* x, const T* y, T* out, int64_t n) {
@@ -366,8 +366,8 @@ int launch_dot_static(Device* d, const T* x, const T* y, T* out, int64_t n) {
   T* partial = nullptr;
   unsigned int* cnt = nullptr;
   if (p.nchunks > 1) {
-    void* base;
-    PB_CHECK(dot_scratch_address(d, &base));
+    void* base = d->dot_static;
+    if (!base) PB_FAIL(PB_ERR_UNAVAILABLE, "static DOT scratch not resolved for this device");
     partial = (T*)base;
     cnt = (unsigned int*)((char*)base + kStaticDotCounterOffset);
     // The array keeps whatever the previous call left; the arrival counter must
@@ -379,10 +379,10 @@ int launch_dot_static(Device* d, const T* x, const T* y, T* out, int64_t n) {
       ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && (p.chunk % VN == 0);
   if (aligned)
     gemv_kernel<T, true, true><<<(unsigned)p.blocks, kThreads, 0, d->stream>>>(
-        x, y, out, 1, n, n, p.rows_per_block, p.chunk, p.nchunks, partial, cnt);
+        x, y, out, 1, n, n, p.rows_per_block, p.chunk, p.nchunks, partial, cnt, nullptr);
   else
     gemv_kernel<T, false, true><<<(unsigned)p.blocks, kThreads, 0, d->stream>>>(
-        x, y, out, 1, n, n, p.rows_per_block, p.chunk, p.nchunks, partial, cnt);
+        x, y, out, 1, n, n, p.rows_per_block, p.chunk, p.nchunks, partial, cnt, nullptr);
   PB_LAUNCHED(d);
   return PB_OK;
 }
@@ -399,6 +399,18 @@ int launch_fill(Device* d, T* out, size_t n, T value) {
 }
 
 }  // namespace
+
+int dot_static_prepare(Device* d) {
+  void* ptr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&ptr, g_dot_scratch);
+  if (e != cudaSuccess || !ptr)
+    PB_FAIL(PB_ERR_CUDA, "cudaGetSymbolAddress(static DOT scratch) failed: %s",
+            cudaGetErrorString(e));
+  d->dot_static = ptr;
+  PB_CHECK(prepare_dot_kernels<float>(d));
+  PB_CHECK(prepare_dot_kernels<double>(d));
+  return PB_OK;
+}
 
 // DOT into device memory (the local partial of the sharded DOT).
 int dot_device(Device* d, int dtype, int64_t n, const void* x, const void* y, void* out) {
@@ -450,6 +462,30 @@ int pb_gemv(pb_ctx* ctx, int dev, int dtype, int64_t rows, int64_t K, const void
     return launch_gemv<double, false>(d, (const double*)A, (const double*)x, (double*)y, rows, K,
                                       K);
   PB_FAIL(PB_ERR_INVALID, "unknown dtype %d", dtype);
+}
+
+int pb_gemv_residual(pb_ctx* ctx, int dev, int dtype, int64_t rows, int64_t K, const void* A,
+                     const void* x, const void* b, void* out) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  if (rows < 0 || K < 0) PB_FAIL(PB_ERR_INVALID, "negative GEMV extent");
+  if (!rows) return PB_OK;
+  if (!out || !b) PB_FAIL(PB_ERR_INVALID, "null residual operand or output");
+  if (dtype != PB_F32 && dtype != PB_F64) PB_FAIL(PB_ERR_INVALID, "unknown dtype %d", dtype);
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  const size_t bytes = (size_t)rows * (dtype == PB_F32 ? 4 : 8);
+  // K == 0: A x is zero, so the result is b - 0 = b (the reference casts b).
+  if (!K) {
+    if (out != b) PB_CUDA(cudaMemcpyAsync(out, b, bytes, cudaMemcpyDeviceToDevice, d->stream));
+    return PB_OK;
+  }
+  if (!A || !x) PB_FAIL(PB_ERR_INVALID, "null input");
+  if (dtype == PB_F32)
+    return launch_gemv<float, false>(d, (const float*)A, (const float*)x, (float*)out, rows, K, K,
+                                     (const float*)b);
+  return launch_gemv<double, false>(d, (const double*)A, (const double*)x, (double*)out, rows, K,
+                                    K, (const double*)b);
 }
 
 int pb_dot(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, const void* y, void* out) {

@@ -488,6 +488,7 @@ int pb_elementwise(pb_ctx* ctx, int dev, int op, int nargs, const void* const* a
   PB_CHECK(enter(ctx, dev, &d));
   bool dense = ((uintptr_t)out & 15) == 0;
   for (int j = 0; j < nargs; ++j) dense &= p.kind[j] != 0 && ((uintptr_t)p.arg[j] & 15) == 0;
+  PB_CHECK(kt_begin(d));
   if (dense) {
     bool f32 = kDenseF32[op] != nullptr && (out_dtype == PB_F32 || out_dtype == PB_BOOL);
     for (int j = 0; j < nargs; ++j) f32 &= p.dtype[j] == PB_F32;
@@ -500,7 +501,7 @@ int pb_elementwise(pb_ctx* ctx, int dev, int op, int nargs, const void* const* a
     elementwise_kernel<<<(unsigned)grid_for(d, p.count), kThreads, 0, d->stream>>>(p);
   }
   PB_LAUNCHED(d);
-  return PB_OK;
+  return kt_end(d);
 }
 
 int pb_gather(pb_ctx* ctx, int dev, int dtype, const void* src, int ndim, const int64_t* shape,
@@ -589,9 +590,10 @@ int pb_reduce(pb_ctx* ctx, int dev, int op, int in_dtype, const void* src, int n
   if (!src) PB_FAIL(PB_ERR_INVALID, "null input");
   if (p.reduced < 256 && p.count >= (int64_t)d->sm_count * kThreads) {
     p.chunks = 1;
+    PB_CHECK(kt_begin(d));
     reduce_threads_kernel<<<(unsigned)grid_for(d, p.count), kThreads, 0, d->stream>>>(p, 0);
     PB_LAUNCHED(d);
-    return PB_OK;
+    return kt_end(d);
   }
   // One wave of blocks, at least 4096 reduced indices each.
   int64_t chunks = wave(d, reduce_blocks_kernel) / p.count;
@@ -606,8 +608,10 @@ int pb_reduce(pb_ctx* ctx, int dev, int op, int in_dtype, const void* src, int n
     PB_CHECK(scratch(d, (size_t)p.count * p.chunks * sizeof(double), &ws));
     p.partial = static_cast<double*>(ws);
   }
+  PB_CHECK(kt_begin(d));
   reduce_blocks_kernel<<<(unsigned)(p.count * p.chunks), kThreads, 0, d->stream>>>(p);
   PB_LAUNCHED(d);
+  PB_CHECK(kt_end(d));
   if (p.chunks > 1) {
     reduce_threads_kernel<<<(unsigned)grid_for(d, p.count), kThreads, 0, d->stream>>>(p, 1);
     PB_LAUNCHED(d);

@@ -248,9 +248,10 @@ int gemm_dmma_f64(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
   const bool vec = K % 2 == 0 && N % 2 == 0 && ((uintptr_t)A & 15) == 0 && ((uintptr_t)B & 15) == 0;
   auto kernel = vec ? dmma_gemm_kernel<true> : dmma_gemm_kernel<false>;
   PB_CHECK(allow_smem(d, (const void*)kernel, smem));
+  PB_CHECK(kt_begin(d));
   kernel<<<dim3((unsigned)gx, (unsigned)gy, gz), NT, smem, d->stream>>>(p);
   PB_LAUNCHED(d);
-  return PB_OK;
+  return kt_end(d);
 }
 
 }  // namespace pb

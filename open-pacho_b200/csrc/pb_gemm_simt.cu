@@ -164,9 +164,10 @@ int launch_simt(Device* d, const BatchMap& map, int64_t batch, int64_t M, int64_
   const unsigned gz = (unsigned)(batch < 65535 ? batch : 65535);
   const size_t smem = 2 * BK * (BM + BN) * sizeof(T);
   PB_CHECK(allow_smem(d, (const void*)simt_gemm_kernel<T>, smem));
+  PB_CHECK(kt_begin(d));
   simt_gemm_kernel<T><<<dim3((unsigned)gx, (unsigned)gy, gz), NT, smem, d->stream>>>(p);
   PB_LAUNCHED(d);
-  return PB_OK;
+  return kt_end(d);
 }
 
 }  // namespace

@@ -1193,8 +1193,10 @@ int launch_tf32(Device* d, const CUtensorMap& ma, const CUtensorMap& mb, const T
   // Persistent: one CTA per SM (shared memory allows no more), work items strided.
   const int64_t items = p.tiles * p.ksplit;
   const int64_t grid = items < d->sm_count ? items : d->sm_count;
-  return launch_dependent(d, tf32x3_gemm_kernel<BN>, dim3((unsigned)grid), dim3(GEMM_THREADS),
-                          (size_t)smem, ma, mb, p);
+  PB_CHECK(kt_begin(d));
+  PB_CHECK(launch_dependent(d, tf32x3_gemm_kernel<BN>, dim3((unsigned)grid), dim3(GEMM_THREADS),
+                            (size_t)smem, ma, mb, p));
+  return kt_end(d);
 }
 
 // Operands and non-finite handling of a launch (after p.ksplit is set); the
@@ -1241,8 +1243,10 @@ int launch_tmem(Device* d, const CUtensorMap& ma, const CUtensorMap& mb, const C
   PB_CHECK(allow_smem(d, (const void*)tf32x3_tmem_kernel<FBN>, smem));
   const int64_t items = p.tiles * p.ksplit;
   const int64_t grid = items < d->sm_count ? items : d->sm_count;
-  return launch_dependent(d, tf32x3_tmem_kernel<FBN>, dim3((unsigned)grid), dim3(T_THREADS),
-                          (size_t)smem, ma, mb, mc, p, (int)Kp);
+  PB_CHECK(kt_begin(d));
+  PB_CHECK(launch_dependent(d, tf32x3_tmem_kernel<FBN>, dim3((unsigned)grid), dim3(T_THREADS),
+                            (size_t)smem, ma, mb, mc, p, (int)Kp));
+  return kt_end(d);
 }
 
 }  // namespace

@@ -11,6 +11,7 @@
 #include <set>
 #include <utility>
 #include <string>
+#include <vector>
 
 #include "../../include/pacho_b200.h"
 
@@ -87,6 +88,13 @@ struct Device {
   int* err_dev = nullptr;
   cudaEvent_t t0 = nullptr, t1 = nullptr;
   std::atomic<uint64_t> launches{0};
+  // Per-kernel timer (pb_ktimer_*): event pairs around main kernels while on.
+  int kt_on = 0;
+  size_t kt_used = 0;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> kt_events;
+  // Device address of the fixed DOT scratch of pb_dot_noalloc, looked up when
+  // the context is created (with the device current).
+  void* dot_static = nullptr;
   // NCCL communicator (ncclComm_t) when joined.
   void* comm = nullptr;
   int nranks = 1, rank = 0;
@@ -96,6 +104,7 @@ struct Device {
   struct MailSlot* box[8] = {};
   int box_ranks = 0, box_rank = 0;
   unsigned long long box_seq = 0;
+  unsigned long long box_wait_ns = 10ull * 1000 * 1000 * 1000;  // mailbox wait limit
 };
 
 }  // namespace pb
@@ -145,6 +154,13 @@ inline int64_t resident_blocks(Device* d, const void* kernel, int threads) {
   known[key] = n;
   return n;
 }
+// Per-kernel timer: bracket the main kernel of an entry point (no-ops while
+// the timer is off).  kt_begin records the start event, kt_end the end event.
+int kt_begin(Device* d);
+int kt_end(Device* d);
+// Resolve the fixed DOT scratch of pb_dot_noalloc on d's device and load the
+// kernels it launches (pb_blas1.cu); called by pb_init with the device current.
+int dot_static_prepare(Device* d);
 // Fill `count` elements of dtype PB_F32 / PB_F64 / PB_BOOL with `value`.
 int fill_device(Device* d, int dtype, void* dst, size_t count, double value);
 // Ensure at least `n` operand tag words; returns them and a fresh generation.
@@ -186,17 +202,19 @@ struct PushArgs {
 };
 
 // Wait (one thread) until `slot` carries sequence number `seq`; false, with
-// the kernel error flag set, after kMailboxWaitNs.  The acquire load orders
-// the payload reads after it.
+// the kernel error flag set, after `limit_ns` (the context's limit, 10 s
+// unless pb_peer_set_wait changed it).  The acquire load orders the payload
+// reads after it.
 constexpr unsigned long long kMailboxWaitNs = 10ull * 1000 * 1000 * 1000;
-__device__ __forceinline__ bool mailbox_wait(const MailSlot* slot, unsigned long long seq, int* err) {
+__device__ __forceinline__ bool mailbox_wait(const MailSlot* slot, unsigned long long seq, int* err,
+                                             unsigned long long limit_ns) {
   unsigned long long t0, t, v;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
   for (;;) {
     asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(&slot->seq) : "memory");
     if (v == seq) return true;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    if (t - t0 > kMailboxWaitNs) {
+    if (t - t0 > limit_ns) {
       atomicExch(err, KERR_WAIT_TIMEOUT);
       return false;
     }

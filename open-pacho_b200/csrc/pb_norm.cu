@@ -489,6 +489,7 @@ int launch_rows(Device* d, const T* x, T* out, NormPair* pair_out, int64_t rows,
   }
   constexpr int VN = 16 / sizeof(T);
   bool aligned = ((uintptr_t)x % 16 == 0) && (rows == 1 || K % VN == 0) && (p.chunk % VN == 0);
+  PB_CHECK(kt_begin(d));
   if (aligned)
     norm_rows_kernel<T, true, PAIR_OUT><<<(unsigned)p.blocks, kThreads, 0, d->stream>>>(
         x, out, pair_out, rows, K, p.rows_per_block, p.chunk, p.nchunks, partial, cnt, push);
@@ -496,7 +497,7 @@ int launch_rows(Device* d, const T* x, T* out, NormPair* pair_out, int64_t rows,
     norm_rows_kernel<T, false, PAIR_OUT><<<(unsigned)p.blocks, kThreads, 0, d->stream>>>(
         x, out, pair_out, rows, K, p.rows_per_block, p.chunk, p.nchunks, partial, cnt, push);
   PB_LAUNCHED(d);
-  return PB_OK;
+  return kt_end(d);
 }
 
 template <typename T>
@@ -522,10 +523,11 @@ int launch_cols(Device* d, const T* x, T* out, int64_t outer, int64_t R, int64_t
     partial = (NormPair*)s;
     PB_CHECK(counters(d, (size_t)tiles, &cnt));
   }
+  PB_CHECK(kt_begin(d));
   norm_cols_kernel<T><<<(unsigned)(tiles * nchunks), kThreads, 0, d->stream>>>(
       x, out, outer, R, inner, itiles, chunk, nchunks, partial, cnt);
   PB_LAUNCHED(d);
-  return PB_OK;
+  return kt_end(d);
 }
 
 }  // namespace
@@ -542,16 +544,17 @@ int norm_pair_global(Device* d, int dtype, int64_t n, const void* x, void* pair_
 }
 
 // Merge the pairs of every rank from this rank's mailbox, in rank order, and
-// write the norm: one thread, each wait bounded (kMailboxWaitNs) with the
-// kernel error flag set when it runs out.
+// write the norm: one thread, each wait bounded (the context's limit, 10 s by
+// default) with the kernel error flag set when it runs out.
 template <typename T>
 __global__ void mailbox_norm_kernel(const MailSlot* box, int nranks, int parity,
-                                    unsigned long long seq, T* out, int* err) {
+                                    unsigned long long seq, T* out, int* err,
+                                    unsigned long long wait_ns) {
   if (threadIdx.x != 0) return;
   NormPair s;
   for (int r = 0; r < nranks; ++r) {
     const MailSlot* slot = box + r * 2 + parity;
-    if (!mailbox_wait(slot, seq, err)) return;
+    if (!mailbox_wait(slot, seq, err, wait_ns)) return;
     NormPair q;
     q.ssq = *(volatile const double*)&slot->a;
     q.e = *(volatile const int*)&slot->e;
@@ -576,10 +579,10 @@ int norm_push_empty(Device* d, int dtype, const PushArgs& a) {
 int mailbox_norm(Device* d, int dtype, int parity, unsigned long long seq, void* out) {
   if (dtype == PB_F32)
     mailbox_norm_kernel<float><<<1, 32, 0, d->stream>>>(d->box[d->box_rank], d->box_ranks, parity,
-                                                        seq, (float*)out, d->err_dev);
+                                                        seq, (float*)out, d->err_dev, d->box_wait_ns);
   else
     mailbox_norm_kernel<double><<<1, 32, 0, d->stream>>>(d->box[d->box_rank], d->box_ranks, parity,
-                                                         seq, (double*)out, d->err_dev);
+                                                         seq, (double*)out, d->err_dev, d->box_wait_ns);
   PB_LAUNCHED(d);
   return PB_OK;
 }
@@ -663,6 +666,7 @@ int pb_norm_strided(pb_ctx* ctx, int dev, int dtype, int out_ndim, const int64_t
   PB_CHECK(enter(ctx, dev, &d));
   if (!R) return fill_device(d, dtype, out, (size_t)count, 0.0);
   if (!x) PB_FAIL(PB_ERR_INVALID, "null input");
+  PB_CHECK(kt_begin(d));
   if (dtype == PB_F32)
     norm_strided_kernel<float><<<(unsigned)count, kThreads, 0, d->stream>>>((const float*)x,
                                                                             (float*)out, s, R);
@@ -670,7 +674,7 @@ int pb_norm_strided(pb_ctx* ctx, int dev, int dtype, int out_ndim, const int64_t
     norm_strided_kernel<double><<<(unsigned)count, kThreads, 0, d->stream>>>(
         (const double*)x, (double*)out, s, R);
   PB_LAUNCHED(d);
-  return PB_OK;
+  return kt_end(d);
 }
 
 }  // extern "C"

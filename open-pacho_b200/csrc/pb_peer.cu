@@ -11,7 +11,7 @@
 // Every later exchange is: push (payload, system fence, release store of the
 // call's sequence number into slot [rank][seq % 2] of every mailbox), then one
 // thread per rank waits for all sequence numbers (acquire loads, bounded at
-// kMailboxWaitNs, error flag on timeout) and merges in rank order, so every
+// the context's wait limit, 10 s unless pb_peer_set_wait changed it; error flag on timeout) and merges in rank order, so every
 // rank computes identical bits.
 #include <string.h>
 
@@ -45,12 +45,13 @@ __global__ void push_value_kernel(const T* v, const PushArgs a) {
 // Sum of every rank's partial, in rank order.
 template <typename T>
 __global__ void mailbox_sum_kernel(const MailSlot* box, int nranks, int parity,
-                                   unsigned long long seq, T* out, int* err) {
+                                   unsigned long long seq, T* out, int* err,
+                                   unsigned long long wait_ns) {
   if (threadIdx.x != 0) return;
   double s = 0.0;
   for (int r = 0; r < nranks; ++r) {
     const MailSlot* slot = box + r * 2 + parity;
-    if (!mailbox_wait(slot, seq, err)) return;
+    if (!mailbox_wait(slot, seq, err, wait_ns)) return;
     s += *(volatile const double*)&slot->a;
   }
   *out = (T)s;
@@ -142,6 +143,15 @@ int pb_peer_close(pb_ctx* ctx, int dev) {
   return close_boxes(d);
 }
 
+int pb_peer_set_wait(pb_ctx* ctx, int dev, uint64_t limit_ns) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  d->box_wait_ns = limit_ns ? (unsigned long long)limit_ns : kMailboxWaitNs;
+  return PB_OK;
+}
+
 int pb_dot_sharded(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, const void* y,
                    void* out) {
   if (!ctx || !out) PB_FAIL(PB_ERR_INVALID, "null argument");
@@ -158,12 +168,13 @@ int pb_dot_sharded(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, co
     push_value_kernel<float><<<1, 32, 0, d->stream>>>((const float*)out, a);
     PB_LAUNCHED(d);
     mailbox_sum_kernel<float><<<1, 32, 0, d->stream>>>(d->box[d->box_rank], d->box_ranks, a.parity,
-                                                       seq, (float*)out, d->err_dev);
+                                                       seq, (float*)out, d->err_dev, d->box_wait_ns);
   } else {
     push_value_kernel<double><<<1, 32, 0, d->stream>>>((const double*)out, a);
     PB_LAUNCHED(d);
     mailbox_sum_kernel<double><<<1, 32, 0, d->stream>>>(d->box[d->box_rank], d->box_ranks,
-                                                        a.parity, seq, (double*)out, d->err_dev);
+                                                        a.parity, seq, (double*)out, d->err_dev,
+                                                        d->box_wait_ns);
   }
   PB_LAUNCHED(d);
   return PB_OK;

@@ -79,6 +79,33 @@ int operand_tags(Device* d, size_t n, unsigned int** out, unsigned int* gen) {
   return PB_OK;
 }
 
+constexpr size_t kMaxTimedLaunches = 4096;
+
+int kt_begin(Device* d) {
+  if (!d->kt_on) return PB_OK;
+  if (d->kt_used >= kMaxTimedLaunches)
+    PB_FAIL(PB_ERR_UNSUPPORTED, "kernel timer holds at most %zu launches between reads",
+            kMaxTimedLaunches);
+  if (d->kt_used == d->kt_events.size()) {
+    cudaEvent_t a, b;
+    PB_CUDA(cudaEventCreate(&a));
+    if (cudaEventCreate(&b) != cudaSuccess) {
+      cudaEventDestroy(a);
+      PB_FAIL(PB_ERR_CUDA, "cudaEventCreate failed");
+    }
+    d->kt_events.emplace_back(a, b);
+  }
+  PB_CUDA(cudaEventRecord(d->kt_events[d->kt_used].first, d->stream));
+  return PB_OK;
+}
+
+int kt_end(Device* d) {
+  if (!d->kt_on) return PB_OK;
+  PB_CUDA(cudaEventRecord(d->kt_events[d->kt_used].second, d->stream));
+  ++d->kt_used;
+  return PB_OK;
+}
+
 int tensor_map_encoder(void** fn) {
   static std::once_flag once;
   static void* encoder = nullptr;
@@ -106,6 +133,13 @@ static void release_device(Device* d) {
   if (d->stream) cudaStreamSynchronize(d->stream);
   if (d->t0) cudaEventDestroy(d->t0);
   if (d->t1) cudaEventDestroy(d->t1);
+  for (auto& ev : d->kt_events) {
+    cudaEventDestroy(ev.first);
+    cudaEventDestroy(ev.second);
+  }
+  d->kt_events.clear();
+  d->kt_used = 0;
+  d->dot_static = nullptr;
   if (d->err_host) cudaFreeHost(d->err_host);
   if (d->stream) cudaStreamDestroy(d->stream);
   if (d->pool) cudaMemPoolTrimTo(d->pool, 0);
@@ -240,6 +274,7 @@ int pb_init(int ndev, const int* ordinals, pb_ctx** out) {
       fail("cudaEventCreate", e);
       break;
     }
+    if ((status = dot_static_prepare(d)) != PB_OK) break;
   }
   if (status != PB_OK) {
     for (int i = 0; i < ndev; ++i) release_device(&ctx->devs[i]);
@@ -388,6 +423,52 @@ int pb_timer_stop(pb_ctx* ctx, int dev, float* ms) {
   PB_CUDA(cudaEventSynchronize(d->t1));
   PB_CUDA(cudaEventElapsedTime(ms, d->t0, d->t1));
   return check_kernel_error(d);
+}
+
+int pb_ktimer_enable(pb_ctx* ctx, int dev, int enable) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  d->kt_on = enable != 0;
+  d->kt_used = 0;
+  return PB_OK;
+}
+
+int pb_ktimer_read(pb_ctx* ctx, int dev, double* total_ms, uint64_t* launches) {
+  if (!ctx || !total_ms || !launches) PB_FAIL(PB_ERR_INVALID, "null argument");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  PB_CUDA(cudaStreamSynchronize(d->stream));
+  double total = 0.0;
+  for (size_t i = 0; i < d->kt_used; ++i) {
+    float ms = 0.0f;
+    PB_CUDA(cudaEventElapsedTime(&ms, d->kt_events[i].first, d->kt_events[i].second));
+    total += ms;
+  }
+  *total_ms = total;
+  *launches = d->kt_used;
+  d->kt_used = 0;
+  return check_kernel_error(d);
+}
+
+int pb_memory_stats(pb_ctx* ctx, int dev, size_t* pool_reserved, size_t* pool_used,
+                    size_t* scratch_bytes, size_t* device_free) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  uint64_t reserved = 0, used = 0;
+  PB_CUDA(cudaMemPoolGetAttribute(d->pool, cudaMemPoolAttrReservedMemCurrent, &reserved));
+  PB_CUDA(cudaMemPoolGetAttribute(d->pool, cudaMemPoolAttrUsedMemCurrent, &used));
+  size_t free_b = 0, total_b = 0;
+  PB_CUDA(cudaMemGetInfo(&free_b, &total_b));
+  if (pool_reserved) *pool_reserved = (size_t)reserved;
+  if (pool_used) *pool_used = (size_t)used;
+  if (scratch_bytes) *scratch_bytes = d->scratch_bytes;
+  if (device_free) *device_free = free_b;
+  return PB_OK;
 }
 
 int pb_launch_count(pb_ctx* ctx, int dev, uint64_t* count) {

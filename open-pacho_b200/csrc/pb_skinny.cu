@@ -171,9 +171,10 @@ int launch_rows(Device* d, SkinnyParams<T>& p, bool aligned) {
   auto kernel = aligned ? skinny_kernel<T, MR, true> : skinny_kernel<T, MR, false>;
   PB_CHECK(allow_smem(d, (const void*)kernel, smem));
   const unsigned gz = (unsigned)(p.batch < 65535 ? p.batch : 65535);
+  PB_CHECK(kt_begin(d));
   kernel<<<dim3((unsigned)p.strips, (unsigned)p.ksplit, gz), kThreads, smem, d->stream>>>(p);
   PB_LAUNCHED(d);
-  return PB_OK;
+  return kt_end(d);
 }
 
 template <typename T>

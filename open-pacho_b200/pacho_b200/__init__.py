@@ -1,100 +1,37 @@
 """pacho_b200: B200 (sm_100a) backend for OpenPacho's linear-algebra hot path.
 
 * :class:`B200Backend` -- OpenPacho's backend protocol (``matmul``, ``norm``,
-  ``upload``/``download``/``empty``/``full``, ``synchronize``) over the C-ABI
-  library ``libpacho_b200.so`` (hand-written CUDA for sm_100a).
-* :func:`register` -- adds ``"b200"`` to an installed OpenPacho's dispatch.
-* ``asarray``/``asnumpy``/``matmul``/``dot``/``linalg.norm``/``set_backend``/
-  ``use_backend``, the elementwise ufuncs, ``where``, ``sum``/``mean``/
-  ``amin``/``amax``, ``transpose``/``diag`` -- the same public API for
-  environments without OpenPacho.
-* :mod:`pacho_b200.distributed` -- sharded GEMM and norm across GPUs (NCCL).
-* ``devices()`` and ``python -m pacho_b200 devices|benchmark`` -- discovery and
-  the synchronized benchmark of OpenPacho's ``pacho`` command.
+  ``upload``/``download``/``empty``/``full``, ``synchronize``; ``elementwise``,
+  ``gather``, ``reduce`` around the path; ``residual_matvec`` and
+  ``create_lowering`` for compiled plans) over the C-ABI library
+  ``libpacho_b200.so`` (hand-written CUDA for sm_100a).
+* :func:`register` -- adds ``"b200"`` to an installed OpenPacho's dispatch, so
+  ``openpacho.set_backend("b200")``, ``openpacho.asarray(x, backend="b200")``,
+  ``@``, ``openpacho.linalg.norm``, ``openpacho.compile`` and the ``pacho``
+  command (``python -m pacho_b200``) run on the B200.
+* :mod:`pacho_b200.distributed` -- the sharded forms (batch split, row blocks
+  with B broadcast, norm and DOT partials over NVLink) for one process per GPU.
+* :func:`devices` -- the visible B200s as OpenPacho-style ``DeviceInfo``.
+* :class:`DeviceArray` -- a typed view of a device buffer, returned by this
+  package's own functions when they are not handed OpenPacho arrays.
 """
 
-from . import linalg
-from .api import (
-    absolute,
-    add,
-    amax,
-    amin,
-    array,
-    asarray,
-    asnumpy,
-    cos,
-    diag,
-    divide,
-    dot,
-    empty,
-    equal,
-    exp,
-    full,
-    get_backend,
-    greater,
-    greater_equal,
-    isfinite,
-    less,
-    less_equal,
-    log,
-    matmul,
-    mean,
-    multiply,
-    ndarray,
-    negative,
-    not_equal,
-    ones,
-    ones_like,
-    positive,
-    power,
-    reshape,
-    set_backend,
-    sin,
-    sqrt,
-    subtract,
-    sum,
-    synchronize,
-    tanh,
-    to_backend,
-    transpose,
-    true_divide,
-    use_backend,
-    where,
-    zeros,
-    zeros_like,
-)
-from .backend import B200Backend, DeviceBuffer
+from .backend import B200Backend, DeviceArray, DeviceBuffer
 from .discovery import DeviceInfo, devices
 from .exceptions import BackendMismatchError, BackendUnavailableError, UnsupportedDtypeError
 from .register import register, unregister
 
-__version__ = "0.1.0"
+__version__ = "0.2.0"
 
 __all__ = [
     "B200Backend",
     "BackendMismatchError",
     "BackendUnavailableError",
+    "DeviceArray",
     "DeviceBuffer",
     "DeviceInfo",
     "UnsupportedDtypeError",
-    "array",
-    "asarray",
-    "asnumpy",
     "devices",
-    "dot",
-    "empty",
-    "full",
-    "get_backend",
-    "linalg",
-    "matmul",
-    "ndarray",
-    "ones",
     "register",
-    "reshape",
-    "set_backend",
-    "synchronize",
-    "to_backend",
     "unregister",
-    "use_backend",
-    "zeros",
 ]

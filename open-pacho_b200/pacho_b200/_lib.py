@@ -81,9 +81,13 @@ PROTOTYPES = {
     "pb_timer_start": [_ctx, _i],
     "pb_timer_stop": [_ctx, _i, C.POINTER(C.c_float)],
     "pb_launch_count": [_ctx, _i, C.POINTER(C.c_uint64)],
+    "pb_ktimer_enable": [_ctx, _i, _i],
+    "pb_ktimer_read": [_ctx, _i, C.POINTER(C.c_double), C.POINTER(C.c_uint64)],
+    "pb_memory_stats": [_ctx, _i, C.POINTER(_sz), C.POINTER(_sz), C.POINTER(_sz), C.POINTER(_sz)],
     "pb_gemm": [_ctx, _i, _i, _i, _pi64, _pi64, _pi64, _i64, _i64, _i64, _p, _p, _p],
     "pb_gemm_ex": [_ctx, _i, _i, _i, _pi64, _pi64, _pi64, _i64, _i64, _i64, _p, _p, _p, _i],
     "pb_gemv": [_ctx, _i, _i, _i64, _i64, _p, _p, _p],
+    "pb_gemv_residual": [_ctx, _i, _i, _i64, _i64, _p, _p, _p, _p],
     "pb_elementwise": [_ctx, _i, _i, _i, C.POINTER(_p), C.POINTER(_i), _pi64, _i, _pi64, _i, _p],
     "pb_gather": [_ctx, _i, _i, _p, _i, _pi64, _i64, _pi64, _p],
     "pb_reduce": [_ctx, _i, _i, _i, _p, _i, _pi64, C.c_uint32, _i, _p],
@@ -92,6 +96,7 @@ PROTOTYPES = {
     "pb_peer_export": [_ctx, _i, _i, _i, C.c_char_p],
     "pb_peer_import": [_ctx, _i, _i, C.c_char_p],
     "pb_peer_close": [_ctx, _i],
+    "pb_peer_set_wait": [_ctx, _i, C.c_uint64],
     "pb_dot_sharded": [_ctx, _i, _i, _i64, _p, _p, _p],
     "pb_norm": [_ctx, _i, _i, _i64, _i64, _i64, _p, _p],
     "pb_norm_strided": [_ctx, _i, _i, _i, _pi64, _pi64, _i, _pi64, _pi64, _p, _p],

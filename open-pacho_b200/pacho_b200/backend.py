@@ -56,6 +56,56 @@ class DeviceBuffer:
             pass
 
 
+class DeviceArray:
+    """A typed view of one :class:`DeviceBuffer`: the four attributes the
+    backend protocol reads of an operand (``shape``, ``ndim``, ``dtype``,
+    ``_data``) plus ``numpy()``.  It is what this package's own functions
+    (multi-GPU, the compiled-plan lowering) return when they are not handed
+    OpenPacho arrays; it has no arithmetic of its own -- OpenPacho's
+    ``ndarray`` is the array type users compute with."""
+
+    __slots__ = ("_backend", "_data", "shape", "dtype")
+
+    def __init__(self, backend: "B200Backend", data: DeviceBuffer, shape, dtype):
+        self._backend = backend
+        self._data = data
+        self.shape = tuple(int(d) for d in shape)
+        self.dtype = np.dtype(dtype)
+
+    @property
+    def ndim(self) -> int:
+        return len(self.shape)
+
+    @property
+    def size(self) -> int:
+        return prod(self.shape)
+
+    @property
+    def nbytes(self) -> int:
+        return self.size * self.dtype.itemsize
+
+    def numpy(self) -> np.ndarray:
+        return self._backend.download(self)
+
+    def item(self):
+        if self.size != 1:
+            raise ValueError("only one-element arrays convert to a Python scalar")
+        return self.numpy().reshape(()).item()
+
+    def __repr__(self):
+        return f"DeviceArray(shape={self.shape}, dtype={self.dtype}, device={self._backend.ordinal})"
+
+
+def wrap_like(template, data, shape, dtype, backend):
+    """An array of ``template``'s kind around ``data``: OpenPacho's ndarray
+    (its ``_wrap`` constructor, src/openpacho/_array.py:43-51) when the caller
+    passed OpenPacho arrays, else a :class:`DeviceArray`."""
+    wrap = getattr(type(template), "_wrap", None)
+    if wrap is not None:
+        return wrap(data, tuple(shape), np.dtype(dtype), backend)
+    return DeviceArray(backend, data, shape, dtype)
+
+
 def _broadcast_strides(shape, own):
     """Element strides of a C-contiguous operand of shape ``own`` seen through
     NumPy broadcasting to ``shape`` (0 along broadcast dimensions)."""
@@ -287,6 +337,42 @@ class B200Backend:
                     "pb_norm_strided",
                 )
         return out
+
+    def residual_matvec(self, a, x, b):
+        """``b - a @ x`` in one GEMV launch with the subtraction in its
+        epilogue (``pb_gemv_residual``); the compiled plans call it for a
+        residual whose product has no other use (src/openpacho/_compiler.py:
+        157-176, 306-307).  Checks as residual_matvec_data
+        (src/openpacho/_gemv.py:10-23)."""
+        if a.ndim != 2 or x.ndim != 1 or b.ndim != 1:
+            raise ValueError("Residual GEMV requires a matrix and two vectors")
+        rows, columns = a.shape
+        if tuple(x.shape) != (columns,) or tuple(b.shape) != (rows,):
+            raise ValueError("Residual GEMV dimensions do not match")
+        dtype = np.dtype(a.dtype)
+        if dtype not in (np.dtype(np.float32), np.dtype(np.float64)) or x.dtype != dtype or b.dtype != dtype:
+            raise ValueError("Residual GEMV requires matching float32/float64 dtypes")
+        if any(getattr(v._data, "backend", None) is not self for v in (a, x, b)):
+            raise ValueError("Residual GEMV inputs must belong to the same backend")
+        out = self.empty((rows,), dtype)
+        if rows:
+            with self._lock:
+                self._require_open()
+                self._check(
+                    self._lib.pb_gemv_residual(self._ctx, 0, _lib.dtype_code(dtype), rows, columns,
+                                               C.c_void_p(a._data.ptr), C.c_void_p(x._data.ptr),
+                                               C.c_void_p(b._data.ptr), C.c_void_p(out.ptr)),
+                    "pb_gemv_residual",
+                )
+        return out
+
+    def create_lowering(self):
+        """The compiled-plan lowering (src/openpacho/_lowering.py:224-231):
+        residual GEMVs fused into the GEMV epilogue, elementwise groups and
+        their reductions on the b200 kernels."""
+        from .lowering import B200Lowering
+
+        return B200Lowering(self)
 
     def prepare_padded_matmul(self, ashape, bshape, shape, dtype):
         """Decline the padding hint (src/openpacho/_padding.py:19-22): TMA

@@ -11,8 +11,17 @@ the sharded forms of its hot path that split naturally:
 * :func:`sharded_norm` -- global Euclidean norm of a vector sliced across ranks
   (local (scale, ssq) pairs exchanged and merged in rank order);
 * :func:`sharded_dot` -- global DOT of sliced vectors (local DOT + sum);
-* :func:`rowblock_matmul` -- row blocks of A per rank, B broadcast from a root;
-* :func:`batch_matmul` -- the leading batch dimension split across ranks.
+* :func:`rowblock_matmul` -- row blocks of A per rank, B broadcast from a root,
+  optionally the row blocks of C gathered onto every rank;
+* :func:`batch_matmul` -- the leading batch dimension split across ranks
+  (B broadcasting over it), optionally gathered;
+* :func:`scatter_rows` / :func:`gather_rows` -- this rank's block of a host
+  array on its GPU, and the blocks of every rank assembled on every GPU
+  (one NCCL broadcast per rank into its rows, uneven blocks allowed).
+
+Arrays are anything with the backend protocol's ``shape``/``dtype``/``_data``
+(OpenPacho arrays on the b200 backend, or :class:`~pacho_b200.backend.DeviceArray`);
+results come back as the same kind.
 
 No data-path collective is used where the work is independent (row blocks,
 batch split); the broadcast of B happens once per operand.  The norm and DOT
@@ -31,8 +40,7 @@ import time
 import numpy as np
 
 from . import _lib
-from .api import asarray, ndarray
-from .backend import B200Backend
+from .backend import B200Backend, DeviceArray, wrap_like
 
 
 class RankFailure(RuntimeError):
@@ -116,6 +124,14 @@ class Group:
                 lib.pb_peer_close(b._ctx, 0)
         return agreed
 
+    def exchange(self, tag: str, value: int) -> list[int]:
+        """Every rank's integer ``value`` for ``tag``, in rank order (host store)."""
+        if self.world == 1:
+            return [int(value)]
+        key = f"{self.prefix}/x/{tag}"
+        self.store.set(f"{key}/{self.rank}", str(int(value)).encode())
+        return [int(_store_get(self.store, f"{key}/{r}", self.timeout)) for r in range(self.world)]
+
     def heartbeat(self):
         """Announce this rank at the next step and wait (bounded) for every
         peer; raises RankFailure, before any collective, if one is missing."""
@@ -153,18 +169,22 @@ class Group:
             self.close()
 
 
-def _buf(a: ndarray) -> C.c_void_p:
+def _buf(a) -> C.c_void_p:
     return C.c_void_p(a._data.ptr)
 
 
-def sharded_norm(group: Group, x_local: ndarray) -> ndarray:
+def _scalar(template, out, dtype, backend):
+    return wrap_like(template, out, (), dtype, backend)
+
+
+def sharded_norm(group: Group, x_local):
     """Euclidean norm of the concatenation of every rank's ``x_local``
     (any shape, flattened; may be empty).  Every rank gets the result."""
     b = group.backend
     dtype = b.validate_dtype(x_local.dtype)
     out = b.empty((1,), dtype)
+    n = int(np.prod(x_local.shape))
     if group.world == 1:
-        n = x_local.size
         with b._lock:
             if n:
                 _lib.check(b._lib.pb_norm(b._ctx, 0, _lib.dtype_code(dtype), 1, n, 1, _buf(x_local),
@@ -172,65 +192,114 @@ def sharded_norm(group: Group, x_local: ndarray) -> ndarray:
             else:
                 _lib.check(b._lib.pb_fill(b._ctx, 0, _lib.dtype_code(dtype), C.c_void_p(out.ptr), 1,
                                           0.0), "pb_fill")
-        return ndarray._wrap(out, (), dtype, b)
+        return _scalar(x_local, out, dtype, b)
     group.heartbeat()
     with b._lock:
-        _lib.check(b._lib.pb_norm_sharded(b._ctx, 0, _lib.dtype_code(dtype), x_local.size,
-                                          _buf(x_local) if x_local.size else None, C.c_void_p(out.ptr)),
+        _lib.check(b._lib.pb_norm_sharded(b._ctx, 0, _lib.dtype_code(dtype), n,
+                                          _buf(x_local) if n else None, C.c_void_p(out.ptr)),
                    "pb_norm_sharded")
-    return ndarray._wrap(out, (), dtype, b)
+    return _scalar(x_local, out, dtype, b)
 
 
-def sharded_dot(group: Group, u_local: ndarray, v_local: ndarray) -> ndarray:
+def sharded_dot(group: Group, u_local, v_local):
     """DOT of vectors sliced identically across ranks; every rank gets it."""
     b = group.backend
-    if u_local.shape != v_local.shape or u_local.ndim != 1:
+    if tuple(u_local.shape) != tuple(v_local.shape) or len(u_local.shape) != 1:
         raise ValueError("sharded_dot takes equal 1-D slices")
     dtype = b.validate_dtype(np.result_type(u_local.dtype, v_local.dtype))
+    if u_local.dtype != dtype or v_local.dtype != dtype:
+        raise NotImplementedError("sharded_dot needs both slices in the result dtype")
     out = b.empty((1,), dtype)
     code = _lib.dtype_code(dtype)
+    n = u_local.shape[0]
     if group.p2p:
         group.heartbeat()
         with b._lock:
-            _lib.check(b._lib.pb_dot_sharded(b._ctx, 0, code, u_local.size, _buf(u_local),
-                                             _buf(v_local), C.c_void_p(out.ptr)), "pb_dot_sharded")
-        return ndarray._wrap(out, (), dtype, b)
+            _lib.check(b._lib.pb_dot_sharded(b._ctx, 0, code, n, _buf(u_local), _buf(v_local),
+                                             C.c_void_p(out.ptr)), "pb_dot_sharded")
+        return _scalar(u_local, out, dtype, b)
     with b._lock:
-        _lib.check(b._lib.pb_dot(b._ctx, 0, code, u_local.size, _buf(u_local), _buf(v_local),
+        _lib.check(b._lib.pb_dot(b._ctx, 0, code, n, _buf(u_local), _buf(v_local),
                                  C.c_void_p(out.ptr)), "pb_dot")
     if group.world > 1:
         group.heartbeat()
         with b._lock:
             _lib.check(b._lib.pb_allreduce_sum(b._ctx, 0, code, C.c_void_p(out.ptr), 1),
                        "pb_allreduce_sum")
-    return ndarray._wrap(out, (), dtype, b)
+    return _scalar(u_local, out, dtype, b)
 
 
-def broadcast(group: Group, a: ndarray, root: int = 0) -> ndarray:
+def broadcast(group: Group, a, root: int = 0):
     """In-place broadcast of ``a`` (same shape and dtype on every rank)."""
     if group.world > 1:
         b = group.backend
+        nbytes = int(np.prod(a.shape)) * np.dtype(a.dtype).itemsize
         group.heartbeat()
         with b._lock:
-            _lib.check(b._lib.pb_broadcast(b._ctx, 0, _buf(a), a.nbytes, root), "pb_broadcast")
+            _lib.check(b._lib.pb_broadcast(b._ctx, 0, _buf(a), nbytes, root), "pb_broadcast")
     return a
 
 
-def rowblock_matmul(group: Group, a_local: ndarray, b: ndarray) -> ndarray:
+def _matmul(group: Group, a, b):
+    """``a @ b`` on this rank's GPU through the backend protocol."""
+    be = group.backend
+    dtype = be.validate_dtype(np.result_type(a.dtype, b.dtype))
+    if a.dtype != dtype or b.dtype != dtype:
+        raise NotImplementedError("sharded matmul needs both operands in the result dtype")
+    if len(a.shape) < 2 or len(b.shape) < 2:
+        raise ValueError("sharded matmul takes matrices (or batches of them)")
+    if a.shape[-1] != b.shape[-2]:
+        raise ValueError("matmul inner dimensions do not match")
+    batch = np.broadcast_shapes(tuple(a.shape[:-2]), tuple(b.shape[:-2]))
+    shape = tuple(batch) + (a.shape[-2], b.shape[-1])
+    return wrap_like(a, be.matmul(a, b, shape, dtype), shape, dtype, be)
+
+
+def gather_rows(group: Group, local):
+    """Every rank's block of rows (leading dimension; the trailing
+    dimensions equal on all ranks) stacked in rank order, on every rank.  One
+    NCCL broadcast per rank, in place into that rank's rows of the result;
+    the blocks may differ in length."""
+    be = group.backend
+    if group.world == 1:
+        return local
+    rows = group.exchange(f"gather/{group._step}", local.shape[0] if local.shape else 0)
+    trailing = tuple(local.shape[1:])
+    row_bytes = int(np.prod(trailing)) * np.dtype(local.dtype).itemsize
+    shape = (sum(rows),) + trailing
+    out = be.empty(shape, local.dtype)
+    offsets = np.concatenate([[0], np.cumsum(rows)]).astype(int)
+    mine = rows[group.rank] * row_bytes
+    with be._lock:
+        if mine:
+            _lib.check(be._lib.pb_d2d(be._ctx, 0, C.c_void_p(out.ptr + int(offsets[group.rank]) * row_bytes),
+                                      _buf(local), mine), "pb_d2d")
+    group.heartbeat()
+    with be._lock:
+        for r in range(group.world):
+            if rows[r]:
+                _lib.check(be._lib.pb_broadcast(be._ctx, 0, C.c_void_p(out.ptr + int(offsets[r]) * row_bytes),
+                                                rows[r] * row_bytes, r), "pb_broadcast")
+    return wrap_like(local, out, shape, local.dtype, be)
+
+
+def rowblock_matmul(group: Group, a_local, b, *, gather: bool = False):
     """``a_local @ b`` where ``a_local`` is this rank's row block of A and
-    ``b`` is already on every rank (see :func:`broadcast`).  Returns this
-    rank's row block of C; no collective on the data path."""
-    from .api import matmul
+    ``b`` is on every rank (see :func:`broadcast`): this rank's row block of C,
+    with no collective on the data path; ``gather=True`` returns the whole C
+    on every rank (:func:`gather_rows`)."""
+    c_local = _matmul(group, a_local, b)
+    return gather_rows(group, c_local) if gather else c_local
 
-    return matmul(a_local, b)
 
-
-def batch_matmul(group: Group, a_local: ndarray, b: ndarray) -> ndarray:
+def batch_matmul(group: Group, a_local, b, *, gather: bool = False):
     """Batched ``a_local @ b`` for this rank's slice of the leading batch
-    dimension of A (B broadcasts over it)."""
-    from .api import matmul
-
-    return matmul(a_local, b)
+    dimension of A, B broadcasting over it; with
+    ``gather=True`` every rank gets the whole batched product."""
+    if len(a_local.shape) < 3:
+        raise ValueError("batch_matmul splits a leading batch dimension of A")
+    c_local = _matmul(group, a_local, b)
+    return gather_rows(group, c_local) if gather else c_local
 
 
 def local_rows(a: np.ndarray, group: Group) -> np.ndarray:
@@ -239,8 +308,14 @@ def local_rows(a: np.ndarray, group: Group) -> np.ndarray:
     return np.ascontiguousarray(a[start:stop])
 
 
-def upload_local(a: np.ndarray, group: Group) -> ndarray:
-    return asarray(local_rows(a, group), backend=group.backend)
+def scatter_rows(a: np.ndarray, group: Group) -> DeviceArray:
+    """This rank's row block of host array ``a`` (every rank holds ``a``) on
+    its GPU."""
+    block = local_rows(a, group)
+    return DeviceArray(group.backend, group.backend.upload(block), block.shape, block.dtype)
+
+
+upload_local = scatter_rows
 
 
 __all__ = [
@@ -248,8 +323,10 @@ __all__ = [
     "RankFailure",
     "batch_matmul",
     "broadcast",
+    "gather_rows",
     "local_rows",
     "rowblock_matmul",
+    "scatter_rows",
     "shard_range",
     "sharded_dot",
     "sharded_norm",

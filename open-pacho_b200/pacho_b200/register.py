@@ -4,7 +4,8 @@ OpenPacho hard-codes its backend names: ``get_backend`` accepts backend
 objects only if they are a ``NumpyBackend`` or are named opencl/vulkan/cuda,
 and strings only from that set (src/openpacho/backends.py:198-214).
 ``_array`` binds ``get_backend`` at import (src/openpacho/_array.py:11), as
-does ``random`` (src/openpacho/random.py:17), while ``set_backend`` and
+do ``random`` (src/openpacho/random.py:18) and ``cli`` (src/openpacho/cli.py:15),
+while ``set_backend`` and
 ``use_backend`` look the module global up at call time (backends.py:219,226).
 So :func:`register` wraps ``get_backend`` and rebinds the wrapper in each of
 those places.  The wrapper resolves ``"b200"`` (optionally ``device=``) and
@@ -18,6 +19,10 @@ from functools import lru_cache
 from .backend import B200Backend
 
 _MARK = "_pacho_b200_wrapped"
+# Modules that bind get_backend by name at import: the array front end
+# (src/openpacho/_array.py:11), random (src/openpacho/random.py:18) and the
+# command line (src/openpacho/cli.py:15).
+_BINDERS = ("_array", "random", "cli")
 
 
 @lru_cache(maxsize=8)
@@ -76,7 +81,7 @@ def register(openpacho=None):
     get_backend.__doc__ = original.__doc__
     backends.get_backend = get_backend
     _wrap_devices(openpacho, backends)
-    for name in ("_array", "random"):
+    for name in _BINDERS:
         try:
             module = importlib.import_module(f"{openpacho.__name__}.{name}")
         except ImportError:
@@ -135,7 +140,7 @@ def unregister(openpacho=None):
         return
     original = wrapped.__wrapped__
     backends.get_backend = original
-    for name in ("_array", "random"):
+    for name in _BINDERS:
         try:
             module = importlib.import_module(f"{openpacho.__name__}.{name}")
         except ImportError:

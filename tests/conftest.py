@@ -7,6 +7,7 @@ device is missing; ``-m "not gpu"`` tests run on any CPU machine.
 from __future__ import annotations
 
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -19,6 +20,19 @@ for p in (ROOT / "open-pacho_b200", ROOT, ROOT / "tests" / "golden"):
         sys.path.insert(0, str(p))
 
 GOLDEN = ROOT / "tests" / "golden"
+
+# OpenPacho's own front end (the reference) for the CPU integration tests:
+# importable when installed, or from a source tree named by OPENPACHO_SRC
+# (the directory that contains the ``openpacho`` package).  Those tests skip
+# without it; the GPU machines do not have it.
+_OPENPACHO_SRC = os.environ.get("OPENPACHO_SRC")
+if _OPENPACHO_SRC and _OPENPACHO_SRC not in sys.path:
+    sys.path.append(_OPENPACHO_SRC)
+
+
+@pytest.fixture(scope="session")
+def openpacho():
+    return pytest.importorskip("openpacho", reason="OpenPacho not importable (set OPENPACHO_SRC)")
 
 
 def pytest_configure(config):

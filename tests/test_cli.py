@@ -1,13 +1,20 @@
-"""The ``python -m pacho_b200`` command and ``devices("b200")`` (CPU parts).
+"""``python -m pacho_b200`` runs OpenPacho's own ``pacho`` command with b200.
 
-Mirrors src/openpacho/cli.py:100-147: argument choices, exit status 2 with a
-message when discovery fails, and OpenPacho's own ``devices`` learning the
-``"b200"`` name through :func:`pacho_b200.register`.
+The command is OpenPacho's (src/openpacho/cli.py:99-147); this package only
+registers b200 and lets the two ``--backend`` options accept it.  These CPU
+tests run the real command (skipped without OpenPacho) with the host stand-in
+in place of the GPU backend, so the benchmark's own validation and report
+come out of OpenPacho's code.
 """
 
 from __future__ import annotations
 
+import argparse
 import ctypes as C
+import importlib
+import json
+import os
+import subprocess
 import sys
 from pathlib import Path
 
@@ -15,7 +22,12 @@ import numpy as np
 import pytest
 
 import pacho_b200 as pb
-from pacho_b200 import _lib, cli
+from host_b200 import HostB200
+from pacho_b200 import _lib, command
+
+register_module = importlib.import_module("pacho_b200.register")
+
+ROOT = Path(__file__).resolve().parent.parent
 
 
 def _gpu_visible() -> bool:
@@ -23,35 +35,57 @@ def _gpu_visible() -> bool:
     return _lib.load().pb_device_count(C.byref(n)) == 0 and n.value > 0
 
 
-def test_backend_choice_is_b200_only():
-    with pytest.raises(SystemExit):
-        cli.main(["benchmark", "--backend", "cuda"])
-    with pytest.raises(SystemExit):
-        cli.main(["devices", "--backend", "opencl"])
-    with pytest.raises(ValueError):
-        pb.devices("cuda")
+def test_command_without_openpacho_exits_2():
+    env = {k: v for k, v in os.environ.items() if k not in ("OPENPACHO_SRC", "PYTHONPATH")}
+    env["PYTHONPATH"] = str(ROOT / "open-pacho_b200")
+    proc = subprocess.run([sys.executable, "-c", "import sys; sys.modules['openpacho'] = None; "
+                           "from pacho_b200.command import main; raise SystemExit(main(['devices']))"],
+                          capture_output=True, text=True, env=env, timeout=120)
+    assert proc.returncode == 2
+    assert "OpenPacho is not installed" in proc.stderr
 
 
-def test_discovery_failure_exits_2_with_a_message(capsys):
+def test_backend_option_accepts_b200_only_while_the_command_runs(openpacho):
+    parser = argparse.ArgumentParser()
+    with command._backend_choice_b200():
+        parser.add_argument("--backend", choices=("opencl", "cuda"))
+        parser.add_argument("--other", choices=("x",))
+    assert parser.parse_args(["--backend", "b200"]).backend == "b200"
+    with pytest.raises(SystemExit):
+        parser.parse_args(["--other", "b200"])
+    later = argparse.ArgumentParser()
+    later.add_argument("--backend", choices=("opencl",))
+    with pytest.raises(SystemExit):
+        later.parse_args(["--backend", "b200"])
+
+
+def test_pacho_benchmark_on_b200_is_openpachos_benchmark(openpacho, monkeypatch, capsys):
+    host = HostB200()
+    monkeypatch.setattr(register_module, "_get_b200", lambda device: host)
+    try:
+        rc = command.main(["benchmark", "--backend", "b200", "--size", "16", "--repeat", "2"], openpacho)
+        report = json.loads(capsys.readouterr().out)
+    finally:
+        pb.unregister(openpacho)
+    assert rc == 0
+    assert report["backend"] == "b200" and report["device"] == "host stand-in"
+    assert [c["operation"] for c in report["cases"]] == ["add", "matmul", "sum"]
+    assert report["all_valid"]
+    methods = {c[0] for c in host.calls}
+    assert {"upload", "elementwise", "matmul", "reduce", "download"} <= methods
+
+
+def test_pacho_devices_b200_without_a_gpu_exits_2(openpacho, capsys):
     if _gpu_visible():
         pytest.skip("a GPU is visible")
-    assert cli.main(["devices"]) == 2
-    assert "b200 device discovery failed" in capsys.readouterr().err
-    assert cli.main(["benchmark", "--size", "8"]) == 2
+    try:
+        assert command.main(["devices", "--backend", "b200"], openpacho) == 2
+    finally:
+        pb.unregister(openpacho)
+    assert capsys.readouterr().err.startswith("pacho: ")
 
 
-def test_benchmark_rejects_bad_arguments():
-    with pytest.raises(ValueError):
-        cli.benchmark(size=0)
-    with pytest.raises(ValueError):
-        cli.benchmark(dtype="float16")
-
-
-def test_register_teaches_openpacho_devices_b200():
-    reference_src = Path("/root/reference/src")
-    if reference_src.exists() and str(reference_src) not in sys.path:
-        sys.path.append(str(reference_src))
-    openpacho = pytest.importorskip("openpacho")
+def test_register_teaches_openpacho_devices_b200(openpacho):
     import openpacho.cli as ocli
 
     original = openpacho.backends.devices
@@ -59,48 +93,28 @@ def test_register_teaches_openpacho_devices_b200():
     try:
         assert openpacho.backends.devices is not original
         assert ocli.devices is openpacho.backends.devices
+        assert ocli.get_backend is openpacho.backends.get_backend
         if not _gpu_visible():
             with pytest.raises(openpacho.BackendUnavailableError):
                 openpacho.backends.devices("b200")
     finally:
         pb.unregister(openpacho)
     assert openpacho.backends.devices is original and ocli.devices is original
+    assert ocli.get_backend is openpacho.backends.get_backend
 
 
-def test_ndarray_methods_route_to_the_backend():
-    class Fake(pb.B200Backend):
-        device = "fake"
-
-        def __init__(self):  # no library, no device
-            self.calls = []
-
-        def validate_dtype(self, dtype):
-            return np.dtype(dtype)
-
-        def reduce(self, a, axes, keepdims, dtype, *, operation="sum"):
-            self.calls.append(("reduce", axes, operation, np.dtype(dtype)))
-            return object()
-
-        def gather(self, a, shape, offset, strides):
-            self.calls.append(("gather", tuple(shape), offset, tuple(strides)))
-            return object()
-
-        def elementwise(self, name, args, shape, dtype):
-            self.calls.append(("elementwise", name))
-            return object()
-
-        def upload(self, host):
-            return object()
-
-    f = Fake()
-    a = pb.ndarray._wrap(object(), (2, 3), np.float32, f)
-    assert a.T.shape == (3, 2)
-    a.transpose(1, 0)
-    a.sum(axis=1)
-    a.min()
-    a.max(axis=0)
-    a.mean()
-    assert f.calls[:2] == [("gather", (3, 2), 0, (1, 3)), ("gather", (3, 2), 0, (1, 3))]
-    assert [c[1:3] for c in f.calls if c[0] == "reduce"] == [((1,), "sum"), ((0, 1), "min"),
-                                                             ((0,), "max"), ((0, 1), "sum")]
-    assert f.calls[-1] == ("elementwise", np.true_divide.__name__)  # "divide" in NumPy 2
+def test_openpacho_array_methods_route_to_the_backend(openpacho):
+    """OpenPacho's ndarray methods on a b200 array reach gather/reduce/
+    elementwise (src/openpacho/_array.py:88-160, 389-456)."""
+    host = HostB200()
+    pb.register(openpacho)
+    try:
+        a = openpacho.asarray(np.arange(6, dtype=np.float32).reshape(2, 3), backend=host)
+        assert a.T.shape == (3, 2)
+        np.testing.assert_array_equal(openpacho.asnumpy(a.transpose(1, 0)), np.arange(6).reshape(2, 3).T)
+        np.testing.assert_array_equal(openpacho.asnumpy(a.sum(axis=1)), [3, 12])
+        assert openpacho.asnumpy(a.min()) == 0 and openpacho.asnumpy(a.mean()) == 2.5
+    finally:
+        pb.unregister(openpacho)
+    kinds = [c[0] for c in host.calls]
+    assert kinds.count("gather") == 2 and kinds.count("reduce") == 3

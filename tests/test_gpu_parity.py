@@ -15,7 +15,7 @@ import cases
 import numpy as np
 import pytest
 
-import pacho_b200 as pb
+import front as pb
 from oracle import exact, numpy_backend, tolerance
 from pacho_b200 import _lib
 
@@ -113,7 +113,7 @@ def _call_gemm_ex(backend, a, b, algo):
         _lib.i64_array(_matrix_strides(batch, b.shape[:-2])), m, n, k,
         C.c_void_p(da.ptr), C.c_void_p(db.ptr), C.c_void_p(dc.ptr), algo)
     _lib.check(status, "pb_gemm_ex")
-    return backend.download(pb.api.ndarray._wrap(dc, out_shape, dtype, backend))
+    return pb.wrap(dc, out_shape, dtype, backend).numpy()
 
 
 def _gemm_shapes():

@@ -10,18 +10,13 @@ the same calls the compiled plans make (src/openpacho/_compiler.py:298-305).
 from __future__ import annotations
 
 import ctypes as C
-import sys
 import threading
 import weakref
-from pathlib import Path
 
 import numpy as np
 import pytest
 
-REFERENCE_SRC = Path("/root/reference/src")
-if REFERENCE_SRC.exists() and str(REFERENCE_SRC) not in sys.path:
-    sys.path.append(str(REFERENCE_SRC))
-openpacho = pytest.importorskip("openpacho")
+openpacho = pytest.importorskip("openpacho", reason="OpenPacho not importable (set OPENPACHO_SRC)")
 
 import pacho_b200  # noqa: E402
 from pacho_b200 import _lib  # noqa: E402
@@ -163,13 +158,52 @@ def test_openpacho_elementwise_reductions_and_views_reach_their_entry_points(fak
 
 
 def test_openpacho_compiled_residual_plan_on_b200(fake_b200):
-    """A compiled solver step (b - A @ x, then its norm) runs through the same
-    entry points (src/openpacho/_compiler.py:298-305; no lowering hook)."""
+    """A compiled solver step (b - A @ x, then its norm): the product has no
+    other use, so the plan's residual step reaches the fused GEMV epilogue
+    (src/openpacho/_compiler.py:157-176, 306-307, through create_lowering)."""
     A = openpacho.asarray(np.ones((64, 64), np.float64), backend=fake_b200)
     x = openpacho.asarray(np.ones(64, np.float64), backend=fake_b200)
     b = openpacho.asarray(np.ones(64, np.float64), backend=fake_b200)
-    step = openpacho.compile(lambda A, x, b: (b - A @ x, openpacho.linalg.norm(b - A @ x)))
-    r, n = step(A, x, b)
-    assert r.shape == (64,) and n.shape == ()
+    step = openpacho.compile(lambda A, x, b: openpacho.linalg.norm(b - A @ x))
+    n = step(A, x, b)
+    assert n.shape == ()
     called = [name for name, _ in fake_b200._lib.calls]
-    assert "pb_gemv" in called and "pb_elementwise" in called and "pb_norm" in called
+    assert "pb_gemv_residual" in called and "pb_norm" in called
+    assert "pb_gemv" not in called
+    (args,) = _entries(fake_b200, "pb_gemv_residual")
+    assert args[2] == _lib.PB_F64 and args[3:5] == (64, 64)
+
+
+def test_compiled_plans_with_the_b200_lowering_match_openpachos_numpy_backend():
+    """OpenPacho's real compiler over the b200 lowering (host stand-in for the
+    arithmetic): residual GEMV, elementwise groups with scalars and casts, and
+    a reduction of an elementwise group give the NumPy backend's bits."""
+    from host_b200 import HostB200
+
+    host = HostB200()
+    rng = np.random.default_rng(5)
+    A = rng.standard_normal((48, 33)).astype(np.float32)
+    x = rng.standard_normal(33).astype(np.float32)
+    b = rng.standard_normal(48).astype(np.float32)
+    programs = (
+        lambda A, x, b: b - A @ x,
+        lambda A, x, b: ((b * 2.0 - 1) / 3.0).astype(np.float64) + b,
+        lambda A, x, b: openpacho.sum(b * b + 1.5, axis=0),
+        lambda A, x, b: openpacho.where(b > 0, b, 0.0) - openpacho.sqrt(openpacho.absolute(b)),
+        lambda A, x, b: (openpacho.linalg.norm(b - A @ x), openpacho.amax(A * 2.0, axis=1)),
+    )
+    pacho_b200.register(openpacho)
+    try:
+        for fn in programs:
+            host.calls.clear()
+            got = openpacho.compile(fn)(*(openpacho.asarray(v, backend=host) for v in (A, x, b)))
+            want = openpacho.compile(fn)(*(openpacho.asarray(v, backend="numpy") for v in (A, x, b)))
+            got = got if isinstance(got, tuple) else (got,)
+            want = want if isinstance(want, tuple) else (want,)
+            for g, w in zip(got, want):
+                g, w = openpacho.asnumpy(g), openpacho.asnumpy(w)
+                assert g.dtype == w.dtype and g.shape == w.shape
+                np.testing.assert_array_equal(g, w)
+        assert any(c[0] == "residual_matvec" for c in host.calls)
+    finally:
+        pacho_b200.unregister(openpacho)
