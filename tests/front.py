@@ -105,7 +105,7 @@ def wrap(data, shape, dtype, backend):
 def asarray(x, backend=None):
     if isinstance(x, Arr):
         return x
-    host = np.ascontiguousarray(x)
+    host = np.asarray(x, order="C")  # keeps 0-d arrays 0-d (ascontiguousarray would not)
     return Arr(backend, backend.upload(host), host.shape, host.dtype)
 
 
@@ -124,13 +124,12 @@ def apply(name, *inputs):
     """One elementwise operation with NumPy's type resolution."""
     backend = _backend_of(inputs)
     if name == "where":
-        branches = [type(v) if isinstance(v, PY_SCALARS) else v.dtype for v in inputs[1:]]
         samples = [v if isinstance(v, PY_SCALARS) else np.empty(0, v.dtype) for v in inputs[1:]]
         out = np.result_type(*samples)
         resolved = (np.dtype(bool), out, out, out)
-        del branches
     else:
-        types = tuple(type(v) if isinstance(v, PY_SCALARS) else v.dtype for v in inputs)
+        types = tuple(np.dtype(bool) if isinstance(v, bool) else type(v) if isinstance(v, PY_SCALARS)
+                      else v.dtype for v in inputs)
         resolved = tuple(np.dtype(t) for t in getattr(np, name).resolve_dtypes(types + (None,)))
     shape = np.broadcast_shapes(*(getattr(v, "shape", ()) for v in inputs))
     operands = []

@@ -55,6 +55,9 @@ class HostB200(B200Backend):
     def _log(self, method, *details):
         self.calls.append((method,) + details)
 
+    def _buffer(self, array):
+        return HostBuffer(array, self)
+
     def __del__(self):
         pass
 
@@ -68,7 +71,7 @@ class HostB200(B200Backend):
         host = np.array(a, copy=True)
         self.validate_dtype(host.dtype)
         self._log("upload", host.shape, host.dtype)
-        return HostBuffer(host, self)
+        return self._buffer(host)
 
     def download(self, a):
         self._log("download", tuple(a.shape), np.dtype(a.dtype))
@@ -76,40 +79,40 @@ class HostB200(B200Backend):
 
     def empty(self, shape, dtype):
         dtype = self.validate_dtype(dtype)
-        return HostBuffer(np.zeros(prod(shape), dtype), self)
+        return self._buffer(np.zeros(prod(shape), dtype))
 
     def full(self, shape, value, dtype):
         dtype = self.validate_dtype(dtype)
         self._log("full", tuple(shape), value, dtype)
-        return HostBuffer(np.full(prod(shape), value, dtype), self)
+        return self._buffer(np.full(prod(shape), value, dtype))
 
     def matmul(self, a, b, shape, dtype):
         self._log("matmul", tuple(a.shape), tuple(b.shape), tuple(shape), np.dtype(dtype))
         with np.errstate(all="ignore"):
             out = numpy_backend.matmul(_value(a), _value(b))
-        return HostBuffer(np.asarray(out, dtype).reshape(shape), self)
+        return self._buffer(np.asarray(out, dtype).reshape(shape))
 
     def norm(self, a, axes, keepdims, dtype):
         self._log("norm", tuple(a.shape), tuple(axes), keepdims, np.dtype(dtype))
-        return HostBuffer(numpy_backend.norm_data(_value(a), tuple(axes), dtype), self)
+        return self._buffer(numpy_backend.norm_data(_value(a), tuple(axes), dtype))
 
     def elementwise(self, name, args, shape, dtype):
         self._log("elementwise", name, tuple(tuple(a.shape) for a in args), tuple(shape), np.dtype(dtype))
         out = numpy_backend.elementwise(name, [_value(a) for a in args], dtype)
-        return HostBuffer(np.broadcast_to(out, tuple(shape)), self)
+        return self._buffer(np.broadcast_to(out, tuple(shape)))
 
     def gather(self, a, shape, offset, strides):
         self._log("gather", tuple(a.shape), tuple(shape), offset, tuple(strides))
-        return HostBuffer(numpy_backend.gather(_value(a), tuple(shape), offset, tuple(strides)), self)
+        return self._buffer(numpy_backend.gather(_value(a), tuple(shape), offset, tuple(strides)))
 
     def reduce(self, a, axes, keepdims, dtype, *, operation="sum"):
         self._log("reduce", tuple(a.shape), tuple(axes), keepdims, np.dtype(dtype), operation)
-        return HostBuffer(numpy_backend.reduce(_value(a), tuple(axes), False, dtype, operation), self)
+        return self._buffer(numpy_backend.reduce(_value(a), tuple(axes), False, dtype, operation))
 
     def residual_matvec(self, a, x, b):
         self._log("residual_matvec", tuple(a.shape), tuple(x.shape), tuple(b.shape))
         y = numpy_backend.matmul(_value(a), _value(x))
-        return HostBuffer(numpy_backend.elementwise("subtract", (_value(b), y), b.dtype), self)
+        return self._buffer(numpy_backend.elementwise("subtract", (_value(b), y), b.dtype))
 
     def release_cached_memory(self):
         self._log("release_cached_memory")
