@@ -287,6 +287,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 
+// TMEM -> registers, 32 lanes x 16 columns (load and wait in one statement).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]),"=r"(r[1]),"=r"(r[2]),"=r"(r[3]),"=r"(r[4]),"=r"(r[5]),"=r"(r[6]),"=r"(r[7]),"=r"(r[8]),"=r"(r[9]),"=r"(r[10]),"=r"(r[11]),"=r"(r[12]),"=r"(r[13]),"=r"(r[14]),"=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
 // Two 32-column loads in flight before one wait.
 __device__ __forceinline__ void tmem_ld32x2(uint32_t ta, uint32_t tb, uint32_t (&a)[32],
                                             uint32_t (&b)[32]) {
@@ -710,13 +720,33 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 // once its full barrier fires: the TMA for slice g is only issued after the
 // MMAs of slice g - STAGES (the previous user of the columns) completed.
 
+#ifndef PB_TF32_WIDE
+#define PB_TF32_WIDE 1  // 0: no 128 x 192 tiles (measurement builds)
+#endif
 #ifndef PB_TF32_FCHUNK
 #define PB_TF32_FCHUNK 3
 #endif
 constexpr int FCHUNK = PB_TF32_FCHUNK;
 constexpr int T_SPLIT_WARPS = 4, T_ACC_WARPS = 8;
-constexpr int T_ACC_WARP0 = 2 + T_SPLIT_WARPS;
-constexpr int T_THREADS = 32 * (2 + T_SPLIT_WARPS + T_ACC_WARPS);
+
+// Warp roles by tile width.  FBN = 64 / 128: 14 warps (TMA, MMA, split 2..5,
+// promote/store 6..13) at the 128 registers a thread that 14 warps leave (the
+// register file is split over the SM's four sub-partitions).  FBN = 192: the
+// promote warps hold 96 running sums each, so 16 warps are launched at 128
+// registers as four warp groups -- {TMA, MMA, two idle}, {split x4},
+// {promote/store x4} x 2 -- and after set-up the first two groups give
+// registers up for the last two (setmaxnreg): 64 + 96 + 176 + 176 = 512 =
+// 4 x 128, so the increase is always available.
+template <int FBN>
+struct TRoles {
+  static constexpr bool kRegs = FBN == 192;
+  static constexpr int SPLIT0 = kRegs ? 4 : 2;        // first A-split warp
+  static constexpr int ACC0 = SPLIT0 + T_SPLIT_WARPS;  // first promote/store warp
+  static constexpr int THREADS = 32 * (ACC0 + T_ACC_WARPS);
+  static constexpr int REG_CTRL = 64, REG_SPLIT = 96, REG_ACC = 176;
+  static_assert(!kRegs || (THREADS == 512 && REG_CTRL + REG_SPLIT + 2 * REG_ACC <= 4 * 128),
+                "register reallocation must fit the launch's 512 x 128 registers");
+};
 
 template <int FBN>
 struct TSmem {
@@ -724,14 +754,19 @@ struct TSmem {
   static constexpr int B_BYTES = FBN * BK * 4;  // B hi or B lo slice
   static constexpr int A = 0, BHI = A_BYTES, BLO = A_BYTES + B_BYTES;
   static constexpr int STAGE = A_BYTES + 2 * B_BYTES;
-  static constexpr int STAGES = FBN == 128 ? 4 : 6;
+  static constexpr int STAGES = FBN == 192 ? 3 : FBN == 128 ? 4 : 6;
+  // A hi/lo buffers in tensor memory.  At FBN = 192 the two accumulators take
+  // 384 of the 512 columns, so only two slices' A parts fit: those buffers
+  // cycle on their own (the split of slice g waits for the MMAs of slice
+  // g - TST), decoupled from the shared-memory ring.
+  static constexpr int TST = FBN == 192 ? 2 : STAGES;
   // Epilogue staging: a 32 x 32 fp32 box (4 KiB, 128-byte swizzle) per warp.
   static constexpr int OUT = STAGES * STAGE, OUT_BYTES = T_ACC_WARPS * 4096;
   static constexpr int TOTAL = OUT + OUT_BYTES + 1024 + 256;
   static constexpr uint32_t ACOL = 2 * FBN;     // first A column in TMEM
   static constexpr uint32_t TMEM_COLS = 512;
-  static_assert(ACOL + 64 * STAGES <= TMEM_COLS, "TMEM columns");
-  static_assert(8 * (3 * STAGES + 4) + 8 <= 256, "barrier area");
+  static_assert(ACOL + 64 * TST <= TMEM_COLS, "TMEM columns");
+  static_assert(8 * (3 * STAGES + 6) + 8 <= 256, "barrier area");
 };
 
 // hi = round-to-nearest tf32 of x (ties away), lo = tf32(x - hi), in
@@ -743,6 +778,16 @@ __device__ __forceinline__ void split_bits(float x, uint32_t& hi, uint32_t& lo) 
   const uint32_t b = __float_as_uint(x);
   hi = (b + 0x1000u) & 0xffffe000u;
   lo = (__float_as_uint(x - __uint_as_float(hi)) + 0x1000u) & 0xffffe000u;
+}
+
+// Warp-group register reallocation (every warp of the group executes it).
+template <int N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // D (TMEM) += A (TMEM, 128 lanes x 8 columns at tmem_a) * B (smem descriptor).
@@ -811,11 +856,12 @@ __device__ __forceinline__ void store_tma(const Tf32Params& p, const CUtensorMap
 }
 
 template <int FBN>
-__global__ void __launch_bounds__(T_THREADS, 1)
+__global__ void __launch_bounds__(TRoles<FBN>::THREADS, 1)
     tf32x3_tmem_kernel(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b,
                        const __grid_constant__ CUtensorMap map_c, Tf32Params p, int Kp) {
   using L = TSmem<FBN>;
+  using R = TRoles<FBN>;
   constexpr int S = L::STAGES;
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -826,7 +872,11 @@ __global__ void __launch_bounds__(T_THREADS, 1)
   // full[S] (TMA landed), ready[S] (A split into TMEM), empty[S] (MMAs done), accf[2], acce[2]
   const uint32_t full0 = bars, ready0 = bars + 8 * S, empty0 = bars + 16 * S;
   const uint32_t accf0 = bars + 24 * S, acce0 = accf0 + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 3 * S + 4);
+  // tfree[TST] (MMAs of the slice done with a TMEM A buffer; used when TST < S)
+  constexpr int TS = L::TST;
+  constexpr bool kTfree = TS < S;
+  const uint32_t tfree0 = acce0 + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 3 * S + 6);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -841,6 +891,8 @@ __global__ void __launch_bounds__(T_THREADS, 1)
       mbar_init(accf0 + 8 * b, 1);
       mbar_init(acce0 + 8 * b, T_ACC_WARPS);
     }
+    if (kTfree)
+      for (int t = 0; t < TS; ++t) mbar_init(tfree0 + 8 * t, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -864,6 +916,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
+    if constexpr (R::kRegs) reg_dealloc<R::REG_CTRL>();
     if (lane == 0) {
       // ------------------------------------------------ TMA producer
       int64_t g = 0;
@@ -898,6 +951,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
       }
     }
   } else if (warp == 1) {
+    if constexpr (R::kRegs) reg_dealloc<R::REG_CTRL>();
     if (lane == 0) {
       // ------------------------------------------------ MMA issuer
       const uint32_t idesc = instr_desc(FBN);
@@ -924,7 +978,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t st = base + s * L::STAGE;
-            const uint32_t ahi = tmem + L::ACOL + 64u * s, alo = ahi + 32u;
+            const uint32_t ahi = tmem + L::ACOL + 64u * (uint32_t)(g % TS), alo = ahi + 32u;
             const uint64_t bhi = smem_desc(st + L::BHI), blo = smem_desc(st + L::BLO);
             const bool first = kb == kb_start;
 #pragma unroll
@@ -935,13 +989,15 @@ __global__ void __launch_bounds__(T_THREADS, 1)
 #pragma unroll
             for (int k = 0; k < BK / 8; ++k) umma_tf32_ts(d, ahi + 8 * k, bhi + 2 * k, idesc, 1u);
             umma_commit(empty0 + 8 * s);
+            if (kTfree) umma_commit(tfree0 + 8 * (int)(g % TS));
           }
           umma_commit(accf0 + 8 * buf);
         }
       }
     }
-  } else if (warp < T_ACC_WARP0) {
-    // ------------------------------------------------ split A (warps 2..5)
+  } else if (warp >= R::SPLIT0 && warp < R::ACC0) {
+    // ----------------------------------- split A (warps 2..5, or 4..7)
+    if constexpr (R::kRegs) reg_dealloc<R::REG_SPLIT>();
     // Each lane splits its row of every landed A slice (32 values) into the
     // stage's hi and lo columns of its TMEM lane.
     const int quad = warp & 3;
@@ -961,27 +1017,33 @@ __global__ void __launch_bounds__(T_THREADS, 1)
       const int64_t arow = ao * p.M + tc.m_tile * BM + row;  // row of A over all matrices
       for (int kb = kb0; kb < kb1; ++kb, ++g) {
         const int s = (int)(g % S);
-        const bool got = mbar_wait(full0 + 8 * s, (uint32_t)((g / S) & 1), abort_flag, p.err);
+        bool got = mbar_wait(full0 + 8 * s, (uint32_t)((g / S) & 1), abort_flag, p.err);
+        // The TMEM buffer of this slice was last read by the MMAs of slice
+        // g - TS (with TS == S the full barrier above already implies it).
+        const int t = (int)(g % TS);
+        if (kTfree && got)
+          got = mbar_wait(tfree0 + 8 * t, (uint32_t)(((g / TS) & 1) ^ 1), abort_flag, p.err);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         // This lane's row is 128 bytes; the 128-byte swizzle stores its 16-byte
         // chunk j at position j ^ (row % 8).
         const float4* src = reinterpret_cast<const float4*>(gbase + s * L::STAGE + L::A + row * 128);
-        const uint32_t acol = tmem + lane_off + L::ACOL + 64u * s;
+        const uint32_t acol = tmem + lane_off + L::ACOL + 64u * (uint32_t)t;
         float amin = FLT_MAX;  // smallest magnitude of the row's 32 values (NaN ignored)
         __syncwarp();  // converged for the .aligned TMEM stores
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           uint32_t hi[16], lo[16];
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const float4 v = src[(4 * h + t) ^ (row & 7)];
-            split_bits(v.x, hi[4 * t], lo[4 * t]);
-            split_bits(v.y, hi[4 * t + 1], lo[4 * t + 1]);
-            split_bits(v.z, hi[4 * t + 2], lo[4 * t + 2]);
-            split_bits(v.w, hi[4 * t + 3], lo[4 * t + 3]);
+          for (int q = 0; q < 4; ++q) {
+            const float4 v = src[(4 * h + q) ^ (row & 7)];
+            split_bits(v.x, hi[4 * q], lo[4 * q]);
+            split_bits(v.y, hi[4 * q + 1], lo[4 * q + 1]);
+            split_bits(v.z, hi[4 * q + 2], lo[4 * q + 2]);
+            split_bits(v.w, hi[4 * q + 3], lo[4 * q + 3]);
             amin = fminf(amin, fminf(fminf(fabsf(v.x), fabsf(v.y)), fminf(fabsf(v.z), fabsf(v.w))));
           }
           tmem_st16(acol + 16u * h, hi);
@@ -989,13 +1051,13 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         }
         if (amin < kTinyMag) {
           // A zero or tiny value: tag the row if one of the 32 is tiny.
-          bool t = false;
+          bool tagged_row = false;
 #pragma unroll
           for (int t8 = 0; t8 < 8; ++t8) {
             const float4 v = src[t8 ^ (row & 7)];
-            t |= tiny(v.x) | tiny(v.y) | tiny(v.z) | tiny(v.w);
+            tagged_row |= tiny(v.x) | tiny(v.y) | tiny(v.z) | tiny(v.w);
           }
-          if (t) {
+          if (tagged_row) {
             p.rowtag[arow] = p.gen;
             p.tagany[0] = p.gen;
             __threadfence();
@@ -1008,14 +1070,15 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         if (lane == 0) mbar_arrive(ready0 + 8 * s);
       }
     }
-  } else {
-    // ------------------------------- promote and store (warps 6..13)
+  } else if (warp >= R::ACC0) {
+    // ------------------- promote and store (warps 6..13, or 8..15)
+    if constexpr (R::kRegs) reg_alloc<R::REG_ACC>();
     // Every FCHUNK slices the MMA thread commits a chunk of the tile into one
     // of the two TMEM accumulators; these warps add it into fp32 registers,
     // free the accumulator, and at the end of the work item store the tile.
     constexpr int COLS = FBN / 2;
     const int quad = warp & 3;
-    const int half = (warp - T_ACC_WARP0) >> 2;
+    const int half = (warp - R::ACC0) >> 2;
     const int row = quad * 32 + lane;  // row of the tile (TMEM lane)
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const uint32_t acc_base = tmem + lane_off + (uint32_t)(half * COLS);
@@ -1031,15 +1094,21 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         ok = false;
         return;
       }
-      // One 32-column piece at a time (these warps are off the critical path;
-      // two pieces in flight would not fit the 128-register cap of 14 warps).
+      // One piece at a time (these warps are off the critical path; two
+      // pieces in flight would not fit the register cap of 14 warps): 32
+      // columns, or 16 where the running sums themselves take 96 registers.
+      constexpr int PIECE = COLS > 64 ? 16 : 32;
 #pragma unroll
-      for (int piece = 0; piece < COLS / 32; ++piece) {
-        uint32_t r[32];
-        tmem_ld32(acc_base + (uint32_t)(buf * FBN + piece * 32), r);
+      for (int piece = 0; piece < COLS / PIECE; ++piece) {
+        uint32_t r[PIECE];
+        if constexpr (PIECE == 32)
+          tmem_ld32(acc_base + (uint32_t)(buf * FBN + piece * 32), r);
+        else
+          tmem_ld16(acc_base + (uint32_t)(buf * FBN + piece * 16), r);
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          acc[piece * 32 + i] = first ? __uint_as_float(r[i]) : acc[piece * 32 + i] + __uint_as_float(r[i]);
+        for (int i = 0; i < PIECE; ++i)
+          acc[piece * PIECE + i] =
+              first ? __uint_as_float(r[i]) : acc[piece * PIECE + i] + __uint_as_float(r[i]);
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
@@ -1060,12 +1129,16 @@ __global__ void __launch_bounds__(T_THREADS, 1)
       const int64_t col0 = tc.n_tile * FBN + half * COLS;
       if (p.tma_store)
         store_tma<COLS>(p, &map_c, tc, split, quad, col0, acc,
-                        reinterpret_cast<float4*>(gbase + L::OUT + (warp - T_ACC_WARP0) * 4096),
-                        base + L::OUT + (warp - T_ACC_WARP0) * 4096);
+                        reinterpret_cast<float4*>(gbase + L::OUT + (warp - R::ACC0) * 4096),
+                        base + L::OUT + (warp - R::ACC0) * 4096);
       else
         finish_item<COLS>(p, tc, split, tc.m_tile * BM + row, col0, acc);
     }
     if (lane == 0) bulk_wait_all();  // staging buffers are read before the CTA exits
+  } else {
+    // Warps 2 and 3 of the first warp group (FBN = 192) have no role; they
+    // give their registers up with the group.
+    if constexpr (R::kRegs) reg_dealloc<R::REG_CTRL>();
   }
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -1244,7 +1317,7 @@ int launch_tmem(Device* d, const CUtensorMap& ma, const CUtensorMap& mb, const C
   const int64_t items = p.tiles * p.ksplit;
   const int64_t grid = items < d->sm_count ? items : d->sm_count;
   PB_CHECK(kt_begin(d));
-  PB_CHECK(launch_dependent(d, tf32x3_tmem_kernel<FBN>, dim3((unsigned)grid), dim3(T_THREADS),
+  PB_CHECK(launch_dependent(d, tf32x3_tmem_kernel<FBN>, dim3((unsigned)grid), dim3(TRoles<FBN>::THREADS),
                             (size_t)smem, ma, mb, mc, p, (int)Kp));
   return kt_end(d);
 }
@@ -1262,7 +1335,12 @@ int gemm_f32_fused(Device* d, const BatchMap& map, int64_t batch, int64_t M, int
   // 128-wide tiles (split K when they are few): at 128 x 64 the A split per
   // slice costs as much as the slice's MMAs (1024^3 on B200: 57.0 TFLOP/s
   // against 59.7 with 128 x 128 and a 2-way split).
-  const int fbn = N <= 64 ? 64 : 128;
+  // 128 x 192 where it pads N no more than 128 x 128 does (config 3: N = 384
+  // = 2 x 192): a third less A splitting per flop and the wider MMA's higher
+  // rate (measured back to back: 2806 flop/clk/SM at N = 128, 3799 at 256).
+  const int64_t waste128 = ceil_div(N, (int64_t)128) * 128 - N;
+  const int64_t waste192 = ceil_div(N, (int64_t)192) * 192 - N;
+  const int fbn = N <= 64 ? 64 : (N >= 192 && waste192 <= waste128 && PB_TF32_WIDE) ? 192 : 128;
   const int tiles_n = (int)ceil_div(N, (int64_t)fbn);
   const int64_t tiles = (int64_t)tiles_m * tiles_n * batch;
   const int kblocks = (int)(Kp / BK);
@@ -1307,8 +1385,9 @@ int gemm_f32_fused(Device* d, const BatchMap& map, int64_t batch, int64_t M, int
   split_bt_kernel<2><<<dim3((unsigned)gx, (unsigned)gy, (unsigned)nB), 256, 0, d->stream>>>(
       B, Bt, K, N, Kp, p.coltag, p.cgroups, p.tagany, p.gen);
   PB_LAUNCHED(d);
-  PB_CHECK(fbn == 128 ? launch_tmem<128>(d, ma, mb, mc, p, Kp)
-                      : launch_tmem<64>(d, ma, mb, mc, p, Kp));
+  PB_CHECK(fbn == 192   ? launch_tmem<192>(d, ma, mb, mc, p, Kp)
+           : fbn == 128 ? launch_tmem<128>(d, ma, mb, mc, p, Kp)
+                        : launch_tmem<64>(d, ma, mb, mc, p, Kp));
   if (ksplit > 1) PB_CHECK(launch_reduce(d, p, batch * M * N));
   if (p.repair_inline) return PB_OK;
   return gemm_nonfinite_repair_f32(d, map, batch, M, N, K, A, B, C, p.nf);
