@@ -90,6 +90,39 @@ __global__ void split_a_kernel(const float* __restrict__ A, float* __restrict__ 
   }
 }
 
+// The same split with 16-byte accesses (K % 4 == 0, A 16-byte aligned): a
+// thread per 4 consecutive k of a row, the row found by a multiply-shift
+// division by Kp / 4 (a launch constant) instead of a 64-bit division per
+// element, which made the scalar pass issue-bound (16384^2: ~6 ms).
+__global__ void __launch_bounds__(256) split_a4_kernel(const float* __restrict__ A,
+                                                       float* __restrict__ Ap, int64_t rows,
+                                                       int64_t K, int64_t Kp, FastDiv fd_q,
+                                                       unsigned int* rowtag, unsigned int* tagany,
+                                                       unsigned int gen) {
+  const int64_t q = Kp / 4;
+  const int64_t total = rows * q;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = fdiv(i, fd_q);
+    const int64_t k = (i - r * q) * 4;
+    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (k < K) v = __ldg(reinterpret_cast<const float4*>(A + r * K + k));
+    float4 h, l;
+    bool t = split(v.x, h.x, l.x);
+    t |= split(v.y, h.y, l.y);
+    t |= split(v.z, h.z, l.z);
+    t |= split(v.w, h.w, l.w);
+    if (t) {
+      rowtag[r] = gen;
+      tagany[0] = gen;
+    }
+    float4* o = reinterpret_cast<float4*>(Ap + r * 3 * Kp + k);
+    o[0] = l;
+    o[Kp / 4] = h;
+    o[Kp / 2] = h;
+  }
+}
+
 // B (nmat x K x N) -> B't, transposed to K-major through shared memory.
 // SEGS = 3 writes [hi | lo | hi] (nmat*N x 3Kp, for the pre-split GEMM),
 // SEGS = 2 writes [hi | lo] (nmat*N x 2Kp, for the GEMM that splits A in
@@ -1474,8 +1507,16 @@ int gemm_f32_algo(Device* d, const BatchMap& map, int64_t batch, int64_t M, int6
     int64_t blocks = ceil_div(total, (int64_t)256);
     const int64_t cap = (int64_t)d->sm_count * 16;
     if (blocks > cap) blocks = cap;
-    split_a_kernel<<<(unsigned)blocks, 256, 0, d->stream>>>(A, Ap, rows_a, K, Kp, p.rowtag,
-                                                            p.tagany, p.gen);
+    if (K % 4 == 0 && (uintptr_t)A % 16 == 0 && rows_a * (Kp / 4) < (int64_t(1) << 31)) {
+      int64_t b4 = ceil_div(rows_a * (Kp / 4), (int64_t)256);
+      if (b4 > cap) b4 = cap;
+      split_a4_kernel<<<(unsigned)b4, 256, 0, d->stream>>>(A, Ap, rows_a, K, Kp,
+                                                           make_fastdiv(Kp / 4), p.rowtag,
+                                                           p.tagany, p.gen);
+    } else {
+      split_a_kernel<<<(unsigned)blocks, 256, 0, d->stream>>>(A, Ap, rows_a, K, Kp, p.rowtag,
+                                                              p.tagany, p.gen);
+    }
     PB_LAUNCHED(d);
     const int64_t gx = ceil_div(N, (int64_t)SPLIT_TN), gy = Kp / SPLIT_TK;
     if (gx > INT32_MAX || gy > 65535 || nB > 65535)
