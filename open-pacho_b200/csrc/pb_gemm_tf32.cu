@@ -27,6 +27,17 @@
 
 #include "pb_internal.cuh"
 
+// Build parameters of the 3xTF32 kernels (each measured on and off).
+#ifndef PB_TF32_SPLIT_EARLY
+#define PB_TF32_SPLIT_EARLY 1  // split A into registers before waiting for its TMEM buffer
+#endif
+#ifndef PB_TF32_WARM
+#define PB_TF32_WARM 0  // 1: warm the launch parameters and prefetch the tensor maps at entry
+#endif
+#ifndef PB_TF32_PROMOTE_BATCH
+#define PB_TF32_PROMOTE_BATCH 1  // several accumulator loads per wait; 16 warps at FBN = 128
+#endif
+
 namespace pb {
 
 int gemm_simt_f32(Device* d, const BatchMap& map, int64_t batch, int64_t M, int64_t N, int64_t K,
@@ -330,6 +341,20 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "memory");
 }
 
+// Three 16-column loads in flight before one wait.
+__device__ __forceinline__ void tmem_ld16x3(uint32_t ta, uint32_t (&a)[48]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%48];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%49];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47}, [%50];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(a[0]),"=r"(a[1]),"=r"(a[2]),"=r"(a[3]),"=r"(a[4]),"=r"(a[5]),"=r"(a[6]),"=r"(a[7]),"=r"(a[8]),"=r"(a[9]),"=r"(a[10]),"=r"(a[11]),"=r"(a[12]),"=r"(a[13]),"=r"(a[14]),"=r"(a[15]),
+        "=r"(a[16]),"=r"(a[17]),"=r"(a[18]),"=r"(a[19]),"=r"(a[20]),"=r"(a[21]),"=r"(a[22]),"=r"(a[23]),"=r"(a[24]),"=r"(a[25]),"=r"(a[26]),"=r"(a[27]),"=r"(a[28]),"=r"(a[29]),"=r"(a[30]),"=r"(a[31]),
+        "=r"(a[32]),"=r"(a[33]),"=r"(a[34]),"=r"(a[35]),"=r"(a[36]),"=r"(a[37]),"=r"(a[38]),"=r"(a[39]),"=r"(a[40]),"=r"(a[41]),"=r"(a[42]),"=r"(a[43]),"=r"(a[44]),"=r"(a[45]),"=r"(a[46]),"=r"(a[47])
+      : "r"(ta), "r"(ta + 16u), "r"(ta + 32u)
+      : "memory");
+}
+
 // Two 32-column loads in flight before one wait.
 __device__ __forceinline__ void tmem_ld32x2(uint32_t ta, uint32_t tb, uint32_t (&a)[32],
                                             uint32_t (&b)[32]) {
@@ -449,6 +474,29 @@ __device__ __forceinline__ TileCoord tile_coord(const Tf32Params& p, int64_t t) 
   return c;
 }
 
+// First reads of the launch parameters miss the constant cache in a chain of
+// dependent loads (~1.8 us before the first TMA when measured with
+// %globaltimer stamps).  One otherwise idle lane computes its CTA's first work
+// item during set-up -- before the programmatic-launch wait, so under a
+// preceding kernel's tail -- which brings those lines into the cache for every
+// warp; the tensor maps are prefetched likewise.  The result is only kept
+// alive through a shared-memory word.
+__device__ __forceinline__ void warm_params(const Tf32Params& p, volatile int* sink) {
+  int64_t tile;
+  int split;
+  item_of(p, blockIdx.x, tile, split);
+  const TileCoord tc = tile_coord(p, tile);
+  int kb0, kb1;
+  split_range(p, split, kb0, kb1);
+  int64_t ao, bo;
+  batch_offsets(p.map, tc.bz, &ao, &bo);
+  *sink = (int)(ao + bo + kb0 + kb1 + tc.m_tile + tc.n_tile + p.gen + (int)p.M + (int)p.N);
+}
+
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
 // Above these K a flagged output is not recomputed where it is written but
 // its tile is marked for the tiled repair launch: in the epilogue the
 // pipeline waits for the recomputation (bounded by kTimeoutNs); in the
@@ -565,7 +613,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (PB_TF32_WARM) {
+      prefetch_map(&map_a);
+      prefetch_map(&map_b);
+    }
   }
+  if (PB_TF32_WARM && warp == 2 && lane == 0) warm_params(p, abort_flag + 1);
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
@@ -762,17 +815,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 constexpr int FCHUNK = PB_TF32_FCHUNK;
 constexpr int T_SPLIT_WARPS = 4, T_ACC_WARPS = 8;
 
-// Warp roles by tile width.  FBN = 64 / 128: 14 warps (TMA, MMA, split 2..5,
+// Warp roles by tile width.  FBN = 64: 14 warps (TMA, MMA, split 2..5,
 // promote/store 6..13) at the 128 registers a thread that 14 warps leave (the
-// register file is split over the SM's four sub-partitions).  FBN = 192: the
-// promote warps hold 96 running sums each, so 16 warps are launched at 128
-// registers as four warp groups -- {TMA, MMA, two idle}, {split x4},
-// {promote/store x4} x 2 -- and after set-up the first two groups give
-// registers up for the last two (setmaxnreg): 64 + 96 + 176 + 176 = 512 =
-// 4 x 128, so the increase is always available.
+// register file is split over the SM's four sub-partitions).  FBN = 128 / 192:
+// the promote warps hold 64 / 96 running sums each plus the accumulator
+// columns in flight, so 16 warps are launched at 128 registers as four warp
+// groups -- {TMA, MMA, two idle}, {split x4}, {promote/store x4} x 2 -- and
+// after set-up the first two groups give registers up for the last two
+// (setmaxnreg): 64 + 96 + 176 + 176 = 512 = 4 x 128, so the increase is
+// always available.
 template <int FBN>
 struct TRoles {
-  static constexpr bool kRegs = FBN == 192;
+  static constexpr bool kRegs = PB_TF32_PROMOTE_BATCH ? FBN >= 128 : FBN == 192;
   static constexpr int SPLIT0 = kRegs ? 4 : 2;        // first A-split warp
   static constexpr int ACC0 = SPLIT0 + T_SPLIT_WARPS;  // first promote/store warp
   static constexpr int THREADS = 32 * (ACC0 + T_ACC_WARPS);
@@ -833,13 +887,15 @@ __device__ __forceinline__ void umma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, u
       "r"(tmem_a), "l"(b), "r"(idesc), "r"(accumulate));
 }
 
-// 16 consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+// 32 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(
           taddr),
       "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+      "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+      "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
 }
 
@@ -859,6 +915,9 @@ __device__ __forceinline__ void store_tma(const Tf32Params& p, const CUtensorMap
   const int64_t row = tc.m_tile * BM + quad * 32 + lane;
   const int64_t batch = p.batch;
   const int32_t z = (int32_t)(p.ksplit > 1 ? split * batch + tc.bz : tc.bz);
+  // The launch's tag word, read before the staging work so its L2 round trip
+  // overlaps it.
+  const unsigned int any = p.ksplit == 1 ? __ldcg(p.tagany) : 0u;
   bool bad = false;
   if (p.ksplit == 1 && row < p.M) {
 #pragma unroll
@@ -880,7 +939,7 @@ __device__ __forceinline__ void store_tma(const Tf32Params& p, const CUtensorMap
                    z);
   }
   if (p.ksplit > 1) return;
-  if (row < p.M && __ldcg(p.tagany) == p.gen) bad |= tagged<COLS>(p, tc.bz, row, col0);
+  if (row < p.M && any == p.gen) bad |= tagged<COLS>(p, tc.bz, row, col0);
   if (__any_sync(0xffffffffu, bad)) {
     if (lane == 0) bulk_wait_all();
     __syncwarp();
@@ -929,7 +988,13 @@ __global__ void __launch_bounds__(TRoles<FBN>::THREADS, 1)
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (PB_TF32_WARM) {
+      prefetch_map(&map_a);
+      prefetch_map(&map_b);
+      if (p.tma_store) prefetch_map(&map_c);
+    }
   }
+  if (PB_TF32_WARM && warp == 2 && lane == 0) warm_params(p, abort_flag + 1);
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
@@ -941,11 +1006,14 @@ __global__ void __launch_bounds__(TRoles<FBN>::THREADS, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   const int64_t items = p.tiles * p.ksplit;
-  // Launched as a programmatic dependent of the split pass: the prologue above
-  // overlapped its tail; nothing it wrote is read before this wait.  The next
-  // launch (split reduction or repair) may be scheduled from now on; it waits
-  // for this grid in turn.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // Launched as a programmatic dependent of the split pass.  Each role waits
+  // for the preceding grid (griddepcontrol.wait) only right before its first
+  // access to memory that grid may write -- the producer before its first TMA
+  // load, the promote/store warps before their first global access, the split
+  // warps before writing a tag -- so the set-up and the first work item's
+  // bookkeeping (about 2 us when cold) overlap the preceding grid's tail.  The
+  // next launch (split reduction or repair) may be scheduled from now on; it
+  // waits for this grid in turn.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
@@ -968,6 +1036,7 @@ __global__ void __launch_bounds__(TRoles<FBN>::THREADS, 1)
           const int s = (int)(g % S);
           if (!mbar_wait(empty0 + 8 * s, (uint32_t)(((g / S) & 1) ^ 1), abort_flag, p.err)) break;
           const uint32_t st = base + s * L::STAGE;
+          if (g == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
           mbar_expect_tx(full0 + 8 * s, L::STAGE);
           tma_load_2d(st + L::A, &map_a, kb * BK, a_row, full0 + 8 * s);
           tma_load_2d(st + L::BHI, &map_b, kb * BK, b_row, full0 + 8 * s);
@@ -1051,37 +1120,49 @@ __global__ void __launch_bounds__(TRoles<FBN>::THREADS, 1)
       for (int kb = kb0; kb < kb1; ++kb, ++g) {
         const int s = (int)(g % S);
         bool got = mbar_wait(full0 + 8 * s, (uint32_t)((g / S) & 1), abort_flag, p.err);
-        // The TMEM buffer of this slice was last read by the MMAs of slice
-        // g - TS (with TS == S the full barrier above already implies it).
-        const int t = (int)(g % TS);
-        if (kTfree && got)
-          got = mbar_wait(tfree0 + 8 * t, (uint32_t)(((g / TS) & 1) ^ 1), abort_flag, p.err);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        // Split the landed slice into registers first: only the TMEM stores
+        // wait for the buffer, so the loads and arithmetic stay out of the
+        // chain "MMAs of slice g - TS done -> split g -> MMAs of g".
         // This lane's row is 128 bytes; the 128-byte swizzle stores its 16-byte
         // chunk j at position j ^ (row % 8).
         const float4* src = reinterpret_cast<const float4*>(gbase + s * L::STAGE + L::A + row * 128);
-        const uint32_t acol = tmem + lane_off + L::ACOL + 64u * (uint32_t)t;
-        float amin = FLT_MAX;  // smallest magnitude of the row's 32 values (NaN ignored)
-        __syncwarp();  // converged for the .aligned TMEM stores
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t hi[16], lo[16];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float4 v = src[(4 * h + q) ^ (row & 7)];
-            split_bits(v.x, hi[4 * q], lo[4 * q]);
-            split_bits(v.y, hi[4 * q + 1], lo[4 * q + 1]);
-            split_bits(v.z, hi[4 * q + 2], lo[4 * q + 2]);
-            split_bits(v.w, hi[4 * q + 3], lo[4 * q + 3]);
-            amin = fminf(amin, fminf(fminf(fabsf(v.x), fabsf(v.y)), fminf(fabsf(v.z), fabsf(v.w))));
+        const int t = (int)(g % TS);
+        if (kTfree && !PB_TF32_SPLIT_EARLY) {
+          got = mbar_wait(tfree0 + 8 * t, (uint32_t)(((g / TS) & 1) ^ 1), abort_flag, p.err);
+          if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            break;
           }
-          tmem_st16(acol + 16u * h, hi);
-          tmem_st16(acol + 32u + 16u * h, lo);
         }
+        float amin = FLT_MAX;  // smallest magnitude of the row's 32 values (NaN ignored)
+        uint32_t hi[32], lo[32];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 v = src[q ^ (row & 7)];
+          split_bits(v.x, hi[4 * q], lo[4 * q]);
+          split_bits(v.y, hi[4 * q + 1], lo[4 * q + 1]);
+          split_bits(v.z, hi[4 * q + 2], lo[4 * q + 2]);
+          split_bits(v.w, hi[4 * q + 3], lo[4 * q + 3]);
+          amin = fminf(amin, fminf(fminf(fabsf(v.x), fabsf(v.y)), fminf(fabsf(v.z), fabsf(v.w))));
+        }
+        // The TMEM buffer of this slice was last read by the MMAs of slice
+        // g - TS (with TS == S the full barrier above already implies it).
+        if (kTfree && PB_TF32_SPLIT_EARLY) {
+          got = mbar_wait(tfree0 + 8 * t, (uint32_t)(((g / TS) & 1) ^ 1), abort_flag, p.err);
+          if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            break;
+          }
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t acol = tmem + lane_off + L::ACOL + 64u * (uint32_t)t;
+        __syncwarp();  // converged for the .aligned TMEM stores
+        tmem_st32(acol, hi);
+        tmem_st32(acol + 32u, lo);
         if (amin < kTinyMag) {
           // A zero or tiny value: tag the row if one of the 32 is tiny.
           bool tagged_row = false;
@@ -1091,6 +1172,7 @@ __global__ void __launch_bounds__(TRoles<FBN>::THREADS, 1)
             tagged_row |= tiny(v.x) | tiny(v.y) | tiny(v.z) | tiny(v.w);
           }
           if (tagged_row) {
+            asm volatile("griddepcontrol.wait;" ::: "memory");
             p.rowtag[arow] = p.gen;
             p.tagany[0] = p.gen;
             __threadfence();
@@ -1106,6 +1188,7 @@ __global__ void __launch_bounds__(TRoles<FBN>::THREADS, 1)
   } else if (warp >= R::ACC0) {
     // ------------------- promote and store (warps 6..13, or 8..15)
     if constexpr (R::kRegs) reg_alloc<R::REG_ACC>();
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // before any global access
     // Every FCHUNK slices the MMA thread commits a chunk of the tile into one
     // of the two TMEM accumulators; these warps add it into fp32 registers,
     // free the accumulator, and at the end of the work item store the tile.
@@ -1127,17 +1210,29 @@ __global__ void __launch_bounds__(TRoles<FBN>::THREADS, 1)
         ok = false;
         return;
       }
-      // One piece at a time (these warps are off the critical path; two
-      // pieces in flight would not fit the register cap of 14 warps): 32
-      // columns, or 16 where the running sums themselves take 96 registers.
-      constexpr int PIECE = COLS > 64 ? 16 : 32;
+      // Several loads in flight per wait: each wait is a full round trip
+      // through tensor memory, slowed by the MMAs' own traffic there, and the
+      // next chunk's MMAs wait for this buffer.  With the registers moved to
+      // these warps (TRoles::kRegs): 64 columns per wait (two 32-column
+      // loads) for 64 running sums, 48 (three 16-column loads) for 96; else
+      // one 32-column load per wait.
+      constexpr int PIECE = !PB_TF32_PROMOTE_BATCH ? (COLS > 64 ? 16 : 32)
+                            : COLS == 96 ? 48 : (COLS == 64 && R::kRegs) ? 64 : 32;
 #pragma unroll
       for (int piece = 0; piece < COLS / PIECE; ++piece) {
         uint32_t r[PIECE];
-        if constexpr (PIECE == 32)
-          tmem_ld32(acc_base + (uint32_t)(buf * FBN + piece * 32), r);
-        else
-          tmem_ld16(acc_base + (uint32_t)(buf * FBN + piece * 16), r);
+        const uint32_t ta = acc_base + (uint32_t)(buf * FBN + piece * PIECE);
+        if constexpr (PIECE == 16) {
+          tmem_ld16(ta, r);
+        } else if constexpr (PIECE == 48) {
+          tmem_ld16x3(ta, r);
+        } else if constexpr (PIECE == 64) {
+          uint32_t (&lo32)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[0]);
+          uint32_t (&hi32)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[32]);
+          tmem_ld32x2(ta, ta + 32u, lo32, hi32);
+        } else {
+          tmem_ld32(ta, r);
+        }
 #pragma unroll
         for (int i = 0; i < PIECE; ++i)
           acc[piece * PIECE + i] =
