@@ -907,10 +907,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32
 // partial plane (z = split * batch + bz).  Flagged outputs are recomputed after
 // the warp's stores complete.
 template <int COLS>
+// `boxes_room`: staging buffers of 4 KiB at `stage` (1, or COLS/32 when the
+// CTA's operand ring is idle -- its last work item): with one, each box
+// waits for the previous one to leave the buffer; with one per box, all
+// boxes are staged first and stored back to back.
 __device__ __forceinline__ void store_tma(const Tf32Params& p, const CUtensorMap* map_c,
                                           const TileCoord& tc, int split, int quad, int64_t col0,
                                           const float (&acc)[COLS], float4* stage,
-                                          uint32_t stage_u32) {
+                                          uint32_t stage_u32, bool boxes_room = false) {
   const int lane = threadIdx.x & 31;
   const int64_t row = tc.m_tile * BM + quad * 32 + lane;
   const int64_t batch = p.batch;
@@ -925,17 +929,21 @@ __device__ __forceinline__ void store_tma(const Tf32Params& p, const CUtensorMap
   }
 #pragma unroll
   for (int c = 0; c < COLS / 32; ++c) {
-    if (lane == 0) bulk_wait_read();  // the previous box has left the buffer
-    __syncwarp();
+    float4* box = boxes_room ? stage + c * 256 : stage;  // 256 float4 = 4 KiB
+    const uint32_t box_u32 = boxes_room ? stage_u32 + c * 4096u : stage_u32;
+    if (!boxes_room) {
+      if (lane == 0) bulk_wait_read();  // the previous box has left the buffer
+      __syncwarp();
+    }
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      stage[lane * 8 + (j ^ (lane & 7))] =
+      box[lane * 8 + (j ^ (lane & 7))] =
           make_float4(acc[c * 32 + 4 * j], acc[c * 32 + 4 * j + 1], acc[c * 32 + 4 * j + 2],
                       acc[c * 32 + 4 * j + 3]);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
     if (lane == 0)
-      tma_store_3d(map_c, stage_u32, (int32_t)(col0 + c * 32), (int32_t)(tc.m_tile * BM + quad * 32),
+      tma_store_3d(map_c, box_u32, (int32_t)(col0 + c * 32), (int32_t)(tc.m_tile * BM + quad * 32),
                    z);
   }
   if (p.ksplit > 1) return;
@@ -1256,9 +1264,17 @@ __global__ void __launch_bounds__(TRoles<FBN>::THREADS, 1)
       const TileCoord tc = tile_coord(p, tile);
       const int64_t col0 = tc.n_tile * FBN + half * COLS;
       if (p.tma_store)
+      {
+        // The CTA's last work item: no TMA load is outstanding and every MMA
+        // has completed (the last chunk's commit covers them all), so the
+        // operand ring can stage all of this warp's boxes.
+        const bool last = w + (int64_t)gridDim.x >= items;
+        const uint32_t off = last ? (uint32_t)((warp - R::ACC0) * (COLS / 32) * 4096)
+                                  : (uint32_t)(L::OUT + (warp - R::ACC0) * 4096);
+        static_assert(T_ACC_WARPS * (COLS / 32) * 4096 <= L::OUT, "ring holds every box");
         store_tma<COLS>(p, &map_c, tc, split, quad, col0, acc,
-                        reinterpret_cast<float4*>(gbase + L::OUT + (warp - R::ACC0) * 4096),
-                        base + L::OUT + (warp - R::ACC0) * 4096);
+                        reinterpret_cast<float4*>(gbase + off), base + off, last);
+      }
       else
         finish_item<COLS>(p, tc, split, tc.m_tile * BM + row, col0, acc);
     }
