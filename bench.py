@@ -326,19 +326,35 @@ class Gpu:
         self.check(self.raw.pb_timer_stop(self.ctx, 0, C.byref(ms)), "timer")
         return ms.value / 1e3
 
-    def kernel_seconds(self, fn, reps):
+    def kernel_seconds(self, fn, reps, graph=False):
         """Average duration of the main kernel of `fn` (CUDA events around each
-        launch on the library's stream) and the launches seen."""
+        launch on the library's stream) and the launches seen.  With `graph`,
+        `fn` is captured with the events inside the graph and replayed `reps`
+        times, so the host's submission gaps between an event and its kernel
+        cannot enter the time."""
         self.sync()
-        self.check(self.raw.pb_ktimer_enable(self.ctx, 0, 1), "ktimer")
+        total, count = C.c_double(), C.c_uint64()
+        if not graph:
+            self.check(self.raw.pb_ktimer_enable(self.ctx, 0, 1), "ktimer")
+            try:
+                for _ in range(reps):
+                    fn()
+                self.check(self.raw.pb_ktimer_read(self.ctx, 0, C.byref(total), C.byref(count)), "ktimer")
+            finally:
+                self.raw.pb_ktimer_enable(self.ctx, 0, 0)
+            return (total.value / 1e3 / count.value if count.value else None), count.value
+        self.check(self.raw.pb_ktimer_enable(self.ctx, 0, 2), "ktimer")
         try:
-            for _ in range(reps):
-                fn()
-            total, count = C.c_double(), C.c_uint64()
-            self.check(self.raw.pb_ktimer_read(self.ctx, 0, C.byref(total), C.byref(count)), "ktimer")
+            with self.backend.capture(fn) as g:
+                ms, launches = 0.0, 0
+                for _ in range(reps):
+                    g.launch()
+                    self.check(self.raw.pb_ktimer_read(self.ctx, 0, C.byref(total), C.byref(count)), "ktimer")
+                    ms += total.value
+                    launches += count.value
         finally:
             self.raw.pb_ktimer_enable(self.ctx, 0, 0)
-        return (total.value / 1e3 / count.value if count.value else None), count.value
+        return (ms / 1e3 / launches if launches else None), launches
 
     def launches(self):
         return self.backend.launch_count()
@@ -430,6 +446,11 @@ class Workload:
     kernel_key = ""
     main_launches = 1
     extra: dict = {}
+
+    def graphable(self):
+        """Whether one step can be captured into a CUDA graph (no exchange
+        whose sequence numbers advance per call, nothing allocated)."""
+        return True
 
     def scale(self):
         return 1e12 if self.unit == "TFLOP/s" else 1e9
@@ -689,8 +710,8 @@ class GemvDot(Workload):
     def kernel_step(self):
         self.gemv()
 
-    def more_kernels(self):
-        t, _ = self.gpu.kernel_seconds(self.dot, self.args.steps)
+    def more_kernels(self, graph=False):
+        t, _ = self.gpu.kernel_seconds(self.dot, self.args.steps, graph=graph)
         return {"gemv_gbs": None, "dot_ms": t * 1e3, "dot_gbs": self.bytes_dot / t / 1e9}
 
     def e2e_setup(self):
@@ -785,6 +806,11 @@ class Norm(Workload):
             self.kernel_key = f"norm_{self.dtype}:norm"
         self.dx = gpu.upload(self.xl)
         self.units = self.kernel_units = float(self.xl.nbytes)
+
+    def graphable(self):
+        # The sharded full norm exchanges through the peer mailboxes (or NCCL),
+        # whose sequence numbers advance with every call.
+        return self.rows_mode or not self.comm.active
 
     def step(self):
         g = self.gpu
@@ -1012,20 +1038,51 @@ def measure(w: Workload, gpu: Gpu, comm: Comm, args, dist: Dist, pk: dict) -> di
     for _ in range(args.warmup):
         w.step()
     gpu.sync()
-    dist.barrier()
-    with Clocks(gpu.backend.ordinal) as clocks:
-        gpu.busy(w.step, dist)
+    # One step captured into a CUDA graph and replayed (after the eager
+    # warm-up has sized every internal buffer), unless it cannot be captured.
+    # Every rank decides the same way: the steps may hold collectives.
+    # With --launch auto the faster of the two is chosen on a short
+    # calibration (max over ranks) before the timed region: a graph replay
+    # saves the host's per-launch cost, eager launches keep the overlap of one
+    # step's first kernel with the previous step's last (programmatic
+    # dependent launch), which the boundary between two replays does not.
+    use_graph = args.launch != "eager" and dist.max(0.0 if w.graphable() else 1.0) == 0.0
+    graph = gpu.backend.capture(w.step) if use_graph else None
+    alt = None
+    try:
+        if graph:
+            calib = max(3, min(args.steps, 20))
+            for _ in range(2):
+                graph.launch()
+            t_graph = dist.max(gpu.timer(graph.launch, calib))
+            t_eager = dist.max(gpu.timer(w.step, calib))
+            replay = not (args.launch == "auto" and t_eager < t_graph)
+            alt = (("eager launches through the C ABI", w.step) if replay else
+                   ("one step captured as a CUDA graph, replayed each step", graph.launch))
+        else:
+            replay = False
+        step = graph.launch if replay else w.step
+        gpu.sync()
         dist.barrier()
-        l0 = gpu.launches()
-        seconds = gpu.timer(w.step, args.steps)
-        launches = gpu.launches() - l0
+        with Clocks(gpu.backend.ordinal) as clocks:
+            gpu.busy(step, dist)
+            dist.barrier()
+            l0 = gpu.launches()
+            seconds = gpu.timer(step, args.steps)
+            launches = graph.launches * args.steps if replay else gpu.launches() - l0
+        if alt:
+            dist.barrier()
+            alt = (alt[0], dist.max(gpu.timer(alt[1], args.steps)))
+    finally:
+        if graph:
+            graph.close()
     seconds = dist.max(seconds)
     total_units = dist.sum(w.units)
 
     # Main kernel alone (events around each launch), max over ranks.
-    kt, kl = gpu.kernel_seconds(w.kernel_step, args.steps)
+    kt, kl = gpu.kernel_seconds(w.kernel_step, args.steps, graph=use_graph)
     kt = dist.max(kt or 0.0)
-    more = w.more_kernels() if hasattr(w, "more_kernels") else {}
+    more = w.more_kernels(use_graph) if hasattr(w, "more_kernels") else {}
 
     # End to end through the C ABI with pinned host buffers.
     w.e2e_setup()
@@ -1048,6 +1105,13 @@ def measure(w: Workload, gpu: Gpu, comm: Comm, args, dist: Dist, pk: dict) -> di
         "ms_per_step": seconds / args.steps * 1e3, "scaling": w.scaling, "dtype": w.dtype,
         "config": w.config(), "clocks": clocks.summary(), "gpu_launches": launches,
     }
+    rec["config"]["launch"] = ("one step captured as a CUDA graph, replayed each step" if replay
+                               else "eager launches through the C ABI")
+    if graph:
+        rec["config"]["launch_choice"] = args.launch
+    if alt:
+        rec["other_launch_mode"] = {"launch": alt[0], "value": total_units * args.steps / alt[1] / scale,
+                                    "ms_per_step": alt[1] / args.steps * 1e3}
     rec["roofline"] = roofline(w, kt, pk)
     rec["kernel_ms"] = kt * 1e3
     if more:
@@ -1186,8 +1250,13 @@ class Residual(Workload):
         g.check(g.raw.pb_elementwise(g.ctx, 0, L.EW_OPS["subtract"], 2, ptrs, codes, L.i64_array([1, 1]), 1,
                                      L.i64_array([16384]), L.PB_F32, p_(self.dy)), "subtract")
 
-    def more_kernels(self):
-        t = self.gpu.timer(self.unfused, self.args.steps) / self.args.steps
+    def more_kernels(self, graph=False):
+        if graph:
+            self.unfused()
+            with self.gpu.backend.capture(self.unfused) as g:
+                t = self.gpu.timer(g.launch, self.args.steps) / self.args.steps
+        else:
+            t = self.gpu.timer(self.unfused, self.args.steps) / self.args.steps
         return {"unfused_gemv_then_subtract_ms": t * 1e3,
                 "unfused_bytes": 4.0 * (16384 * 16384 + 2 * 16384 + 16384) + 12.0 * 16384,
                 "fused_bytes": self.units}
@@ -1362,6 +1431,9 @@ def main(argv=None):
     parser.add_argument("--n", type=int, default=0,
                         help="GEMM / vecmat / around-path size override (profiling captures); 0 = BASELINE")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--launch", choices=("auto", "graph", "eager"), default="auto",
+                        help="replay each step as a captured CUDA graph, launch it eagerly, or "
+                             "take the faster of the two on a calibration run (auto)")
     args = parser.parse_args(argv)
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")

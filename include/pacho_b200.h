@@ -125,9 +125,33 @@ int pb_launch_count(pb_ctx* ctx, int dev, uint64_t* count);
  * the last enable/read, and starts a new count.  At most 4096 launches are
  * kept between reads (PB_ERR_UNSUPPORTED beyond).  An event between two
  * chained launches serialises them, so time the whole step with the timer off.
- * No counterpart in the reference. */
+ * enable = 2 is for a captured step: the event pairs become nodes of the graph,
+ * each replay re-records them, and a read returns the last replay's times
+ * without starting a new count.  No counterpart in the reference. */
 int pb_ktimer_enable(pb_ctx* ctx, int dev, int enable);
 int pb_ktimer_read(pb_ctx* ctx, int dev, double* total_ms, uint64_t* launches);
+/* CUDA graphs of hot-path calls.  pb_capture_begin starts a (relaxed) capture
+ * of the device stream; the entry points called until pb_capture_end are
+ * recorded, not run, and pb_capture_end returns an instantiated graph that
+ * pb_graph_launch replays on the device stream (same pointers, shapes and
+ * scalars as captured; the data in the buffers is read afresh every replay).
+ * During a capture, calls that synchronise, allocate, free or grow the
+ * context's internal buffers, and the sharded mailbox / NCCL exchanges, fail
+ * with PB_ERR_UNSUPPORTED: make one uncaptured call of the same shapes first so
+ * the buffers have their size.  A failed call leaves the capture open; end it
+ * with pb_capture_end (which may then fail) before anything else.  While any
+ * graph lives, buffers that grow are kept until the last graph is destroyed,
+ * and pb_trim is refused.  Destroy graphs before pb_shutdown.  A 3xTF32 GEMM
+ * replays the operand generation it was captured with, so an operand row or
+ * column group that held a tiny value (nonzero, below 2^-57) in an earlier
+ * replay stays on the float32-FMA recompute in later ones (within the same
+ * error bound, slower) until the graph is captured again.  No counterpart in
+ * the reference,
+ * whose CUDA backend launches eagerly (src/openpacho/_cuda.py). */
+int pb_capture_begin(pb_ctx* ctx, int dev);
+int pb_capture_end(pb_ctx* ctx, int dev, void** graph);
+int pb_graph_launch(pb_ctx* ctx, int dev, void* graph);
+int pb_graph_destroy(pb_ctx* ctx, int dev, void* graph);
 /* Device memory in use by this context on `dev`: bytes the stream-ordered
  * pool holds reserved from the driver and in use, the size of the context's
  * grow-only scratch buffer, and the device's free memory (cudaMemGetInfo).

@@ -241,6 +241,9 @@ int pb_norm_sharded(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, v
   Device* d;
   PB_CHECK(enter(ctx, dev, &d));
   if (n > 0 && !x) PB_FAIL(PB_ERR_INVALID, "null input");
+  if (d->capturing)
+    PB_FAIL(PB_ERR_UNSUPPORTED, "the sharded norm cannot be captured: its exchange advances "
+                                "sequence numbers and allocates with every call");
   // With peer mailboxes mapped: push over NVLink from the norm kernel itself.
   if (d->box_ranks > 1) return norm_sharded_p2p(d, dtype, n, x, out);
   PB_CHECK(need_comm(d));

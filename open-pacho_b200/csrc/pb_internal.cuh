@@ -88,7 +88,8 @@ struct Device {
   int* err_dev = nullptr;
   cudaEvent_t t0 = nullptr, t1 = nullptr;
   std::atomic<uint64_t> launches{0};
-  // Per-kernel timer (pb_ktimer_*): event pairs around main kernels while on.
+  // Per-kernel timer (pb_ktimer_*): event pairs around main kernels while on
+  // (1), or on with the pairs kept across reads (2: events inside a graph).
   int kt_on = 0;
   size_t kt_used = 0;
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> kt_events;
@@ -105,6 +106,12 @@ struct Device {
   int box_ranks = 0, box_rank = 0;
   unsigned long long box_seq = 0;
   unsigned long long box_wait_ns = 10ull * 1000 * 1000 * 1000;  // mailbox wait limit
+  // A stream capture (pb_capture_begin) is in progress: nothing may allocate.
+  int capturing = 0;
+  // Instantiated graphs not yet destroyed.  While any lives, a buffer that
+  // grows is retired (kept) instead of freed: a graph may still use it.
+  int graphs_live = 0;
+  std::vector<void*> retired;
 };
 
 }  // namespace pb

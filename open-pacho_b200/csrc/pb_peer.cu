@@ -161,6 +161,9 @@ int pb_dot_sharded(pb_ctx* ctx, int dev, int dtype, int64_t n, const void* x, co
   Device* d;
   PB_CHECK(enter(ctx, dev, &d));
   if (d->box_ranks < 2) PB_FAIL(PB_ERR_INVALID, "no peer mailboxes; call pb_peer_export/import");
+  if (d->capturing)
+    PB_FAIL(PB_ERR_UNSUPPORTED, "the mailbox exchange cannot be captured: its sequence numbers "
+                                "advance with every call");
   PB_CHECK(dot_device(d, dtype, n, x, y, out));  // local partial into out
   const unsigned long long seq = ++d->box_seq;
   const PushArgs a = push_args(d, seq);

@@ -33,9 +33,31 @@ int enter(pb_ctx* ctx, int dev, Device** out) {
   return PB_OK;
 }
 
+// During a stream capture nothing may allocate: a call that would grow a
+// buffer fails and asks for one uncaptured call of the same shape first.
+#define PB_NO_GROWTH_IN_CAPTURE(d)                                                          \
+  do {                                                                                      \
+    if ((d)->capturing)                                                                     \
+      PB_FAIL(PB_ERR_UNSUPPORTED,                                                           \
+              "a buffer would grow during stream capture: make one uncaptured call of the " \
+              "same shape first");                                                          \
+  } while (0)
+
+// Frees a library buffer, or keeps it until the last graph is destroyed.
+static int release_buffer(Device* d, void* p) {
+  if (!p) return PB_OK;
+  if (d->graphs_live > 0) {
+    d->retired.push_back(p);
+    return PB_OK;
+  }
+  PB_CUDA(cudaFreeAsync(p, d->stream));
+  return PB_OK;
+}
+
 int scratch(Device* d, size_t bytes, void** out) {
   if (bytes > d->scratch_bytes) {
-    if (d->scratch) PB_CUDA(cudaFreeAsync(d->scratch, d->stream));
+    PB_NO_GROWTH_IN_CAPTURE(d);
+    PB_CHECK(release_buffer(d, d->scratch));
     d->scratch = nullptr;
     d->scratch_bytes = 0;
     size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
@@ -48,7 +70,8 @@ int scratch(Device* d, size_t bytes, void** out) {
 
 int counters(Device* d, size_t n, unsigned int** out) {
   if (n > d->counters_n) {
-    if (d->counters) PB_CUDA(cudaFreeAsync(d->counters, d->stream));
+    PB_NO_GROWTH_IN_CAPTURE(d);
+    PB_CHECK(release_buffer(d, d->counters));
     d->counters = nullptr;
     d->counters_n = 0;
     size_t want = n < 4096 ? 4096 : n;
@@ -63,9 +86,10 @@ int counters(Device* d, size_t n, unsigned int** out) {
 
 int operand_tags(Device* d, size_t n, unsigned int** out, unsigned int* gen) {
   if (n > d->tags_n || d->tag_gen == UINT32_MAX) {
+    PB_NO_GROWTH_IN_CAPTURE(d);
     const size_t want = n > d->tags_n ? (n < 65536 ? 65536 : n) : d->tags_n;
     if (want > d->tags_n) {
-      if (d->tags) PB_CUDA(cudaFreeAsync(d->tags, d->stream));
+      PB_CHECK(release_buffer(d, d->tags));
       d->tags = nullptr;
       d->tags_n = 0;
       PB_CUDA(cudaMallocAsync((void**)&d->tags, want * sizeof(unsigned int), d->pool, d->stream));
@@ -95,13 +119,16 @@ int kt_begin(Device* d) {
     }
     d->kt_events.emplace_back(a, b);
   }
-  PB_CUDA(cudaEventRecord(d->kt_events[d->kt_used].first, d->stream));
+  // Inside a capture the pair must become event nodes of the graph.
+  PB_CUDA(cudaEventRecordWithFlags(d->kt_events[d->kt_used].first, d->stream,
+                                   d->capturing ? cudaEventRecordExternal : cudaEventRecordDefault));
   return PB_OK;
 }
 
 int kt_end(Device* d) {
   if (!d->kt_on) return PB_OK;
-  PB_CUDA(cudaEventRecord(d->kt_events[d->kt_used].second, d->stream));
+  PB_CUDA(cudaEventRecordWithFlags(d->kt_events[d->kt_used].second, d->stream,
+                                   d->capturing ? cudaEventRecordExternal : cudaEventRecordDefault));
   ++d->kt_used;
   return PB_OK;
 }
@@ -130,6 +157,8 @@ static void release_device(Device* d) {
   if (d->scratch) cudaFreeAsync(d->scratch, d->stream);
   if (d->counters) cudaFreeAsync(d->counters, d->stream);
   if (d->tags) cudaFreeAsync(d->tags, d->stream);
+  for (void* p : d->retired) cudaFreeAsync(p, d->stream);
+  d->retired.clear();
   if (d->stream) cudaStreamSynchronize(d->stream);
   if (d->t0) cudaEventDestroy(d->t0);
   if (d->t1) cudaEventDestroy(d->t1);
@@ -307,6 +336,7 @@ int pb_alloc(pb_ctx* ctx, int dev, size_t bytes, void** ptr) {
   std::lock_guard<std::recursive_mutex> g(ctx->mu);
   Device* d;
   PB_CHECK(enter(ctx, dev, &d));
+  if (d->capturing) PB_FAIL(PB_ERR_UNSUPPORTED, "%s cannot run during stream capture", __func__);
   if (bytes == 0) bytes = 16;
   PB_CUDA(cudaMallocAsync(ptr, bytes, d->pool, d->stream));
   return PB_OK;
@@ -318,6 +348,7 @@ int pb_free(pb_ctx* ctx, int dev, void* ptr) {
   std::lock_guard<std::recursive_mutex> g(ctx->mu);
   Device* d;
   PB_CHECK(enter(ctx, dev, &d));
+  if (d->capturing) PB_FAIL(PB_ERR_UNSUPPORTED, "%s cannot run during stream capture", __func__);
   PB_CUDA(cudaFreeAsync(ptr, d->stream));
   return PB_OK;
 }
@@ -329,6 +360,8 @@ int pb_h2d(pb_ctx* ctx, int dev, void* dst, const void* src, size_t bytes, int b
   std::lock_guard<std::recursive_mutex> g(ctx->mu);
   Device* d;
   PB_CHECK(enter(ctx, dev, &d));
+  if (blocking && d->capturing)
+    PB_FAIL(PB_ERR_UNSUPPORTED, "a blocking copy cannot run during stream capture");
   PB_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, d->stream));
   if (blocking) PB_CUDA(cudaStreamSynchronize(d->stream));
   return PB_OK;
@@ -339,6 +372,7 @@ int pb_d2h(pb_ctx* ctx, int dev, void* dst, const void* src, size_t bytes) {
   std::lock_guard<std::recursive_mutex> g(ctx->mu);
   Device* d;
   PB_CHECK(enter(ctx, dev, &d));
+  if (d->capturing) PB_FAIL(PB_ERR_UNSUPPORTED, "%s cannot run during stream capture", __func__);
   if (bytes) {
     if (!dst || !src) PB_FAIL(PB_ERR_INVALID, "null pointer in pb_d2h");
     PB_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, d->stream));
@@ -372,6 +406,7 @@ int pb_sync(pb_ctx* ctx, int dev) {
   std::lock_guard<std::recursive_mutex> g(ctx->mu);
   Device* d;
   PB_CHECK(enter(ctx, dev, &d));
+  if (d->capturing) PB_FAIL(PB_ERR_UNSUPPORTED, "%s cannot run during stream capture", __func__);
   if (d->comm) PB_CHECK(comm_stream_wait(d));
   else PB_CUDA(cudaStreamSynchronize(d->stream));
   return check_kernel_error(d);
@@ -394,6 +429,9 @@ int pb_trim(pb_ctx* ctx, int dev) {
   std::lock_guard<std::recursive_mutex> g(ctx->mu);
   Device* d;
   PB_CHECK(enter(ctx, dev, &d));
+  if (d->graphs_live > 0)
+    PB_FAIL(PB_ERR_UNSUPPORTED, "pb_trim would free buffers that live graphs use");
+  if (d->capturing) PB_FAIL(PB_ERR_UNSUPPORTED, "%s cannot run during stream capture", __func__);
   if (d->scratch) PB_CUDA(cudaFreeAsync(d->scratch, d->stream));
   d->scratch = nullptr;
   d->scratch_bytes = 0;
@@ -410,6 +448,7 @@ int pb_timer_start(pb_ctx* ctx, int dev) {
   std::lock_guard<std::recursive_mutex> g(ctx->mu);
   Device* d;
   PB_CHECK(enter(ctx, dev, &d));
+  if (d->capturing) PB_FAIL(PB_ERR_UNSUPPORTED, "%s cannot run during stream capture", __func__);
   PB_CUDA(cudaEventRecord(d->t0, d->stream));
   return PB_OK;
 }
@@ -419,6 +458,7 @@ int pb_timer_stop(pb_ctx* ctx, int dev, float* ms) {
   std::lock_guard<std::recursive_mutex> g(ctx->mu);
   Device* d;
   PB_CHECK(enter(ctx, dev, &d));
+  if (d->capturing) PB_FAIL(PB_ERR_UNSUPPORTED, "%s cannot run during stream capture", __func__);
   PB_CUDA(cudaEventRecord(d->t1, d->stream));
   PB_CUDA(cudaEventSynchronize(d->t1));
   PB_CUDA(cudaEventElapsedTime(ms, d->t0, d->t1));
@@ -430,8 +470,64 @@ int pb_ktimer_enable(pb_ctx* ctx, int dev, int enable) {
   std::lock_guard<std::recursive_mutex> g(ctx->mu);
   Device* d;
   PB_CHECK(enter(ctx, dev, &d));
-  d->kt_on = enable != 0;
+  if (d->capturing) PB_FAIL(PB_ERR_UNSUPPORTED, "the kernel timer cannot change during capture");
+  d->kt_on = enable < 0 || enable > 2 ? 1 : enable;
   d->kt_used = 0;
+  return PB_OK;
+}
+
+int pb_capture_begin(pb_ctx* ctx, int dev) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  if (d->capturing) PB_FAIL(PB_ERR_INVALID, "a capture is already in progress");
+  PB_CUDA(cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeRelaxed));
+  d->capturing = 1;
+  return PB_OK;
+}
+
+int pb_capture_end(pb_ctx* ctx, int dev, void** graph) {
+  if (!ctx || !graph) PB_FAIL(PB_ERR_INVALID, "null argument");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  if (!d->capturing) PB_FAIL(PB_ERR_INVALID, "no capture in progress");
+  d->capturing = 0;
+  cudaGraph_t cg = nullptr;
+  PB_CUDA(cudaStreamEndCapture(d->stream, &cg));
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t e = cudaGraphInstantiate(&exec, cg, 0);
+  cudaGraphDestroy(cg);
+  if (e != cudaSuccess)
+    PB_FAIL(PB_ERR_CUDA, "cudaGraphInstantiate failed: %s", cudaGetErrorString(e));
+  *graph = exec;
+  ++d->graphs_live;
+  return PB_OK;
+}
+
+int pb_graph_launch(pb_ctx* ctx, int dev, void* graph) {
+  if (!ctx || !graph) PB_FAIL(PB_ERR_INVALID, "null argument");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  PB_CUDA(cudaGraphLaunch((cudaGraphExec_t)graph, d->stream));
+  return PB_OK;
+}
+
+int pb_graph_destroy(pb_ctx* ctx, int dev, void* graph) {
+  if (!graph) return PB_OK;
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  // The graph may still run on the stream: destroying the executable is safe
+  // then, freeing what it uses is ordered after it on the same stream.
+  PB_CUDA(cudaGraphExecDestroy((cudaGraphExec_t)graph));
+  if (d->graphs_live > 0 && --d->graphs_live == 0) {
+    for (void* p : d->retired) PB_CUDA(cudaFreeAsync(p, d->stream));
+    d->retired.clear();
+  }
   return PB_OK;
 }
 
@@ -440,6 +536,7 @@ int pb_ktimer_read(pb_ctx* ctx, int dev, double* total_ms, uint64_t* launches) {
   std::lock_guard<std::recursive_mutex> g(ctx->mu);
   Device* d;
   PB_CHECK(enter(ctx, dev, &d));
+  if (d->capturing) PB_FAIL(PB_ERR_UNSUPPORTED, "%s cannot run during stream capture", __func__);
   PB_CUDA(cudaStreamSynchronize(d->stream));
   double total = 0.0;
   for (size_t i = 0; i < d->kt_used; ++i) {
@@ -449,7 +546,7 @@ int pb_ktimer_read(pb_ctx* ctx, int dev, double* total_ms, uint64_t* launches) {
   }
   *total_ms = total;
   *launches = d->kt_used;
-  d->kt_used = 0;
+  if (d->kt_on != 2) d->kt_used = 0;
   return check_kernel_error(d);
 }
 

@@ -84,6 +84,10 @@ PROTOTYPES = {
     "pb_ktimer_enable": [_ctx, _i, _i],
     "pb_ktimer_read": [_ctx, _i, C.POINTER(C.c_double), C.POINTER(C.c_uint64)],
     "pb_memory_stats": [_ctx, _i, C.POINTER(_sz), C.POINTER(_sz), C.POINTER(_sz), C.POINTER(_sz)],
+    "pb_capture_begin": [_ctx, _i],
+    "pb_capture_end": [_ctx, _i, C.POINTER(C.c_void_p)],
+    "pb_graph_launch": [_ctx, _i, C.c_void_p],
+    "pb_graph_destroy": [_ctx, _i, C.c_void_p],
     "pb_gemm": [_ctx, _i, _i, _i, _pi64, _pi64, _pi64, _i64, _i64, _i64, _p, _p, _p],
     "pb_gemm_ex": [_ctx, _i, _i, _i, _pi64, _pi64, _pi64, _i64, _i64, _i64, _p, _p, _p, _i],
     "pb_gemv": [_ctx, _i, _i, _i64, _i64, _p, _p, _p],

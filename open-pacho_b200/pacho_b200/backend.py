@@ -96,6 +96,41 @@ class DeviceArray:
         return f"DeviceArray(shape={self.shape}, dtype={self.dtype}, device={self._backend.ordinal})"
 
 
+class Graph:
+    """A captured sequence of library calls (``B200Backend.capture``),
+    replayed on the device stream by ``launch()``; ``close()`` frees it."""
+
+    def __init__(self, backend: "B200Backend", handle: int, launches: int):
+        self._backend, self._handle, self.launches = backend, handle, launches
+
+    def launch(self):
+        b = self._backend
+        with b._lock:
+            b._require_open()
+            if not self._handle:
+                raise RuntimeError("graph is closed")
+            b._check(b._lib.pb_graph_launch(b._ctx, 0, C.c_void_p(self._handle)), "pb_graph_launch")
+
+    def close(self):
+        b, h = self._backend, self._handle
+        self._handle = 0
+        if h and not b._closed:
+            with b._lock:
+                b._check(b._lib.pb_graph_destroy(b._ctx, 0, C.c_void_p(h)), "pb_graph_destroy")
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+
 def wrap_like(template, data, shape, dtype, backend):
     """An array of ``template``'s kind around ``data``: OpenPacho's ndarray
     (its ``_wrap`` constructor, src/openpacho/_array.py:43-51) when the caller
@@ -158,6 +193,7 @@ class B200Backend:
         self._lock = threading.RLock()
         self._closed = False
         self._buffers = weakref.WeakSet()
+        self._graphs = weakref.WeakSet()
         ctx = C.c_void_p()
         ordinals = (C.c_int * 1)(identifier)
         status = self._lib.pb_init(1, ordinals, C.byref(ctx))
@@ -465,6 +501,29 @@ class B200Backend:
             )
         return out
 
+    # --------------------------------------------------------------- graphs
+    def capture(self, fn) -> Graph:
+        """Record the library calls `fn` makes on this device into a CUDA graph
+        instead of running them.  `fn` must only launch work on buffers that
+        already exist (no allocation, download or synchronisation), and one
+        uncaptured call of the same shapes must have run before.  The graph's
+        `launches` is the number of kernels one replay runs."""
+        with self._lock:
+            self._require_open()
+            before = self.launch_count()
+            self._check(self._lib.pb_capture_begin(self._ctx, 0), "pb_capture_begin")
+            handle = C.c_void_p()
+            try:
+                fn()
+            except BaseException:
+                if self._lib.pb_capture_end(self._ctx, 0, C.byref(handle)) == _lib.PB_OK:
+                    self._lib.pb_graph_destroy(self._ctx, 0, handle)
+                raise
+            self._check(self._lib.pb_capture_end(self._ctx, 0, C.byref(handle)), "pb_capture_end")
+            graph = Graph(self, handle.value, self.launch_count() - before)
+            self._graphs.add(graph)
+            return graph
+
     # --------------------------------------------------------------- timing
     def launch_count(self) -> int:
         value = C.c_uint64(0)
@@ -478,6 +537,8 @@ class B200Backend:
             if self._closed:
                 return
             self._lib.pb_sync(self._ctx, 0)
+            for graph in list(self._graphs):
+                graph.close()
             for buf in list(self._buffers):
                 buf.release()
             self._closed = True
