@@ -1418,6 +1418,88 @@ def b200_arm(args, dist: Dist) -> int:
     return 0
 
 
+def pool_arm(args) -> int:
+    """BASELINE config 5 through one backend object that holds N GPUs in one
+    process (``B200Backend("0-<N-1>")``): A and B live on the primary, the
+    product is split into row blocks by the backend itself, and the timed
+    step includes the NVLink transfers (A blocks and B out, C blocks back).
+    Run as one process, not under torchrun; the single-GPU product of the
+    same inputs is timed beside it."""
+    from pacho_b200 import B200Backend, DeviceArray
+
+    f64 = args.workload == "pool_f64"
+    n = args.n or (8192 if f64 else 16384)
+    dtype = np.float64 if f64 else np.float32
+    be = B200Backend(f"0-{args.gpus - 1}") if args.gpus > 1 else B200Backend(0)
+    A, B = gen_gemm(4, n, dtype)
+    dA = DeviceArray(be, be.upload(A), A.shape, dtype)
+    dB = DeviceArray(be, be.upload(B), B.shape, dtype)
+    lib, ctx = be._lib, be._ctx
+
+    def step():
+        return be.matmul(dA, dB, (n, n), dtype)
+
+    def timed(fn, reps):
+        be.synchronize()
+        _lib_check(lib.pb_timer_start(ctx, 0), "timer")
+        for _ in range(reps):
+            out = fn()
+            del out
+        ms = C.c_float()
+        _lib_check(lib.pb_timer_stop(ctx, 0, C.byref(ms)), "timer")
+        return ms.value / 1e3
+
+    for _ in range(args.warmup):
+        step()
+    splits0 = be._pool.splits if be._pool else 0
+    with Clocks(be.ordinal) as clocks:
+        seconds = timed(step, args.steps)
+    split = (be._pool.splits - splits0) == args.steps if be._pool else False
+    out = step()
+    host = np.empty((n, n), dtype)
+    _lib_check(lib.pb_d2h(ctx, 0, C.c_void_p(host.ctypes.data), C.c_void_p(out.ptr), host.nbytes), "d2h")
+    from oracle import numpy_backend, tolerance  # the checker, outside the timed step
+
+    rows = np.random.default_rng(0).choice(n, size=64, replace=False)
+    bad = tolerance.gemm_violations(host[rows], numpy_backend.matmul(A[rows], B), A[rows], B)
+    one = None
+    if be._pool:
+        gain = be.split_min_gain
+        be.split_min_gain = 0.0  # never split: the primary alone
+        for _ in range(2):
+            step()
+        one = timed(step, max(1, min(args.steps, 5))) / max(1, min(args.steps, 5))
+        be.split_min_gain = gain
+    flops = 2.0 * n ** 3
+    value = flops * args.steps / seconds / 1e12
+    line = {
+        "metric": f"{np.dtype(dtype).name} GEMM {n}^3 TFLOP/s, one process over {args.gpus} GPUs",
+        "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": seconds / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f64 (DMMA)" if f64 else "f32 (3xTF32)",
+        "data": DATA,
+        "config": {"workload": f"BASELINE config 5: {np.dtype(dtype).name} {n}^3, N(0,1), default_rng(4)",
+                   "parallelism": (f"one backend over {args.gpus} GPUs: row blocks of A and the whole B "
+                                   "sent from the primary over NVLink, C blocks copied back, all inside "
+                                   "the timed step" if args.gpus > 1 else "one GPU"),
+                   "l2": "operands and output far above the 126 MB L2"},
+        "split_every_step": split, "clocks": clocks.summary(), "parity_violations": int(bad),
+        "peer_access_all_pairs": bool(be._pool.all_peer) if be._pool else None,
+    }
+    if one:
+        line["one_gpu"] = {"ms_per_step": one * 1e3, "value": flops / one / 1e12,
+                           "speedup": one / (seconds / args.steps)}
+    print(json.dumps(line))
+    be.close()
+    return 0
+
+
+def _lib_check(status, what):
+    from pacho_b200 import _lib
+
+    _lib.check(status, what)
+
+
 def main(argv=None):
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
@@ -1426,7 +1508,10 @@ def main(argv=None):
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--workload", default="suite",
                         choices=("suite", "batched", "gemm1024", "gemv_dot", "norm", "norm_rows", "gemm_f32",
-                                 "gemm_f64", "vecmat", "elementwise", "reduce", "residual"))
+                                 "gemm_f64", "vecmat", "elementwise", "reduce", "residual", "pool_f32",
+                                 "pool_f64"),
+                        help="pool_f32 / pool_f64: config 5 through one backend over --gpus GPUs in one "
+                             "process (not under torchrun)")
     parser.add_argument("--dtype", choices=("f32", "f64"), default="f32", help="norm workloads")
     parser.add_argument("--n", type=int, default=0,
                         help="GEMM / vecmat / around-path size override (profiling captures); 0 = BASELINE")
@@ -1439,6 +1524,10 @@ def main(argv=None):
         parser.error("--warmup must be >= 3")
     if args.steps < 1:
         parser.error("--steps must be >= 1")
+    if args.workload.startswith("pool"):
+        if args.impl == "reference":
+            parser.error("the pool workloads have no reference arm; the reference drives one device")
+        return pool_arm(args)
     dist = Dist()
     try:
         if args.impl == "reference":

@@ -130,6 +130,22 @@ int pb_launch_count(pb_ctx* ctx, int dev, uint64_t* count);
  * without starting a new count.  No counterpart in the reference. */
 int pb_ktimer_enable(pb_ctx* ctx, int dev, int enable);
 int pb_ktimer_read(pb_ctx* ctx, int dev, double* total_ms, uint64_t* launches);
+/* Several GPUs in one context (pb_init with ndev > 1; `dev` is the index
+ * into its ordinals).  pb_peer_enable turns on peer access between every pair
+ * of the context's devices that supports it and reports in *all_pairs (may be
+ * NULL) whether every pair does.  pb_copy_peer queues a copy of `bytes` from
+ * `src` on device index `src_dev` to `dst` on `dst_dev` (over NVLink when peer
+ * access is on) on the stream of `stream_dev`, which must be one of the two;
+ * it orders nothing else.  pb_stream_wait makes `waiter`'s stream wait for the
+ * work queued so far on `signal`'s: the caller orders a copy after the
+ * producer of its source and the allocation of its destination, and the
+ * consumer (or a free) after the copy.  No counterpart in the reference, which
+ * drives one device (src/openpacho/_cuda.py:138-199). */
+int pb_peer_enable(pb_ctx* ctx, int* all_pairs);
+int pb_copy_peer(pb_ctx* ctx, int dst_dev, void* dst, int src_dev, const void* src, size_t bytes,
+                 int stream_dev);
+int pb_stream_wait(pb_ctx* ctx, int waiter, int signal);
+
 /* CUDA graphs of hot-path calls.  pb_capture_begin starts a (relaxed) capture
  * of the device stream; the entry points called until pb_capture_end are
  * recorded, not run, and pb_capture_end returns an instantiated graph that

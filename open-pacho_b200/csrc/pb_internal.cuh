@@ -87,6 +87,9 @@ struct Device {
   int* err_host = nullptr;
   int* err_dev = nullptr;
   cudaEvent_t t0 = nullptr, t1 = nullptr;
+  // Marks this stream's position for another device's stream to wait on
+  // (pb_copy_peer, pb_stream_wait); no timing.
+  cudaEvent_t order_ev = nullptr;
   std::atomic<uint64_t> launches{0};
   // Per-kernel timer (pb_ktimer_*): event pairs around main kernels while on
   // (1), or on with the pairs kept across reads (2: events inside a graph).

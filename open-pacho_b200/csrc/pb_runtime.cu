@@ -162,6 +162,7 @@ static void release_device(Device* d) {
   if (d->stream) cudaStreamSynchronize(d->stream);
   if (d->t0) cudaEventDestroy(d->t0);
   if (d->t1) cudaEventDestroy(d->t1);
+  if (d->order_ev) cudaEventDestroy(d->order_ev);
   for (auto& ev : d->kt_events) {
     cudaEventDestroy(ev.first);
     cudaEventDestroy(ev.second);
@@ -299,7 +300,8 @@ int pb_init(int ndev, const int* ordinals, pb_ctx** out) {
       fail("cudaHostGetDevicePointer", e);
       break;
     }
-    if ((e = cudaEventCreate(&d->t0)) != cudaSuccess || (e = cudaEventCreate(&d->t1)) != cudaSuccess) {
+    if ((e = cudaEventCreate(&d->t0)) != cudaSuccess || (e = cudaEventCreate(&d->t1)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&d->order_ev, cudaEventDisableTiming)) != cudaSuccess) {
       fail("cudaEventCreate", e);
       break;
     }
@@ -473,6 +475,75 @@ int pb_ktimer_enable(pb_ctx* ctx, int dev, int enable) {
   if (d->capturing) PB_FAIL(PB_ERR_UNSUPPORTED, "the kernel timer cannot change during capture");
   d->kt_on = enable < 0 || enable > 2 ? 1 : enable;
   d->kt_used = 0;
+  return PB_OK;
+}
+
+// ---- several devices in one context ---------------------------------------
+
+int pb_peer_enable(pb_ctx* ctx, int* all_pairs) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  int all = 1;
+  for (int i = 0; i < ctx->ndev; ++i) {
+    for (int j = 0; j < ctx->ndev; ++j) {
+      const int a = ctx->devs[i].ordinal, b = ctx->devs[j].ordinal;
+      if (a == b) continue;
+      int can = 0;
+      PB_CUDA(cudaDeviceCanAccessPeer(&can, a, b));
+      if (!can) {
+        all = 0;
+        continue;
+      }
+      PB_CUDA(cudaSetDevice(a));
+      const cudaError_t e = cudaDeviceEnablePeerAccess(b, 0);
+      if (e == cudaErrorPeerAccessAlreadyEnabled) {
+        cudaGetLastError();
+      } else if (e != cudaSuccess) {
+        PB_FAIL(PB_ERR_CUDA, "cudaDeviceEnablePeerAccess(%d -> %d): %s", a, b,
+                cudaGetErrorString(e));
+      }
+    }
+  }
+  if (all_pairs) *all_pairs = all;
+  return PB_OK;
+}
+
+// `waiter`'s stream waits for everything queued so far on `signal`'s stream.
+static int join_streams(Device* waiter, Device* signal) {
+  if (waiter == signal) return PB_OK;
+  PB_CUDA(cudaSetDevice(signal->ordinal));
+  PB_CUDA(cudaEventRecord(signal->order_ev, signal->stream));
+  PB_CUDA(cudaSetDevice(waiter->ordinal));
+  PB_CUDA(cudaStreamWaitEvent(waiter->stream, signal->order_ev, 0));
+  return PB_OK;
+}
+
+int pb_stream_wait(pb_ctx* ctx, int waiter, int signal) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device *w, *s;
+  PB_CHECK(enter(ctx, signal, &s));
+  PB_CHECK(enter(ctx, waiter, &w));
+  return join_streams(w, s);
+}
+
+int pb_copy_peer(pb_ctx* ctx, int dst_dev, void* dst, int src_dev, const void* src, size_t bytes,
+                 int stream_dev) {
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  if (!bytes) return PB_OK;
+  if (!dst || !src) PB_FAIL(PB_ERR_INVALID, "null pointer in pb_copy_peer");
+  if (stream_dev != dst_dev && stream_dev != src_dev)
+    PB_FAIL(PB_ERR_INVALID, "pb_copy_peer runs on the source's or the destination's stream");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device *t, *s, *on;
+  PB_CHECK(enter(ctx, src_dev, &s));
+  PB_CHECK(enter(ctx, dst_dev, &t));
+  PB_CHECK(enter(ctx, stream_dev, &on));
+  if (on->capturing) PB_FAIL(PB_ERR_UNSUPPORTED, "pb_copy_peer cannot run during stream capture");
+  if (t == s)
+    PB_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, on->stream));
+  else
+    PB_CUDA(cudaMemcpyPeerAsync(dst, t->ordinal, src, s->ordinal, bytes, on->stream));
   return PB_OK;
 }
 

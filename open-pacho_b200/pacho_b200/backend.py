@@ -21,7 +21,7 @@ from math import prod
 
 import numpy as np
 
-from . import _lib
+from . import _lib, pool
 from . import exceptions as _exc
 
 SUPPORTED = (np.dtype(np.float32), np.dtype(np.float64), np.dtype(np.bool_))
@@ -167,15 +167,24 @@ class B200Backend:
 
     name = "b200"
     fp64 = True
+    # One GPU unless the context holds several (set in __init__).
+    ordinals = (0,)
+    _pool = None
+    split_min_gain = pool.MIN_GAIN
 
-    def __init__(self, device=None):
+    def __init__(self, device=None, *, gpus=None):
         self._lib = _lib.load()
-        identifier = 0 if device is None else int(str(device))
+        try:
+            ordinals = pool.parse_devices(device, gpus)
+        except ValueError as exc:
+            raise _exc.BackendUnavailableError(str(exc)) from exc
+        identifier = ordinals[0]
         count = C.c_int(0)
         status = self._lib.pb_device_count(C.byref(count))
         if status != _lib.PB_OK or count.value == 0:
             raise _exc.BackendUnavailableError(f"no CUDA device for b200: {_lib.last_error()}")
-        if not 0 <= identifier < count.value:
+        missing = [o for o in ordinals if not 0 <= o < count.value]
+        if missing:
             raise _exc.BackendUnavailableError(f"b200 device {device!r} not found ({count.value} visible)")
         name = C.create_string_buffer(256)
         total = C.c_size_t(0)
@@ -195,14 +204,18 @@ class B200Backend:
         self._buffers = weakref.WeakSet()
         self._graphs = weakref.WeakSet()
         ctx = C.c_void_p()
-        ordinals = (C.c_int * 1)(identifier)
-        status = self._lib.pb_init(1, ordinals, C.byref(ctx))
+        status = self._lib.pb_init(len(ordinals), (C.c_int * len(ordinals))(*ordinals), C.byref(ctx))
         if status != _lib.PB_OK:
             raise _exc.BackendUnavailableError(f"b200 initialization failed: {_lib.last_error()}")
         self._ctx = ctx
+        # Arrays live on the first GPU; with more, large products are split.
+        self.ordinals = tuple(ordinals)
+        self._pool = pool.DevicePool(self, len(ordinals)) if len(ordinals) > 1 else None
 
     # ---------------------------------------------------------------- basics
     def __repr__(self):
+        if len(self.ordinals) > 1:
+            return f"B200Backend(devices={list(self.ordinals)}, name={self.device!r})"
         return f"B200Backend(device={self.ordinal}, name={self.device!r})"
 
     def _check(self, status, what):
@@ -325,6 +338,9 @@ class B200Backend:
                 a_batch = a.shape[:-2] if a.ndim > 1 else ()
                 b_batch = b.shape[:-2]
                 batch = np.broadcast_shapes(a_batch, b_batch)
+                if self._pool is not None and a.ndim > 1:
+                    if self._split_matmul(code, dtype, a, b, batch, m, n, k, A, B, O):
+                        return out
                 self._check(
                     lib.pb_gemm(ctx, 0, code, len(batch), _lib.i64_array(batch),
                                 _lib.i64_array(_matrix_strides(batch, a_batch)),
@@ -333,6 +349,35 @@ class B200Backend:
                     "pb_gemm",
                 )
         return out
+
+    def _split_matmul(self, code, dtype, a, b, batch, m, n, k, A, B, O) -> bool:
+        """The product over every GPU of the context, when it pays."""
+        sp = pool.plan(a.shape, b.shape, batch, m, n, k)
+        if sp is None or sp.outer < 2:
+            return False
+        isz = dtype.itemsize
+        flops = 2.0 * prod(batch) * m * n * k
+        if not pool.worth_splitting(flops, isz, prod(a.shape) * isz, prod(b.shape) * isz,
+                                    prod(batch) * m * n * isz, len(self.ordinals),
+                                    min_gain=self.split_min_gain):
+            return False
+        lib, ctx = self._lib, self._ctx
+
+        def gemm(dev, outer, pa, pb, pc):
+            if not sp.batch:
+                status = lib.pb_gemm(ctx, dev, code, 0, _lib.i64_array(()), _lib.i64_array(()),
+                                     _lib.i64_array(()), outer, n, k, C.c_void_p(pa), C.c_void_p(pb),
+                                     C.c_void_p(pc))
+            else:
+                bshape = (outer,) + sp.batch[1:]
+                status = lib.pb_gemm(ctx, dev, code, len(bshape), _lib.i64_array(bshape),
+                                     _lib.i64_array(_matrix_strides(bshape, bshape)),
+                                     _lib.i64_array(_matrix_strides(bshape, bshape if sp.b_block else ())),
+                                     m, n, k, C.c_void_p(pa), C.c_void_p(pb), C.c_void_p(pc))
+            self._check(status, "pb_gemm")
+
+        self._pool.matmul(code, isz, sp, A.value, B.value, O.value, gemm)
+        return True
 
     def norm(self, a, axes, keepdims, dtype):
         """Euclidean/Frobenius norm over ``axes`` (norm_data,

@@ -1,0 +1,183 @@
+"""Host logic of the single-process GPU pool (``device="0-7"``): device lists,
+block plans, the split decision on BASELINE's shapes, and the order of the
+copies, waits and launches the split product queues (against a recording
+stand-in for the library, no GPU)."""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import pytest
+
+from pacho_b200 import _lib, pool
+
+
+def test_parse_devices():
+    assert pool.parse_devices(None) == [0]
+    assert pool.parse_devices(3) == [3]
+    assert pool.parse_devices("5") == [5]
+    assert pool.parse_devices("cuda:2") == [2]
+    assert pool.parse_devices("0-7") == list(range(8))
+    assert pool.parse_devices("0, 2,5") == [0, 2, 5]
+    assert pool.parse_devices("1-2,6") == [1, 2, 6]
+    assert pool.parse_devices(None, gpus=4) == [0, 1, 2, 3]
+    assert pool.parse_devices("4", gpus=2) == [4, 5]
+    assert pool.parse_devices("0-1", gpus=2) == [0, 1]
+    for bad in ("a", "3-1", "0,0", "-1", "0-1x"):
+        with pytest.raises(ValueError):
+            pool.parse_devices(bad)
+    with pytest.raises(ValueError):
+        pool.parse_devices("0-3", gpus=2)
+    with pytest.raises(ValueError):
+        pool.parse_devices(None, gpus=0)
+
+
+@pytest.mark.parametrize("total,parts,align", [(16384, 8, 128), (1000, 8, 128), (8, 8, 1), (3, 8, 1),
+                                               (1, 2, 128), (129, 2, 128), (7, 3, 1), (0, 4, 1)])
+def test_blocks_cover_the_range_in_order(total, parts, align):
+    got = pool.blocks(total, parts, align)
+    assert len(got) <= parts
+    if not total:
+        assert got == []
+        return
+    assert [lo for lo, _ in got] == [0] + [hi for _, hi in got[:-1]]
+    assert (got[-1][1] if got else 0) == total
+    assert all(hi > lo for lo, hi in got)
+    assert all(lo % align == 0 for lo, _ in got)
+    sizes = [hi - lo for lo, hi in got]
+    if len(got) > 1:
+        # Equal up to one alignment unit, except a short last block.
+        assert max(sizes[:-1]) - min(sizes[:-1]) <= align
+
+
+def test_plan_layouts():
+    two_d = pool.plan((4096, 512), (512, 256), (), 4096, 256, 512)
+    assert (two_d.outer, two_d.a_block, two_d.b_block, two_d.c_block, two_d.b_whole) == (4096, 512, 0, 256,
+                                                                                          512 * 256)
+    shared_b = pool.plan((8, 16, 512, 256), (1, 16, 256, 384), (8, 16), 512, 384, 256)
+    assert shared_b is None  # B batched along the inner dimension only: no contiguous cut
+    batched = pool.plan((8, 16, 512, 256), (8, 16, 256, 384), (8, 16), 512, 384, 256)
+    assert (batched.outer, batched.a_block, batched.b_block, batched.c_block) == (
+        8, 16 * 512 * 256, 16 * 256 * 384, 16 * 512 * 384)
+    whole_b = pool.plan((8, 512, 256), (256, 384), (8,), 512, 384, 256)
+    assert (whole_b.outer, whole_b.b_block, whole_b.b_whole) == (8, 0, 256 * 384)
+    assert pool.plan((512, 256), (8, 256, 384), (8,), 512, 384, 256) is None  # A broadcast
+
+
+def test_split_decision_on_baseline_shapes():
+    f32, f64 = 4, 8
+    # Config 5: 16384^3 float32 and 8192^3 float64 split over 8 GPUs.
+    assert pool.worth_splitting(2.0 * 16384 ** 3, f32, 16384 ** 2 * 4, 16384 ** 2 * 4, 16384 ** 2 * 4, 8)
+    assert pool.worth_splitting(2.0 * 8192 ** 3, f64, 8192 ** 2 * 8, 8192 ** 2 * 8, 8192 ** 2 * 8, 8)
+    # Config 1 (1024^3) and config 3 (12.9 GFLOP) stay on one GPU.
+    assert not pool.worth_splitting(2.0 * 1024 ** 3, f32, 4 << 20, 4 << 20, 4 << 20, 8)
+    assert not pool.worth_splitting(2.0 * 8 * 16 * 512 * 256 * 384, f32, 8 * 16 * 512 * 256 * 4,
+                                    16 * 256 * 384 * 4, 8 * 16 * 512 * 384 * 4, 8)
+    assert not pool.worth_splitting(2.0 * 16384 ** 3, f32, 1, 1, 1, 1)
+
+
+class FakeLib:
+    """Records the pool's library calls; pointers are (device, serial)."""
+
+    def __init__(self):
+        self.calls = []
+        self.next = 1 << 40
+
+    def pb_peer_enable(self, ctx, flag):
+        flag._obj.value = 1
+        return 0
+
+    def pb_alloc(self, ctx, dev, nbytes, ptr):
+        self.next += 1 << 32
+        ptr._obj.value = self.next
+        self.calls.append(("alloc", dev, nbytes, self.next))
+        return 0
+
+    def pb_free(self, ctx, dev, ptr):
+        self.calls.append(("free", dev, ptr.value))
+        return 0
+
+    def pb_stream_wait(self, ctx, waiter, signal):
+        self.calls.append(("wait", waiter, signal))
+        return 0
+
+    def pb_copy_peer(self, ctx, dst_dev, dst, src_dev, src, nbytes, on):
+        self.calls.append(("copy", dst_dev, dst.value, src_dev, src.value, nbytes, on))
+        return 0
+
+
+class FakeBackend:
+    def __init__(self):
+        self._lib, self._ctx = FakeLib(), C.c_void_p(1)
+
+
+@pytest.mark.parametrize("ndev", [2, 3, 8])
+def test_split_product_queues_copies_waits_and_launches_in_order(ndev, monkeypatch):
+    monkeypatch.setattr(pool, "CHUNK_BYTES", 1 << 20)
+    be = FakeBackend()
+    dp = pool.DevicePool(be, ndev)
+    assert dp.all_peer
+    M, N, K, isz = 1000, 96, 640, 4
+    sp = pool.plan((M, K), (K, N), (), M, N, K)
+    A, B, O = 1 << 20, 2 << 30, 3 << 30
+    launches = []
+    dp.matmul(_lib.PB_F32, isz, sp, A, B, O,
+              lambda dev, outer, pa, pb, pc: launches.append((dev, outer, pa, pb, pc)))
+    calls = be._lib.calls
+    parts = pool.blocks(M, ndev, pool.ROW_ALIGN)
+    used = len(parts)
+    # Every other device first waits for the primary's stream.
+    assert calls[: used - 1] == [("wait", d, 0) for d in range(1, used)]
+    allocs = [c for c in calls if c[0] == "alloc"]
+    assert len(allocs) == 3 * (used - 1)
+    # Launches: one per block, rows as planned, the primary in place.
+    assert [(d, outer) for d, outer, *_ in launches] == [(d, hi - lo) for d, (lo, hi) in enumerate(parts)]
+    assert launches[0][2:] == (A, B, O)
+    copies = [c for c in calls if c[0] == "copy"]
+    # A blocks from the primary, on the receiver's stream.
+    for d, (lo, hi) in enumerate(parts[1:], start=1):
+        assert ("copy", d, allocs[3 * (d - 1)][3], 0, A + lo * K * isz, (hi - lo) * K * isz, d) in copies
+    # B as a chain in chunks: device d reads device d-1's copy.
+    total = K * N * isz
+    chunks = -(-total // pool.CHUNK_BYTES)
+    chain = [c for c in copies if c[5] <= pool.CHUNK_BYTES and c[3] != c[1] and c[1] != 0 and
+             c[4] != A + parts[c[1]][0] * K * isz]
+    assert len(chain) == chunks * (used - 1)
+    for c in chain:
+        d = c[1]
+        src_base = B if d == 1 else allocs[3 * (d - 2) + 1][3]
+        assert c[3] == d - 1 and src_base <= c[4] < src_base + total and c[6] == d
+    # C blocks back into the result, on the sender's stream, after its launch.
+    for d, (lo, hi) in enumerate(parts[1:], start=1):
+        gather = ("copy", 0, O + lo * N * isz, d, allocs[3 * (d - 1) + 2][3], (hi - lo) * N * isz, d)
+        assert gather in copies
+    # The primary waits for every device at the end, each device for the next
+    # one in the chain (which read its B), then the temporaries go.
+    last = max(i for i, c in enumerate(calls) if c[0] in ("copy", "alloc"))
+    tail = [c for c in calls[last + 1:] if c[0] == "wait"]
+    assert tail == [("wait", 0, d) for d in range(1, used)] + [("wait", d, d + 1) for d in range(1, used - 1)]
+    assert all(c[0] in ("wait", "free") for c in calls[last + 1:])
+    frees = [c for c in calls if c[0] == "free"]
+    assert sorted(f[2] for f in frees) == sorted(a[3] for a in allocs)
+    assert all(f[1] == a[1] for f in frees for a in allocs if a[3] == f[2])
+    assert dp.splits == 1
+
+
+def test_split_frees_temporaries_when_a_launch_fails():
+    be = FakeBackend()
+    dp = pool.DevicePool(be, 4)
+    sp = pool.plan((1024, 64), (64, 64), (), 1024, 64, 64)
+
+    def gemm(dev, *args):
+        if dev == 2:
+            raise RuntimeError("launch failed")
+
+    with pytest.raises(RuntimeError):
+        dp.matmul(_lib.PB_F32, 4, sp, 1 << 20, 2 << 20, 3 << 20, gemm)
+    allocs = [c[3] for c in be._lib.calls if c[0] == "alloc"]
+    frees = [c[2] for c in be._lib.calls if c[0] == "free"]
+    assert sorted(allocs) == sorted(frees) and allocs
+    # Even on failure the primary's stream ends after every device's work.
+    waits = [c for c in be._lib.calls if c[0] == "wait"]
+    assert all(("wait", 0, d) in waits for d in range(1, 4))
+    assert dp.splits == 0
