@@ -508,7 +508,7 @@ constexpr int64_t kReduceRepairMaxK = 1 << 13;
 template <int COLS>
 __device__ __forceinline__ void store_row(float* dst, const float (&v)[COLS], int64_t col0,
                                           int64_t N) {
-  if ((N % 4) == 0 && col0 + COLS <= N) {
+  if ((N % 4) == 0 && col0 + COLS <= N && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
     float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll
     for (int j = 0; j < COLS / 4; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);

@@ -204,9 +204,8 @@ def test_tf32x3_special_values_match_ieee(b200, algo, shape):
     The 3xTF32 split turns some +-Inf results into NaN (0 * Inf cross terms);
     those tiles are recomputed.  The first two shapes fill every SM without
     splitting K, so the marks come from the tcgen05 epilogues; the batched
-    shape splits K four ways, so they come from the split reduction; 1024^3
-    splits K two ways, which the TMEM kernel sums in CTA pairs before its
-    epilogue checks."""
+    shape splits K four ways and 1024^3 two ways, so they come from the split
+    reduction."""
     *batch, m, n, k = shape
     rng = np.random.default_rng(21)
     a = rng.standard_normal((*batch, m, k)).astype(np.float32)
