@@ -133,7 +133,12 @@ int pb_ktimer_read(pb_ctx* ctx, int dev, double* total_ms, uint64_t* launches);
 /* Several GPUs in one context (pb_init with ndev > 1; `dev` is the index
  * into its ordinals).  pb_peer_enable turns on peer access between every pair
  * of the context's devices that supports it and reports in *all_pairs (may be
- * NULL) whether every pair does.  pb_copy_peer queues a copy of `bytes` from
+ * NULL) whether every pair does.  Peer access maps memory from
+ * pb_alloc_mapped (cudaMalloc) into the other devices, not the stream-ordered
+ * pool memory of pb_alloc: a peer copy runs device to device over NVLink when
+ * the side of it that is remote to the issuing device comes from
+ * pb_alloc_mapped (else the driver stages it).  pb_free_mapped waits for the
+ * device's stream before it frees.  pb_copy_peer queues a copy of `bytes` from
  * `src` on device index `src_dev` to `dst` on `dst_dev` (over NVLink when peer
  * access is on) on the stream of `stream_dev`, which must be one of the two;
  * it orders nothing else.  pb_stream_wait makes `waiter`'s stream wait for the
@@ -142,6 +147,8 @@ int pb_ktimer_read(pb_ctx* ctx, int dev, double* total_ms, uint64_t* launches);
  * consumer (or a free) after the copy.  No counterpart in the reference, which
  * drives one device (src/openpacho/_cuda.py:138-199). */
 int pb_peer_enable(pb_ctx* ctx, int* all_pairs);
+int pb_alloc_mapped(pb_ctx* ctx, int dev, size_t bytes, void** ptr);
+int pb_free_mapped(pb_ctx* ctx, int dev, void* ptr);
 int pb_copy_peer(pb_ctx* ctx, int dst_dev, void* dst, int src_dev, const void* src, size_t bytes,
                  int stream_dev);
 int pb_stream_wait(pb_ctx* ctx, int waiter, int signal);

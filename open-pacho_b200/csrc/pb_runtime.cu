@@ -508,6 +508,31 @@ int pb_peer_enable(pb_ctx* ctx, int* all_pairs) {
   return PB_OK;
 }
 
+// Peer copies go device to device over NVLink only where the remote side of
+// the copy is mapped into the issuing device: memory from cudaMalloc, which
+// peer access maps, unlike the stream-ordered pools.
+int pb_alloc_mapped(pb_ctx* ctx, int dev, size_t bytes, void** ptr) {
+  if (!ctx || !ptr) PB_FAIL(PB_ERR_INVALID, "null argument");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  if (d->capturing) PB_FAIL(PB_ERR_UNSUPPORTED, "%s cannot run during stream capture", __func__);
+  PB_CUDA(cudaMalloc(ptr, bytes ? bytes : 16));
+  return PB_OK;
+}
+
+int pb_free_mapped(pb_ctx* ctx, int dev, void* ptr) {
+  if (!ptr) return PB_OK;
+  if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  Device* d;
+  PB_CHECK(enter(ctx, dev, &d));
+  if (d->capturing) PB_FAIL(PB_ERR_UNSUPPORTED, "%s cannot run during stream capture", __func__);
+  PB_CUDA(cudaStreamSynchronize(d->stream));  // the device's work on it is done
+  PB_CUDA(cudaFree(ptr));
+  return PB_OK;
+}
+
 // `waiter`'s stream waits for everything queued so far on `signal`'s stream.
 static int join_streams(Device* waiter, Device* signal) {
   if (waiter == signal) return PB_OK;

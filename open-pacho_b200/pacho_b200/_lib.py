@@ -85,6 +85,8 @@ PROTOTYPES = {
     "pb_ktimer_read": [_ctx, _i, C.POINTER(C.c_double), C.POINTER(C.c_uint64)],
     "pb_memory_stats": [_ctx, _i, C.POINTER(_sz), C.POINTER(_sz), C.POINTER(_sz), C.POINTER(_sz)],
     "pb_peer_enable": [_ctx, C.POINTER(C.c_int)],
+    "pb_alloc_mapped": [_ctx, _i, _sz, C.POINTER(C.c_void_p)],
+    "pb_free_mapped": [_ctx, _i, C.c_void_p],
     "pb_copy_peer": [_ctx, _i, C.c_void_p, _i, C.c_void_p, _sz, _i],
     "pb_stream_wait": [_ctx, _i, _i],
     "pb_capture_begin": [_ctx, _i],

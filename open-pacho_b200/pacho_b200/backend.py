@@ -584,6 +584,8 @@ class B200Backend:
             self._lib.pb_sync(self._ctx, 0)
             for graph in list(self._graphs):
                 graph.close()
+            if self._pool is not None:
+                self._pool.close()
             for buf in list(self._buffers):
                 buf.release()
             self._closed = True

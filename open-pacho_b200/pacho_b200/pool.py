@@ -141,7 +141,16 @@ def worth_splitting(flops: float, itemsize: int, a_bytes: int, b_bytes: int, c_b
 
 class DevicePool:
     """The GEMM split over a backend's devices (indices 0..ndev-1 of its
-    context, 0 = primary)."""
+    context, 0 = primary).
+
+    Peer access maps cudaMalloc memory into the other devices but not the
+    stream-ordered pools the arrays live in, so every copy is issued by the
+    device that owns the pool side of it and reaches the other side through
+    a mapped workspace: the primary pushes the blocks of A into each
+    device's workspace and pulls the blocks of C back out of them; B goes
+    down the chain, each device pushing each chunk on to the next.  The
+    workspaces (A, B and C per device) are grow-only and kept between calls.
+    """
 
     def __init__(self, backend, ndev: int):
         self.b, self.ndev = backend, ndev
@@ -150,70 +159,92 @@ class DevicePool:
         _lib.check(self.lib.pb_peer_enable(self.ctx, C.byref(flag)), "pb_peer_enable")
         self.all_peer = bool(flag.value)
         self.splits = 0  # products run split (for tests and the bench)
+        self.ws = {}  # (device, role) -> (pointer, bytes)
 
-    def _alloc(self, dev, nbytes):
-        ptr = C.c_void_p()
-        _lib.check(self.lib.pb_alloc(self.ctx, dev, max(int(nbytes), 1), C.byref(ptr)), "pb_alloc")
-        return ptr.value
+    def _workspace(self, dev, role, nbytes):
+        ptr, have = self.ws.get((dev, role), (0, 0))
+        if have >= nbytes:
+            return ptr
+        if ptr:
+            # Copies on other devices' streams may still read it.
+            for i in range(self.ndev):
+                _lib.check(self.lib.pb_sync(self.ctx, i), "pb_sync")
+            _lib.check(self.lib.pb_free_mapped(self.ctx, dev, C.c_void_p(ptr)), "pb_free_mapped")
+            del self.ws[(dev, role)]
+        out = C.c_void_p()
+        _lib.check(self.lib.pb_alloc_mapped(self.ctx, dev, max(int(nbytes), 1), C.byref(out)),
+                   "pb_alloc_mapped")
+        self.ws[(dev, role)] = (out.value, int(nbytes))
+        return out.value
+
+    def close(self):
+        """Frees the workspaces (after the primary's stream, which ends
+        after every device's work)."""
+        self.lib.pb_sync(self.ctx, 0)
+        for (dev, _), (ptr, _) in list(self.ws.items()):
+            self.lib.pb_free_mapped(self.ctx, dev, C.c_void_p(ptr))
+        self.ws.clear()
 
     def matmul(self, code, itemsize, sp: Split, A: int, B: int, O: int, gemm) -> None:
         """C = A @ B by blocks of `sp.outer`; `gemm(dev, outer, A, B, C)`
         launches one block's product on device index `dev`.  Called with the
         backend's lock held; the primary's stream ends after every block."""
         lib, ctx = self.lib, self.ctx
+        check = _lib.check
         align = ROW_ALIGN if not sp.batch else 1
         parts = blocks(sp.outer, self.ndev, align)
-        check = _lib.check
-        # Inputs and the output buffer are ready on the primary's stream.
-        for d in range(1, len(parts)):
-            check(lib.pb_stream_wait(ctx, d, 0), "pb_stream_wait")
-        temps = []
+        n = len(parts)
+        placed = [(A, B, O)]
+        for d, (lo, hi) in enumerate(parts[1:], start=1):
+            rows = hi - lo
+            a = self._workspace(d, "a", rows * sp.a_block * itemsize)
+            b = self._workspace(d, "b", (sp.b_block * rows if sp.b_block else sp.b_whole) * itemsize)
+            c = self._workspace(d, "c", rows * sp.c_block * itemsize)
+            placed.append((a, b, c))
+
+        def copy(dst_dev, dst, src_dev, src, nbytes, on):
+            check(lib.pb_copy_peer(ctx, dst_dev, C.c_void_p(dst), src_dev, C.c_void_p(src), nbytes, on),
+                  "pb_copy_peer")
+
         try:
-            placed = [(A, B, O)]
+            # Every device's stream first waits for the primary's (whose last
+            # call ended after every device's work): the workspaces are free.
+            for d in range(1, n):
+                check(lib.pb_stream_wait(ctx, d, 0), "pb_stream_wait")
+            # The primary pushes the blocks of A (and of a batched B).
             for d, (lo, hi) in enumerate(parts[1:], start=1):
                 rows = hi - lo
-                a = self._alloc(d, rows * sp.a_block * itemsize)
-                temps.append((d, a))
-                bb = sp.b_block * rows if sp.b_block else sp.b_whole
-                b = self._alloc(d, bb * itemsize)
-                temps.append((d, b))
-                c = self._alloc(d, rows * sp.c_block * itemsize)
-                temps.append((d, c))
-                check(lib.pb_copy_peer(ctx, d, C.c_void_p(a), 0, C.c_void_p(A + lo * sp.a_block * itemsize),
-                                       rows * sp.a_block * itemsize, d), "pb_copy_peer")
+                copy(d, placed[d][0], 0, A + lo * sp.a_block * itemsize, rows * sp.a_block * itemsize, 0)
                 if sp.b_block:
-                    check(lib.pb_copy_peer(ctx, d, C.c_void_p(b), 0,
-                                           C.c_void_p(B + lo * sp.b_block * itemsize),
-                                           rows * sp.b_block * itemsize, d), "pb_copy_peer")
-                placed.append((a, b, c))
-            if not sp.b_block and len(parts) > 1:
-                # Chain broadcast of the whole B, chunk by chunk.
+                    copy(d, placed[d][1], 0, B + lo * sp.b_block * itemsize, rows * sp.b_block * itemsize, 0)
+            if not sp.b_block and n > 1:
+                # The whole B down the chain, chunk by chunk: device d - 1
+                # pushes a chunk on once its own copy of it has landed.
                 total = sp.b_whole * itemsize
                 for off in range(0, total, CHUNK_BYTES):
                     size = min(CHUNK_BYTES, total - off)
-                    for d in range(1, len(parts)):
+                    for d in range(1, n):
                         if d > 1:
-                            check(lib.pb_stream_wait(ctx, d, d - 1), "pb_stream_wait")
-                        src = placed[d - 1][1]
-                        check(lib.pb_copy_peer(ctx, d, C.c_void_p(placed[d][1] + off), d - 1,
-                                               C.c_void_p(src + off), size, d), "pb_copy_peer")
-            for d, (lo, hi) in enumerate(parts):
-                a, b, c = placed[d]
-                if d == 0:
-                    gemm(0, hi - lo, A, B, O)
-                else:
-                    gemm(d, hi - lo, a, b, c)
-                    check(lib.pb_copy_peer(ctx, 0, C.c_void_p(O + lo * sp.c_block * itemsize), d,
-                                           C.c_void_p(c), (hi - lo) * sp.c_block * itemsize, d),
-                          "pb_copy_peer")
+                            check(lib.pb_stream_wait(ctx, d - 1, d - 2), "pb_stream_wait")
+                        copy(d, placed[d][1] + off, d - 1, placed[d - 1][1] + off, size, d - 1)
+            # Each device after the pushes into it (all joins before any
+            # block is queued, so no device waits for another's block), then
+            # the blocks.
+            for d in range(1, n):
+                check(lib.pb_stream_wait(ctx, d, 0), "pb_stream_wait")
+                if d > 1 and not sp.b_block:
+                    check(lib.pb_stream_wait(ctx, d, d - 1), "pb_stream_wait")
+            for d in range(1, n):
+                lo, hi = parts[d]
+                gemm(d, hi - lo, *placed[d])
+            gemm(0, parts[0][1] - parts[0][0], A, B, O)
+            # The primary pulls the blocks of C into the result.
+            for d, (lo, hi) in enumerate(parts[1:], start=1):
+                check(lib.pb_stream_wait(ctx, 0, d), "pb_stream_wait")
+                copy(0, O + lo * sp.c_block * itemsize, d, placed[d][2], (hi - lo) * sp.c_block * itemsize, 0)
             self.splits += 1
         finally:
-            # The primary's stream ends after every block (its copies write
-            # the result); each device's temporaries are freed on its stream
-            # after the next device in the chain has read its copy of B.
-            for d in range(1, len(parts)):
+            # Whatever happened, the primary's stream ends after every
+            # device's work (so the workspaces are free for the next call).
+            for d in range(1, n):
                 lib.pb_stream_wait(ctx, 0, d)
-            for d in range(1, len(parts) - 1):
-                lib.pb_stream_wait(ctx, d, d + 1)
-            for d, p in temps:
-                lib.pb_free(ctx, d, C.c_void_p(p))

@@ -77,7 +77,7 @@ def test_split_decision_on_baseline_shapes():
 
 
 class FakeLib:
-    """Records the pool's library calls; pointers are (device, serial)."""
+    """Records the pool's library calls; pointers are distinct integers."""
 
     def __init__(self):
         self.calls = []
@@ -87,14 +87,18 @@ class FakeLib:
         flag._obj.value = 1
         return 0
 
-    def pb_alloc(self, ctx, dev, nbytes, ptr):
+    def pb_alloc_mapped(self, ctx, dev, nbytes, ptr):
         self.next += 1 << 32
         ptr._obj.value = self.next
         self.calls.append(("alloc", dev, nbytes, self.next))
         return 0
 
-    def pb_free(self, ctx, dev, ptr):
+    def pb_free_mapped(self, ctx, dev, ptr):
         self.calls.append(("free", dev, ptr.value))
+        return 0
+
+    def pb_sync(self, ctx, dev):
+        self.calls.append(("sync", dev))
         return 0
 
     def pb_stream_wait(self, ctx, waiter, signal):
@@ -111,6 +115,13 @@ class FakeBackend:
         self._lib, self._ctx = FakeLib(), C.c_void_p(1)
 
 
+def _run(dp, be, sp, A, B, O, isz):
+    def gemm(dev, outer, pa, pb, pc):
+        be._lib.calls.append(("gemm", dev, outer, pa, pb, pc))
+
+    dp.matmul(_lib.PB_F32, isz, sp, A, B, O, gemm)
+
+
 @pytest.mark.parametrize("ndev", [2, 3, 8])
 def test_split_product_queues_copies_waits_and_launches_in_order(ndev, monkeypatch):
     monkeypatch.setattr(pool, "CHUNK_BYTES", 1 << 20)
@@ -120,50 +131,65 @@ def test_split_product_queues_copies_waits_and_launches_in_order(ndev, monkeypat
     M, N, K, isz = 1000, 96, 640, 4
     sp = pool.plan((M, K), (K, N), (), M, N, K)
     A, B, O = 1 << 20, 2 << 30, 3 << 30
-    launches = []
-    dp.matmul(_lib.PB_F32, isz, sp, A, B, O,
-              lambda dev, outer, pa, pb, pc: launches.append((dev, outer, pa, pb, pc)))
+    _run(dp, be, sp, A, B, O, isz)
     calls = be._lib.calls
     parts = pool.blocks(M, ndev, pool.ROW_ALIGN)
     used = len(parts)
-    # Every other device first waits for the primary's stream.
-    assert calls[: used - 1] == [("wait", d, 0) for d in range(1, used)]
     allocs = [c for c in calls if c[0] == "alloc"]
-    assert len(allocs) == 3 * (used - 1)
-    # Launches: one per block, rows as planned, the primary in place.
-    assert [(d, outer) for d, outer, *_ in launches] == [(d, hi - lo) for d, (lo, hi) in enumerate(parts)]
-    assert launches[0][2:] == (A, B, O)
-    copies = [c for c in calls if c[0] == "copy"]
-    # A blocks from the primary, on the receiver's stream.
+    ws = {(c[1], role): c[3] for c, role in zip(allocs, ["a", "b", "c"] * used)}
+    assert len(allocs) == 3 * (used - 1) and all(c[1] >= 1 for c in allocs)
+    work = [c for c in calls if c[0] != "alloc"]
+    # Every other device first waits for the primary's stream.
+    assert work[: used - 1] == [("wait", d, 0) for d in range(1, used)]
+    copies = [c for c in work if c[0] == "copy"]
+    # The primary pushes the A blocks into the mapped workspaces.
     for d, (lo, hi) in enumerate(parts[1:], start=1):
-        assert ("copy", d, allocs[3 * (d - 1)][3], 0, A + lo * K * isz, (hi - lo) * K * isz, d) in copies
-    # B as a chain in chunks: device d reads device d-1's copy.
+        assert ("copy", d, ws[(d, "a")], 0, A + lo * K * isz, (hi - lo) * K * isz, 0) in copies
+    # B down the chain in chunks, each pushed by the device before.
     total = K * N * isz
     chunks = -(-total // pool.CHUNK_BYTES)
-    chain = [c for c in copies if c[5] <= pool.CHUNK_BYTES and c[3] != c[1] and c[1] != 0 and
-             c[4] != A + parts[c[1]][0] * K * isz]
+    chain = [c for c in copies if c[1] != 0 and c[3] == c[1] - 1 and
+             (c[3] == 0 and B <= c[4] < B + total or c[3] > 0 and ws[(c[3], "b")] <= c[4] < ws[(c[3], "b")] + total)]
     assert len(chain) == chunks * (used - 1)
-    for c in chain:
-        d = c[1]
-        src_base = B if d == 1 else allocs[3 * (d - 2) + 1][3]
-        assert c[3] == d - 1 and src_base <= c[4] < src_base + total and c[6] == d
-    # C blocks back into the result, on the sender's stream, after its launch.
+    assert all(c[6] == c[3] and ws[(c[1], "b")] <= c[2] < ws[(c[1], "b")] + total for c in chain)
+    # Blocks: the other devices first, the primary last, each with its rows.
+    launches = [c for c in work if c[0] == "gemm"]
+    assert [(c[1], c[2]) for c in launches] == [(d, hi - lo) for d, (lo, hi) in enumerate(parts)][1:] + [
+        (0, parts[0][1] - parts[0][0])]
+    assert launches[-1][3:] == (A, B, O)
+    # No stream waits for a device whose block is already queued, except the
+    # primary's final joins before it pulls each C block.
+    first_gemm = work.index(launches[0])
+    assert all(c[0] != "wait" for c in work[first_gemm:] if not (c[0] == "wait" and c[1] == 0))
+    # The primary pulls each C block after joining that device.
     for d, (lo, hi) in enumerate(parts[1:], start=1):
-        gather = ("copy", 0, O + lo * N * isz, d, allocs[3 * (d - 1) + 2][3], (hi - lo) * N * isz, d)
-        assert gather in copies
-    # The primary waits for every device at the end, each device for the next
-    # one in the chain (which read its B), then the temporaries go.
-    last = max(i for i, c in enumerate(calls) if c[0] in ("copy", "alloc"))
-    tail = [c for c in calls[last + 1:] if c[0] == "wait"]
-    assert tail == [("wait", 0, d) for d in range(1, used)] + [("wait", d, d + 1) for d in range(1, used - 1)]
-    assert all(c[0] in ("wait", "free") for c in calls[last + 1:])
-    frees = [c for c in calls if c[0] == "free"]
-    assert sorted(f[2] for f in frees) == sorted(a[3] for a in allocs)
-    assert all(f[1] == a[1] for f in frees for a in allocs if a[3] == f[2])
+        pull = ("copy", 0, O + lo * N * isz, d, ws[(d, "c")], (hi - lo) * N * isz, 0)
+        i = work.index(pull)
+        assert ("wait", 0, d) in work[first_gemm:i]
     assert dp.splits == 1
+    # A second product of the same shape reuses the workspaces.
+    n_alloc = len(allocs)
+    _run(dp, be, sp, A, B, O, isz)
+    assert len([c for c in be._lib.calls if c[0] == "alloc"]) == n_alloc
+    assert not [c for c in be._lib.calls if c[0] == "free"]
+    dp.close()
+    assert sorted(c[2] for c in be._lib.calls if c[0] == "free") == sorted(c[3] for c in allocs)
 
 
-def test_split_frees_temporaries_when_a_launch_fails():
+def test_growing_a_workspace_waits_for_every_device_first():
+    be = FakeBackend()
+    dp = pool.DevicePool(be, 2)
+    small = pool.plan((256, 64), (64, 64), (), 256, 64, 64)
+    big = pool.plan((4096, 64), (64, 64), (), 4096, 64, 64)
+    _run(dp, be, small, 1 << 20, 2 << 20, 3 << 20, 4)
+    be._lib.calls.clear()
+    _run(dp, be, big, 1 << 20, 2 << 20, 3 << 20, 4)
+    calls = be._lib.calls
+    first_free = next(i for i, c in enumerate(calls) if c[0] == "free")
+    assert {("sync", 0), ("sync", 1)} <= set(calls[:first_free])
+
+
+def test_split_ends_the_primary_after_every_device_when_a_launch_fails():
     be = FakeBackend()
     dp = pool.DevicePool(be, 4)
     sp = pool.plan((1024, 64), (64, 64), (), 1024, 64, 64)
@@ -174,10 +200,6 @@ def test_split_frees_temporaries_when_a_launch_fails():
 
     with pytest.raises(RuntimeError):
         dp.matmul(_lib.PB_F32, 4, sp, 1 << 20, 2 << 20, 3 << 20, gemm)
-    allocs = [c[3] for c in be._lib.calls if c[0] == "alloc"]
-    frees = [c[2] for c in be._lib.calls if c[0] == "free"]
-    assert sorted(allocs) == sorted(frees) and allocs
-    # Even on failure the primary's stream ends after every device's work.
     waits = [c for c in be._lib.calls if c[0] == "wait"]
     assert all(("wait", 0, d) in waits for d in range(1, 4))
     assert dp.splits == 0
