@@ -516,21 +516,17 @@ class Batched(Workload):
         self.pinned = [self.hA, self.hB, self.hC]
         self.gpu.pin(self.pinned)
 
+    e2e_how = ("; one pb_gemm_host call per step: host A and B in, host C out, uploads, "
+               "products and downloads overlapped over the 8 outer batches")
+
     def e2e_step(self):
         g = self.gpu
-        g.h2d(self.dA, self.hA)
-        if self.comm.active:
-            if self.rank == 0:
-                g.h2d(self.dB, self.hB)
-            self.comm.broadcast(self.dB, self.hB.nbytes)
-        else:
-            g.h2d(self.dB, self.hB)
-        self.step()
-        g.d2h_async(self.hC, self.dC)
+        g.check(g.raw.pb_gemm_host(g.ctx, 0, *self.args_gemm, C.c_void_p(self.hA.ctypes.data),
+                                   C.c_void_p(self.hB.ctypes.data), C.c_void_p(self.hC.ctypes.data), 0),
+                "gemm_host")
 
     def e2e_bytes(self):
-        h2d = self.hA.nbytes + (self.hB.nbytes if self.rank == 0 else 0)
-        return h2d, self.hC.nbytes
+        return self.hA.nbytes + self.hB.nbytes, self.hC.nbytes
 
     def violations(self):
         C_ = np.empty((self.per, 16, 512, 384), np.float32)
@@ -620,17 +616,27 @@ class Gemm(Workload):
         self.pinned = [self.Aloc, self.B, self.hC]
         self.gpu.pin(self.pinned)
 
+    @property
+    def e2e_how(self):
+        if self.sharded and self.comm.active:
+            return ", B broadcast by NCCL from rank 0"
+        return ("; one pb_gemm_host call per step: host A and B in, host C out, uploads, products "
+                "and downloads overlapped over row blocks of A")
+
     def e2e_step(self):
         g = self.gpu
-        g.h2d(self.dA, self.Aloc)
         if self.sharded and self.comm.active:
+            g.h2d(self.dA, self.Aloc)
             if self.rank == 0:
                 g.h2d(self.dB, self.B)
             self.comm.broadcast(self.dB, self.B.nbytes)
-        else:
-            g.h2d(self.dB, self.B)
-        self.step()
-        g.d2h_async(self.hC, self.dC)
+            self.step()
+            g.d2h_async(self.hC, self.dC)
+            return
+        n = self.n
+        g.check(g.raw.pb_gemm_host(g.ctx, 0, self.code, 0, self.ns, self.ns, self.ns, self.rows, n, n,
+                                   C.c_void_p(self.Aloc.ctypes.data), C.c_void_p(self.B.ctypes.data),
+                                   C.c_void_p(self.hC.ctypes.data), 0), "gemm_host")
 
     def e2e_bytes(self):
         own_b = (not (self.sharded and self.comm.active)) or self.rank == 0
@@ -1121,8 +1127,7 @@ def measure(w: Workload, gpu: Gpu, comm: Comm, args, dist: Dist, pk: dict) -> di
                   "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                   "ms_per_step": e2e_seconds / e2e_steps * 1e3,
                   "note": "whole job: every rank's pinned host inputs copied in and results read "
-                          "back each step" + (", B broadcast by NCCL from rank 0" if getattr(w, "comm", None)
-                                              and getattr(w.comm, "active", False) and hasattr(w, "dB") else "")}
+                          "back each step" + getattr(w, "e2e_how", "")}
     rec["parity_violations"] = bad
     if w.extra:
         rec.update(w.extra)

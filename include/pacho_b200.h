@@ -222,6 +222,22 @@ int pb_gemm_ex(pb_ctx* ctx, int dev, int dtype, int batch_ndim, const int64_t* b
                const int64_t* a_bstride, const int64_t* b_bstride, int64_t M, int64_t N,
                int64_t K, const void* A, const void* B, void* C, int algo);
 
+/* pb_gemm with A, B and C in HOST memory: returns when C holds the product.
+ * The reference's CUDA backend uploads, multiplies and downloads one step
+ * after another (CUDABackend.upload / matmul / download,
+ * src/openpacho/_cuda.py:241-281, 493-517).  Here the product is cut into
+ * `chunks` pieces (0 = up to 8; at least 4 MiB of traffic each) along the
+ * leading batch dimension when A is dense along it (B broadcast along it or
+ * dense too), else along the rows of A when there is no batch, else one
+ * piece; each piece's A goes up on a host-to-device stream while the previous
+ * piece multiplies and the one before comes down on a device-to-host stream,
+ * so both directions of the host link and the GEMM overlap.  Host buffers
+ * registered with pb_host_register (pinned) let the copies run
+ * asynchronously; pageable ones work, with the driver's staged copies. */
+int pb_gemm_host(pb_ctx* ctx, int dev, int dtype, int batch_ndim, const int64_t* batch_shape,
+                 const int64_t* a_bstride, const int64_t* b_bstride, int64_t M, int64_t N,
+                 int64_t K, const void* A, const void* B, void* C, int chunks);
+
 /* y[r] = sum_k A[r,k] * x[k] for r < rows (leading dims flattened into rows).
  * Replaces matvec_data (src/openpacho/_cuda_gemv.py:47-95) and the cuBLAS
  * ?gemv loop (src/openpacho/_cuda_blas.py:32-61). */

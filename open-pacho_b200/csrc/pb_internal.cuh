@@ -67,6 +67,10 @@ enum : int {
 struct Device {
   int ordinal = -1;
   cudaStream_t stream = nullptr;
+  // Copy streams of pb_gemm_host (host -> device, device -> host) and the
+  // events that order its chunks; created on first use.
+  cudaStream_t up = nullptr, down = nullptr;
+  std::vector<cudaEvent_t> host_events;
   cudaMemPool_t pool = nullptr;
   int sm_count = 0;
   // Scratch memory for multi-block reductions and GEMM operand splits.  Grown
@@ -127,8 +131,16 @@ struct pb_ctx {
 
 namespace pb {
 
+// pb_gemm / pb_gemm_ex with an explicit kernel choice (pb_gemm.cu).
+int gemm_dispatch(pb_ctx* ctx, int dev, int dtype, int batch_ndim, const int64_t* batch_shape,
+                  const int64_t* a_bstride, const int64_t* b_bstride, int64_t M, int64_t N,
+                  int64_t K, const void* A, const void* B, void* C, int algo);
+
 // Validates (ctx, dev), makes the device current and returns its state.
 int enter(pb_ctx* ctx, int dev, Device** out);
+// Reads and clears the device's kernel error word (after a synchronisation):
+// PB_ERR_DEVICE with the kernel's reason if a kernel raised it.
+int check_kernel_error(Device* d);
 // Ensure at least `bytes` of scratch; returns the pointer.
 int scratch(Device* d, size_t bytes, void** out);
 // Ensure at least `n` zeroed counters; returns the pointer.

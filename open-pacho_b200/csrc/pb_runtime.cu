@@ -171,6 +171,11 @@ static void release_device(Device* d) {
   d->kt_used = 0;
   d->dot_static = nullptr;
   if (d->err_host) cudaFreeHost(d->err_host);
+  for (cudaEvent_t e : d->host_events) cudaEventDestroy(e);
+  d->host_events.clear();
+  if (d->up) cudaStreamSynchronize(d->up), cudaStreamDestroy(d->up);
+  if (d->down) cudaStreamSynchronize(d->down), cudaStreamDestroy(d->down);
+  d->up = d->down = nullptr;
   if (d->stream) cudaStreamDestroy(d->stream);
   if (d->pool) cudaMemPoolTrimTo(d->pool, 0);
   d->scratch = nullptr;
@@ -182,7 +187,7 @@ static void release_device(Device* d) {
 }
 
 // Kernel error word check (after a synchronisation).
-static int check_kernel_error(Device* d) {
+int check_kernel_error(Device* d) {
   if (d->err_host && *(volatile int*)d->err_host != KERR_NONE) {
     int code = *(volatile int*)d->err_host;
     *(volatile int*)d->err_host = KERR_NONE;

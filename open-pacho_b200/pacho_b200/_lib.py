@@ -95,6 +95,7 @@ PROTOTYPES = {
     "pb_graph_destroy": [_ctx, _i, C.c_void_p],
     "pb_gemm": [_ctx, _i, _i, _i, _pi64, _pi64, _pi64, _i64, _i64, _i64, _p, _p, _p],
     "pb_gemm_ex": [_ctx, _i, _i, _i, _pi64, _pi64, _pi64, _i64, _i64, _i64, _p, _p, _p, _i],
+    "pb_gemm_host": [_ctx, _i, _i, _i, _pi64, _pi64, _pi64, _i64, _i64, _i64, _p, _p, _p, _i],
     "pb_gemv": [_ctx, _i, _i, _i64, _i64, _p, _p, _p],
     "pb_gemv_residual": [_ctx, _i, _i, _i64, _i64, _p, _p, _p, _p],
     "pb_elementwise": [_ctx, _i, _i, _i, C.POINTER(_p), C.POINTER(_i), _pi64, _i, _pi64, _i, _p],

@@ -350,6 +350,41 @@ class B200Backend:
                 )
         return out
 
+    def matmul_host(self, a, b, *, chunks=0):
+        """``a @ b`` for host (NumPy) arrays of at least two dimensions, with
+        NumPy's broadcasting of leading dimensions: one ``pb_gemm_host`` call,
+        whose upload, product and download overlap piece by piece.  Returns a
+        new host array.  Pinned operands (``pb_host_register``) copy
+        asynchronously; others through the driver's staging."""
+        a = np.ascontiguousarray(a)
+        b = np.ascontiguousarray(b)
+        if a.ndim < 2 or b.ndim < 2:
+            raise ValueError("matmul_host takes operands of at least two dimensions")
+        if a.dtype != b.dtype:
+            raise NotImplementedError("matmul_host needs operands of one dtype")
+        dtype = self.validate_dtype(a.dtype)
+        if dtype.kind != "f":
+            raise NotImplementedError("b200 matmul requires float32 or float64")
+        m, k = a.shape[-2:]
+        k2, n = b.shape[-2:]
+        if k != k2:
+            raise ValueError(f"matmul: inner dimensions differ ({k} and {k2})")
+        a_batch, b_batch = a.shape[:-2], b.shape[:-2]
+        batch = tuple(np.broadcast_shapes(a_batch, b_batch))
+        out = np.empty(batch + (m, n), dtype)
+        if not out.size:
+            return out
+        with self._lock:
+            self._require_open()
+            self._check(
+                self._lib.pb_gemm_host(self._ctx, 0, _lib.dtype_code(dtype), len(batch), _lib.i64_array(batch),
+                                       _lib.i64_array(_matrix_strides(batch, a_batch)),
+                                       _lib.i64_array(_matrix_strides(batch, b_batch)), m, n, k,
+                                       C.c_void_p(a.ctypes.data), C.c_void_p(b.ctypes.data),
+                                       C.c_void_p(out.ctypes.data), int(chunks)),
+                "pb_gemm_host")
+        return out
+
     def _split_matmul(self, code, dtype, a, b, batch, m, n, k, A, B, O) -> bool:
         """The product over every GPU of the context, when it pays."""
         sp = pool.plan(a.shape, b.shape, batch, m, n, k)
