@@ -138,20 +138,22 @@ int pb_ktimer_read(pb_ctx* ctx, int dev, double* total_ms, uint64_t* launches);
  * pool memory of pb_alloc: a peer copy runs device to device over NVLink when
  * the side of it that is remote to the issuing device comes from
  * pb_alloc_mapped (else the driver stages it).  pb_free_mapped waits for the
- * device's stream before it frees.  pb_copy_peer queues a copy of `bytes` from
- * `src` on device index `src_dev` to `dst` on `dst_dev` (over NVLink when peer
- * access is on) on the stream of `stream_dev`, which must be one of the two;
- * it orders nothing else.  pb_stream_wait makes `waiter`'s stream wait for the
- * work queued so far on `signal`'s: the caller orders a copy after the
- * producer of its source and the allocation of its destination, and the
- * consumer (or a free) after the copy.  No counterpart in the reference, which
- * drives one device (src/openpacho/_cuda.py:138-199). */
+ * device's stream before it frees.  Each device has two streams: 0, where
+ * every kernel of the library runs, and 1, a copy stream.  pb_copy_peer queues
+ * a copy of `bytes` from `src` on device index `src_dev` to `dst` on `dst_dev`
+ * on stream `stream` of `stream_dev` (one of the two devices) and orders
+ * nothing else; pb_stream_wait makes stream `waiter_stream` of `waiter` wait
+ * for the work queued so far on stream `signal_stream` of `signal`.  The
+ * caller orders each copy after the producer of its source and the
+ * allocation of its destination, and the consumer (or a free) after the
+ * copy.  No counterpart in the reference, which drives one device
+ * (src/openpacho/_cuda.py:138-199). */
 int pb_peer_enable(pb_ctx* ctx, int* all_pairs);
 int pb_alloc_mapped(pb_ctx* ctx, int dev, size_t bytes, void** ptr);
 int pb_free_mapped(pb_ctx* ctx, int dev, void* ptr);
 int pb_copy_peer(pb_ctx* ctx, int dst_dev, void* dst, int src_dev, const void* src, size_t bytes,
-                 int stream_dev);
-int pb_stream_wait(pb_ctx* ctx, int waiter, int signal);
+                 int stream_dev, int stream);
+int pb_stream_wait(pb_ctx* ctx, int waiter, int waiter_stream, int signal, int signal_stream);
 
 /* CUDA graphs of hot-path calls.  pb_capture_begin starts a (relaxed) capture
  * of the device stream; the entry points called until pb_capture_end are

@@ -538,42 +538,61 @@ int pb_free_mapped(pb_ctx* ctx, int dev, void* ptr) {
   return PB_OK;
 }
 
-// `waiter`'s stream waits for everything queued so far on `signal`'s stream.
-static int join_streams(Device* waiter, Device* signal) {
-  if (waiter == signal) return PB_OK;
-  PB_CUDA(cudaSetDevice(signal->ordinal));
-  PB_CUDA(cudaEventRecord(signal->order_ev, signal->stream));
-  PB_CUDA(cudaSetDevice(waiter->ordinal));
-  PB_CUDA(cudaStreamWaitEvent(waiter->stream, signal->order_ev, 0));
+// Stream `which` of a device: 0 its stream (every kernel of the library runs
+// there), 1 its copy stream (created on first use).
+static int device_stream(Device* d, int which, cudaStream_t* out) {
+  if (which == 0) {
+    *out = d->stream;
+    return PB_OK;
+  }
+  if (which != 1) PB_FAIL(PB_ERR_INVALID, "stream %d: 0 (the device's) or 1 (its copy stream)", which);
+  if (!d->up) {
+    PB_CUDA(cudaSetDevice(d->ordinal));
+    PB_CUDA(cudaStreamCreateWithFlags(&d->up, cudaStreamNonBlocking));
+  }
+  *out = d->up;
   return PB_OK;
 }
 
-int pb_stream_wait(pb_ctx* ctx, int waiter, int signal) {
+int pb_stream_wait(pb_ctx* ctx, int waiter, int waiter_stream, int signal, int signal_stream) {
   if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
   std::lock_guard<std::recursive_mutex> g(ctx->mu);
   Device *w, *s;
   PB_CHECK(enter(ctx, signal, &s));
   PB_CHECK(enter(ctx, waiter, &w));
-  return join_streams(w, s);
+  if (w->capturing || s->capturing)
+    PB_FAIL(PB_ERR_UNSUPPORTED, "pb_stream_wait cannot run during stream capture");
+  cudaStream_t ws, ss;
+  PB_CHECK(device_stream(w, waiter_stream, &ws));
+  PB_CHECK(device_stream(s, signal_stream, &ss));
+  if (ws == ss) return PB_OK;
+  PB_CUDA(cudaSetDevice(s->ordinal));
+  PB_CUDA(cudaEventRecord(s->order_ev, ss));
+  PB_CUDA(cudaSetDevice(w->ordinal));
+  PB_CUDA(cudaStreamWaitEvent(ws, s->order_ev, 0));
+  return PB_OK;
 }
 
 int pb_copy_peer(pb_ctx* ctx, int dst_dev, void* dst, int src_dev, const void* src, size_t bytes,
-                 int stream_dev) {
+                 int stream_dev, int stream) {
   if (!ctx) PB_FAIL(PB_ERR_INVALID, "null context");
   if (!bytes) return PB_OK;
   if (!dst || !src) PB_FAIL(PB_ERR_INVALID, "null pointer in pb_copy_peer");
   if (stream_dev != dst_dev && stream_dev != src_dev)
-    PB_FAIL(PB_ERR_INVALID, "pb_copy_peer runs on the source's or the destination's stream");
+    PB_FAIL(PB_ERR_INVALID, "pb_copy_peer runs on a stream of the source or the destination");
   std::lock_guard<std::recursive_mutex> g(ctx->mu);
   Device *t, *s, *on;
   PB_CHECK(enter(ctx, src_dev, &s));
   PB_CHECK(enter(ctx, dst_dev, &t));
   PB_CHECK(enter(ctx, stream_dev, &on));
   if (on->capturing) PB_FAIL(PB_ERR_UNSUPPORTED, "pb_copy_peer cannot run during stream capture");
+  cudaStream_t st;
+  PB_CHECK(device_stream(on, stream, &st));
+  PB_CUDA(cudaSetDevice(on->ordinal));
   if (t == s)
-    PB_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, on->stream));
+    PB_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, st));
   else
-    PB_CUDA(cudaMemcpyPeerAsync(dst, t->ordinal, src, s->ordinal, bytes, on->stream));
+    PB_CUDA(cudaMemcpyPeerAsync(dst, t->ordinal, src, s->ordinal, bytes, st));
   return PB_OK;
 }
 

@@ -87,8 +87,8 @@ PROTOTYPES = {
     "pb_peer_enable": [_ctx, C.POINTER(C.c_int)],
     "pb_alloc_mapped": [_ctx, _i, _sz, C.POINTER(C.c_void_p)],
     "pb_free_mapped": [_ctx, _i, C.c_void_p],
-    "pb_copy_peer": [_ctx, _i, C.c_void_p, _i, C.c_void_p, _sz, _i],
-    "pb_stream_wait": [_ctx, _i, _i],
+    "pb_copy_peer": [_ctx, _i, C.c_void_p, _i, C.c_void_p, _sz, _i, _i],
+    "pb_stream_wait": [_ctx, _i, _i, _i, _i],
     "pb_capture_begin": [_ctx, _i],
     "pb_capture_end": [_ctx, _i, C.POINTER(C.c_void_p)],
     "pb_graph_launch": [_ctx, _i, C.c_void_p],

@@ -188,7 +188,13 @@ class DevicePool:
     def matmul(self, code, itemsize, sp: Split, A: int, B: int, O: int, gemm) -> None:
         """C = A @ B by blocks of `sp.outer`; `gemm(dev, outer, A, B, C)`
         launches one block's product on device index `dev`.  Called with the
-        backend's lock held; the primary's stream ends after every block."""
+        backend's lock held; the primary's stream ends after every block.
+
+        Each device has its kernel stream (0) and a copy stream (1).  The
+        primary pushes and pulls on its copy stream, so its own block starts
+        at once and each other block's result is pulled as soon as it is
+        done; the chain hops of B run on the copy streams of the devices
+        that forward them."""
         lib, ctx = self.lib, self.ctx
         check = _lib.check
         align = ROW_ALIGN if not sp.batch else 1
@@ -202,15 +208,21 @@ class DevicePool:
             c = self._workspace(d, "c", rows * sp.c_block * itemsize)
             placed.append((a, b, c))
 
+        def wait(w, ws, g, gs):
+            check(lib.pb_stream_wait(ctx, w, ws, g, gs), "pb_stream_wait")
+
         def copy(dst_dev, dst, src_dev, src, nbytes, on):
-            check(lib.pb_copy_peer(ctx, dst_dev, C.c_void_p(dst), src_dev, C.c_void_p(src), nbytes, on),
+            check(lib.pb_copy_peer(ctx, dst_dev, C.c_void_p(dst), src_dev, C.c_void_p(src), nbytes, on, 1),
                   "pb_copy_peer")
 
         try:
-            # Every device's stream first waits for the primary's (whose last
-            # call ended after every device's work): the workspaces are free.
+            # Every stream starts after the primary's kernel stream, whose
+            # last call ended after every device's work: inputs are ready
+            # and the workspaces free.
+            wait(0, 1, 0, 0)
             for d in range(1, n):
-                check(lib.pb_stream_wait(ctx, d, 0), "pb_stream_wait")
+                wait(d, 0, 0, 0)
+                wait(d, 1, 0, 0)
             # The primary pushes the blocks of A (and of a batched B).
             for d, (lo, hi) in enumerate(parts[1:], start=1):
                 rows = hi - lo
@@ -219,32 +231,34 @@ class DevicePool:
                     copy(d, placed[d][1], 0, B + lo * sp.b_block * itemsize, rows * sp.b_block * itemsize, 0)
             if not sp.b_block and n > 1:
                 # The whole B down the chain, chunk by chunk: device d - 1
-                # pushes a chunk on once its own copy of it has landed.
+                # forwards a chunk once its own copy of it has landed.
                 total = sp.b_whole * itemsize
                 for off in range(0, total, CHUNK_BYTES):
                     size = min(CHUNK_BYTES, total - off)
                     for d in range(1, n):
                         if d > 1:
-                            check(lib.pb_stream_wait(ctx, d - 1, d - 2), "pb_stream_wait")
+                            wait(d - 1, 1, d - 2, 1)
                         copy(d, placed[d][1] + off, d - 1, placed[d - 1][1] + off, size, d - 1)
-            # Each device after the pushes into it (all joins before any
-            # block is queued, so no device waits for another's block), then
-            # the blocks.
+            # Each device's block after the pushes into it (all joins queued
+            # before any block, so no device waits for another's product).
             for d in range(1, n):
-                check(lib.pb_stream_wait(ctx, d, 0), "pb_stream_wait")
+                wait(d, 0, 0, 1)
                 if d > 1 and not sp.b_block:
-                    check(lib.pb_stream_wait(ctx, d, d - 1), "pb_stream_wait")
+                    wait(d, 0, d - 1, 1)
             for d in range(1, n):
                 lo, hi = parts[d]
                 gemm(d, hi - lo, *placed[d])
             gemm(0, parts[0][1] - parts[0][0], A, B, O)
-            # The primary pulls the blocks of C into the result.
+            # The primary pulls each block of C as it is done.
             for d, (lo, hi) in enumerate(parts[1:], start=1):
-                check(lib.pb_stream_wait(ctx, 0, d), "pb_stream_wait")
+                wait(0, 1, d, 0)
                 copy(0, O + lo * sp.c_block * itemsize, d, placed[d][2], (hi - lo) * sp.c_block * itemsize, 0)
             self.splits += 1
         finally:
-            # Whatever happened, the primary's stream ends after every
-            # device's work (so the workspaces are free for the next call).
+            # Whatever happened, the primary's kernel stream ends after its
+            # copy stream and every device's work (so the result is complete
+            # there and the workspaces are free for the next call).
+            lib.pb_stream_wait(ctx, 0, 0, 0, 1)
             for d in range(1, n):
-                lib.pb_stream_wait(ctx, 0, d)
+                lib.pb_stream_wait(ctx, 0, 0, d, 0)
+                lib.pb_stream_wait(ctx, 0, 0, d, 1)

@@ -101,12 +101,12 @@ class FakeLib:
         self.calls.append(("sync", dev))
         return 0
 
-    def pb_stream_wait(self, ctx, waiter, signal):
-        self.calls.append(("wait", waiter, signal))
+    def pb_stream_wait(self, ctx, waiter, waiter_stream, signal, signal_stream):
+        self.calls.append(("wait", waiter, waiter_stream, signal, signal_stream))
         return 0
 
-    def pb_copy_peer(self, ctx, dst_dev, dst, src_dev, src, nbytes, on):
-        self.calls.append(("copy", dst_dev, dst.value, src_dev, src.value, nbytes, on))
+    def pb_copy_peer(self, ctx, dst_dev, dst, src_dev, src, nbytes, on, stream):
+        self.calls.append(("copy", dst_dev, dst.value, src_dev, src.value, nbytes, on, stream))
         return 0
 
 
@@ -139,33 +139,48 @@ def test_split_product_queues_copies_waits_and_launches_in_order(ndev, monkeypat
     ws = {(c[1], role): c[3] for c, role in zip(allocs, ["a", "b", "c"] * used)}
     assert len(allocs) == 3 * (used - 1) and all(c[1] >= 1 for c in allocs)
     work = [c for c in calls if c[0] != "alloc"]
-    # Every other device first waits for the primary's stream.
-    assert work[: used - 1] == [("wait", d, 0) for d in range(1, used)]
+    # Every stream first waits for the primary's kernel stream.
+    head = [("wait", 0, 1, 0, 0)] + [w for d in range(1, used) for w in (("wait", d, 0, 0, 0), ("wait", d, 1, 0, 0))]
+    assert work[: len(head)] == head
     copies = [c for c in work if c[0] == "copy"]
+    assert all(c[7] == 1 for c in copies)  # every copy on a copy stream
     # The primary pushes the A blocks into the mapped workspaces.
     for d, (lo, hi) in enumerate(parts[1:], start=1):
-        assert ("copy", d, ws[(d, "a")], 0, A + lo * K * isz, (hi - lo) * K * isz, 0) in copies
-    # B down the chain in chunks, each pushed by the device before.
+        assert ("copy", d, ws[(d, "a")], 0, A + lo * K * isz, (hi - lo) * K * isz, 0, 1) in copies
+    # B down the chain in chunks, each forwarded by the device before.
     total = K * N * isz
     chunks = -(-total // pool.CHUNK_BYTES)
     chain = [c for c in copies if c[1] != 0 and c[3] == c[1] - 1 and
              (c[3] == 0 and B <= c[4] < B + total or c[3] > 0 and ws[(c[3], "b")] <= c[4] < ws[(c[3], "b")] + total)]
     assert len(chain) == chunks * (used - 1)
     assert all(c[6] == c[3] and ws[(c[1], "b")] <= c[2] < ws[(c[1], "b")] + total for c in chain)
-    # Blocks: the other devices first, the primary last, each with its rows.
+    # A hop from d - 1 comes after d - 1's copy stream joined d - 2's.
+    for c in chain:
+        if c[3] >= 1:
+            i = work.index(c)
+            assert ("wait", c[3], 1, c[3] - 1, 1) in work[:i]
+    # Blocks: the other devices first, the primary last, each with its rows;
+    # each device's kernel stream joined its suppliers before any block.
     launches = [c for c in work if c[0] == "gemm"]
     assert [(c[1], c[2]) for c in launches] == [(d, hi - lo) for d, (lo, hi) in enumerate(parts)][1:] + [
         (0, parts[0][1] - parts[0][0])]
     assert launches[-1][3:] == (A, B, O)
-    # No stream waits for a device whose block is already queued, except the
-    # primary's final joins before it pulls each C block.
     first_gemm = work.index(launches[0])
-    assert all(c[0] != "wait" for c in work[first_gemm:] if not (c[0] == "wait" and c[1] == 0))
-    # The primary pulls each C block after joining that device.
+    for d in range(1, used):
+        assert ("wait", d, 0, 0, 1) in work[:first_gemm]
+        if d > 1:
+            assert ("wait", d, 0, d - 1, 1) in work[:first_gemm]
+    # After the first block only the primary's streams wait.
+    assert all(c[1] == 0 for c in work[first_gemm:] if c[0] == "wait")
+    # The primary pulls each C block on its copy stream after joining that
+    # device's kernel stream, and its kernel stream ends after everything.
     for d, (lo, hi) in enumerate(parts[1:], start=1):
-        pull = ("copy", 0, O + lo * N * isz, d, ws[(d, "c")], (hi - lo) * N * isz, 0)
+        pull = ("copy", 0, O + lo * N * isz, d, ws[(d, "c")], (hi - lo) * N * isz, 0, 1)
         i = work.index(pull)
-        assert ("wait", 0, d) in work[first_gemm:i]
+        assert ("wait", 0, 1, d, 0) in work[first_gemm:i]
+    tail = work[-(1 + 2 * (used - 1)):]
+    assert tail[0] == ("wait", 0, 0, 0, 1)
+    assert all(("wait", 0, 0, d, 0) in tail and ("wait", 0, 0, d, 1) in tail for d in range(1, used))
     assert dp.splits == 1
     # A second product of the same shape reuses the workspaces.
     n_alloc = len(allocs)
@@ -201,5 +216,6 @@ def test_split_ends_the_primary_after_every_device_when_a_launch_fails():
     with pytest.raises(RuntimeError):
         dp.matmul(_lib.PB_F32, 4, sp, 1 << 20, 2 << 20, 3 << 20, gemm)
     waits = [c for c in be._lib.calls if c[0] == "wait"]
-    assert all(("wait", 0, d) in waits for d in range(1, 4))
+    assert ("wait", 0, 0, 0, 1) in waits
+    assert all(("wait", 0, 0, d, 0) in waits and ("wait", 0, 0, d, 1) in waits for d in range(1, 4))
     assert dp.splits == 0
