@@ -127,7 +127,10 @@ def _gemm_shapes():
     rng = np.random.default_rng(11)
     for m, n, k in ((128, 128, 32), (129, 255, 33), (300, 520, 97), (1, 300, 64), (257, 1, 40),
                     (64, 64, 1), (200, 136, 1000), (1, 4099, 3000), (3, 1001, 20000),
-                    (8, 64, 5), (5, 2, 70000), (2181, 200, 96), (900, 1100, 500)):
+                    (8, 64, 5), (5, 2, 70000), (2181, 200, 96), (900, 1100, 500),
+                    # two-way K splits: 128- and 64-wide tiles as CTA pairs, and
+                    # (N % 4 != 0) through the partial planes and the reduction
+                    (1000, 1000, 800), (7680, 48, 384), (1000, 998, 800)):
         yield (f"rand{m}x{n}x{k}", rng.standard_normal((m, k)).astype(np.float32),
                rng.standard_normal((k, n)).astype(np.float32))
 
